@@ -1,0 +1,143 @@
+/*
+ * spark_b200.h -- C ABI of the SPARK online-dequant linear path for B200
+ * (sm_100a).  Plain pointers and sizes only; every buffer is owned by the
+ * caller and every call is ordered on the caller's CUDA stream (`stream` is a
+ * cudaStream_t passed as void*, NULL = legacy default stream).
+ *
+ * Return value: SPARK_OK (0), a negative SPARK_ERR_* for an invalid call
+ * (nothing was launched), or a positive cudaError_t from the launch.  The
+ * message of the last error on the calling thread is spark_last_error().
+ *
+ * Packed layouts are exactly the reference's on-disk formats (DJAzzs/SPARK):
+ *   SPFP2 paired  01_core/block_fp2_emu.py:231-267  5 B per 16 weights
+ *   SPFP2 v1      01_core/block_fp2_emu.py:86-167   3 B per 8 weights
+ *   FP3 3-bit     01_core/fp3_emu.py:107-139        3 B per 8 codes + e4m3 scale / 16
+ *   FP3 nibble    01_core/fp3_emu.py:50-73          1 B per 2 codes + e4m3 scale / 16
+ *   NVFP4         01_core/nvfp4_emu.py:81-107       1 B per 2 codes + e4m3 scale / 16
+ *   2:4 SPFP2     01_core/two_four.py:112-155       7 B per 32 weights
+ */
+#ifndef SPARK_B200_H
+#define SPARK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SPARK_API __attribute__((visibility("default")))
+#else
+#define SPARK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPARK_OK 0
+#define SPARK_ERR_INVALID (-1)     /* bad size, pointer or enum */
+#define SPARK_ERR_ALIGNMENT (-2)   /* pointer or stride not aligned as required */
+#define SPARK_ERR_UNSUPPORTED (-3) /* valid request this build does not implement */
+#define SPARK_ERR_WORKSPACE (-4)   /* workspace missing or too small */
+#define SPARK_ERR_DEVICE (-5)      /* a kernel reported an error through its workspace flag */
+
+/* element types of float tensors */
+#define SPARK_DTYPE_F32 0
+#define SPARK_DTYPE_BF16 1
+#define SPARK_DTYPE_F16 2
+
+/* packed weight formats accepted by the linear entry points */
+#define SPARK_FMT_SPFP2 0    /* paired, 5 B / 16 weights (the container's *_packed) */
+#define SPARK_FMT_SPFP2_V1 1 /* 3 B / 8 weights (_detect_format "v1") */
+#define SPARK_FMT_FP3 2      /* 3-bit codes + e4m3 scales (the container's *_fp3_codes/_fp3_scales) */
+#define SPARK_FMT_NVFP4 3    /* e2m1 nibbles + e4m3 scales (*_nvfp4_codes/_nvfp4_scales) */
+#define SPARK_FMT_TWOFOUR 4  /* 2:4-sparse SPFP2, 7 B / 32 weights ("v3-24") */
+
+SPARK_API const char* spark_last_error(void);
+SPARK_API int spark_version(void);
+
+/* ---------------------------------------------------------------- SPFP2 */
+/* pack_blockwise_paired(w) -- 01_core/block_fp2_emu.py:231.
+ * w: n floats (dtype), n % 8 == 0, blocks of 8 over the flattened tensor.
+ * packed: ceil(n/16)*5 bytes; expv: n/8 bytes (may be NULL). */
+SPARK_API int spark_spfp2_pack(const void* w, int w_dtype, int64_t n, uint8_t* packed, uint8_t* expv, void* stream);
+/* pack_blockwise_search(w, window=2) -- 01_core/block_fp2_emu.py:86.  packed: n/8*3 bytes. */
+SPARK_API int spark_spfp2_pack_v1(const void* w, int w_dtype, int64_t n, uint8_t* packed, uint8_t* expv, void* stream);
+/* unpack_blockwise_paired(packed, n_elements) -- 01_core/block_fp2_emu.py:270; replaces the
+ * decode_fp32/decode_fp16 torch ops (01_core/build_spark_fp2.py:28-54) and
+ * spark_decode_launch_f32/f16 (01_core/block_fp2_kernel.cu:67-87). */
+SPARK_API int spark_spfp2_unpack(const uint8_t* packed, int64_t n_elements, void* out, int out_dtype, void* stream);
+/* unpack_blockwise(packed) (3-byte) -- 01_core/block_fp2_emu.py:204. */
+SPARK_API int spark_spfp2_unpack_v1(const uint8_t* packed, int64_t n_blocks, void* out, int out_dtype, void* stream);
+/* channel_fake_quantize(w) forward -- 01_core/block_fp2_emu.py:365 (STE backward is the
+ * identity, :359-362). */
+SPARK_API int spark_spfp2_fake_quant(const void* w, int w_dtype, int64_t n, void* out, int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------- FP3 E1M1 */
+/* fp3_pack_3bit(w) -- 01_core/fp3_emu.py:107.  w: [oc, ic]; codes: ceil(oc*ceil(ic/16)*16/8)*3 B;
+ * scales: oc*ceil(ic/16) e4m3 bytes. */
+SPARK_API int spark_fp3_pack(const void* w, int w_dtype, int64_t oc, int64_t ic, uint8_t* codes, uint8_t* scales,
+                   void* stream);
+/* fp3_pack(w) (nibble codes) -- 01_core/fp3_emu.py:50.  codes: ceil(n/2) B. */
+SPARK_API int spark_fp3_pack_nibble(const void* w, int w_dtype, int64_t oc, int64_t ic, uint8_t* codes, uint8_t* scales,
+                          void* stream);
+/* fp3_unpack_3bit -- 01_core/fp3_emu.py:142. */
+SPARK_API int spark_fp3_unpack(const uint8_t* codes, const uint8_t* scales, int64_t oc, int64_t ic, void* out,
+                     int out_dtype, void* stream);
+/* fp3_unpack (nibble) -- 01_core/fp3_emu.py:76. */
+SPARK_API int spark_fp3_unpack_nibble(const uint8_t* codes, const uint8_t* scales, int64_t oc, int64_t ic, void* out,
+                            int out_dtype, void* stream);
+/* fp3_fake_quant -- 01_core/fp3_emu.py:24 (FP3STE backward is the identity, :96-98). */
+SPARK_API int spark_fp3_fake_quant(const void* w, int w_dtype, int64_t oc, int64_t ic, void* out, int out_dtype,
+                         void* stream);
+
+/* ---------------------------------------------------------------- NVFP4 */
+/* nvfp4_pack -- 01_core/nvfp4_emu.py:81. */
+SPARK_API int spark_nvfp4_pack(const void* w, int w_dtype, int64_t oc, int64_t ic, uint8_t* codes, uint8_t* scales,
+                     void* stream);
+/* nvfp4_unpack -- 01_core/nvfp4_emu.py:109. */
+SPARK_API int spark_nvfp4_unpack(const uint8_t* codes, const uint8_t* scales, int64_t oc, int64_t ic, void* out,
+                       int out_dtype, void* stream);
+/* nvfp4_fake_quant -- 01_core/nvfp4_emu.py:37 (NVFP4STE backward is the identity, :66-68). */
+SPARK_API int spark_nvfp4_fake_quant(const void* w, int w_dtype, int64_t oc, int64_t ic, void* out, int out_dtype,
+                           void* stream);
+
+/* ---------------------------------------------------------------- 2:4 SPFP2 */
+/* two_four_pack -- 01_core/two_four.py:112.  packed: ceil(oc*ceil(ic/16)/2)*7 bytes. */
+SPARK_API int spark_twofour_pack(const void* w, int w_dtype, int64_t oc, int64_t ic, uint8_t* packed, void* stream);
+/* two_four_unpack -- 01_core/two_four.py:158. */
+SPARK_API int spark_twofour_unpack(const uint8_t* packed, int64_t n_elements, void* out, int out_dtype, void* stream);
+/* two_four_fake_quant -- 01_core/two_four.py:70 (TwoFourSTE backward is the identity, :65-67). */
+SPARK_API int spark_twofour_fake_quant(const void* w, int w_dtype, int64_t n, void* out, int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------- linear */
+/* y[M, oc] = x[M, ic] . decode(W)^T (+ bias), fp32 accumulation.
+ * Replaces spark_v3_spfp2_linear_forward / spark_v3_spfp2_forward
+ * (01_core/spark_v3_kernel.cu:172-214) and spark_v3_twofour_forward
+ * (01_core/spark_v3_twofour.cu:162-181), and the decode + F.linear of the layer
+ * classes (02_model/quant_linear.py:133-148, 197-212; 02_model/fp3_linear.py:46-56).
+ *   fmt      SPARK_FMT_*; wq/scales in that format for a row-major [oc, ic] weight
+ *            (scales NULL for SPFP2 / 2:4)
+ *   x        [M, ic] with row stride ldx (elements), dtype x_dtype (bf16, f16 or f32)
+ *   bias     NULL or [oc] of bias_dtype
+ *   y        [M, oc] with row stride ldy, dtype y_dtype
+ *   workspace  device scratch of spark_linear_workspace_size() bytes, zero-filled
+ *            before its first use; calls that share a workspace must not overlap on
+ *            the GPU (use one workspace per stream).
+ */
+SPARK_API size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int64_t ic);
+SPARK_API int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
+                 int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype,
+                 int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads (and clears) the error word a kernel leaves in `workspace` when one of its
+ * bounded waits expires; synchronises `stream`.  Returns SPARK_OK or SPARK_ERR_DEVICE. */
+SPARK_API int spark_workspace_check(void* workspace, void* stream);
+
+/* Elementwise SiLU(gate) * up for the MLP between the gate/up and down projections
+ * (the activation the reference model applies between its MLP linears). */
+SPARK_API int spark_silu_mul(const void* gate, const void* up, void* out, int dtype, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARK_B200_H */

@@ -1,0 +1,800 @@
+// gemv.cu -- online-dequant linear for decode-sized batches (M <= 16 per launch).
+//
+// y[M, oc] = x[M, ic] . decode(W)^T (+ bias) with W in one of the packed SPARK
+// formats.  The work is HBM-bound: every packed byte is read exactly once.
+//
+// Data flow per launch
+//   1. k_prepare_x: x (bf16/f16/f32) -> fp16 scaled by a per-token power of two
+//      sigma (max|x|/sigma in [2^14, 2^15)), written in the column order the
+//      format's decoder produces (so a 16-byte load is a ready MMA B fragment).
+//      Products stay exact: every decoded weight has <= 6 significant bits.
+//   2. k_gemv<FMT, NT>: persistent grid, every warp owns a contiguous range of
+//      "units" (16 rows x 256 columns, 512 for 2:4) in row-group-major order.
+//      A warp streams its units through a private ring of shared-memory stages
+//      filled by bulk async copies (cp.async.bulk + mbarrier complete_tx), one
+//      copy per row segment.  Each thread decodes the packed codes of two rows
+//      straight into fp16 A fragments and issues mma.sync m16n8k16 (fp32
+//      accumulate) against the prepared x.  The tensor pipe is nearly idle at
+//      these M; the limits are the HBM stream and the decode instructions.
+//   3. Row groups split between warps are reduced deterministically: each
+//      contributor writes its fp32 partial to the workspace, bumps a per-row-
+//      group counter, and the last arriver sums the partials in warp order.
+//
+// The packed layouts are the reference's (DJAzzs/SPARK 01_core/*_emu.py).
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace spark {
+
+namespace {
+
+constexpr int kWarps = 8;         // warps per CTA
+constexpr int kDepth = 4;         // ring stages per warp
+constexpr int kMaxTokens = 16;    // tokens per launch (NT = 2 MMA n-tiles)
+constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier wait: 2 s
+
+// ---------------------------------------------------------------- format traits
+template <int FMT> struct Fmt;
+template <> struct Fmt<SPARK_FMT_SPFP2> {
+    static constexpr int kCols = 256;        // columns per unit
+    static constexpr int kCodeBytes = 80;    // per row per unit (16 pairs x 5 B)
+    static constexpr int kScaleBytes = 0;
+    static constexpr int kStride = 80;       // smem row stride (bank-conflict free chunk reads)
+    static constexpr int kChunkWords = 5;    // per thread per row
+    static constexpr int kSteps = 8;         // 8-column blocks per thread per unit
+    // code bits per row: 2.5 per weight
+    static int64_t row_bytes(int64_t ic) { return ic / 16 * 5; }
+};
+template <> struct Fmt<SPARK_FMT_FP3> {
+    static constexpr int kCols = 256;
+    static constexpr int kCodeBytes = 96;    // 256 x 3 bits
+    static constexpr int kScaleBytes = 16;
+    static constexpr int kStride = 112;
+    static constexpr int kChunkWords = 6;
+    static constexpr int kSteps = 8;
+    static int64_t row_bytes(int64_t ic) { return ic / 8 * 3; }
+};
+template <> struct Fmt<SPARK_FMT_NVFP4> {
+    static constexpr int kCols = 256;
+    static constexpr int kCodeBytes = 128;
+    static constexpr int kScaleBytes = 16;
+    static constexpr int kStride = 144;
+    static constexpr int kChunkWords = 8;
+    static constexpr int kSteps = 8;
+    static int64_t row_bytes(int64_t ic) { return ic / 2; }
+};
+template <> struct Fmt<SPARK_FMT_TWOFOUR> {
+    static constexpr int kCols = 512;
+    static constexpr int kCodeBytes = 112;   // 16 pairs of 16-blocks x 7 B
+    static constexpr int kScaleBytes = 0;
+    static constexpr int kStride = 112;
+    static constexpr int kChunkWords = 7;
+    static constexpr int kSteps = 16;
+    static int64_t row_bytes(int64_t ic) { return ic / 32 * 7; }
+};
+
+template <int FMT>
+__host__ __device__ constexpr int stage_bytes() {
+    return 16 * Fmt<FMT>::kStride + (Fmt<FMT>::kScaleBytes ? 16 * 16 : 0);
+}
+
+// Column permutation inside each 8-column block: position p of the prepared x
+// holds original column perm[p].  Decoders emit A registers in this order.
+__host__ __device__ constexpr int perm_col(int fmt, int p) {
+    // SPFP2 and FP3 pair code j with code j+4 in one fp16x2 register
+    return (fmt == SPARK_FMT_SPFP2 || fmt == SPARK_FMT_FP3) ? ((p & 1) ? 4 + (p >> 1) : (p >> 1)) : p;
+}
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// two e4m3 bytes (low 16 bits of a) -> f16x2, exact
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t a) {
+    uint32_t d;
+    asm("{ .reg .b16 t; cvt.u16.u32 t, %1; cvt.rn.f16x2.e4m3x2 %0, t; }" : "=r"(d) : "r"(a));
+    return d;
+}
+
+// four bytes of e2m1 pairs -> four f16x2 (byte k -> out[k]; low nibble -> low half)
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t* o) {
+    asm("{ .reg .b8 b0, b1, b2, b3;\n"
+        "  mov.b32 {b0, b1, b2, b3}, %4;\n"
+        "  cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+        "  cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        "  cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+        "  cvt.rn.f16x2.e2m1x2 %3, b3; }"
+        : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+        : "r"(w));
+}
+
+__device__ __forceinline__ void mma_16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait: false once kWaitNs have passed without the phase completing
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t deadline = globaltimer_ns() + kWaitNs;
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 63u && globaltimer_ns() > deadline) return false;
+    }
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// 32-bit window of a little-endian word array starting at bit `pos`
+// (pos may be negative: zeros shift in).  pos and N are compile-time.
+template <int N>
+__device__ __forceinline__ uint32_t window(const uint32_t* c, int pos) {
+    if (pos < 0) return c[0] << (-pos);
+    const int w = pos >> 5, s = pos & 31;
+    if (s == 0) return c[w];
+    const uint32_t hi = (w + 1 < N) ? c[w + 1] : 0u;
+    return __funnelshift_r(c[w], hi, s);
+}
+
+// ---------------------------------------------------------------- decoders
+// Each decoder turns step s of a thread's chunk (8 columns of one row) into
+// four fp16x2 A registers A[0..3]; A[j] covers prepared columns 2j, 2j+1.
+
+// SPFP2 (block_fp2_emu.py:36, :270-308): value = table(+1,-1,0,0)[code] *
+// 2^(e-10).  fp16 of +-2^k has a zero low byte and high byte sign|(k+15)<<2, so
+// one byte permute of the block table [H, H|0x80, 0, 0] decodes two weights:
+// selector nibbles (2, code j, 2, code j+4).
+__device__ __forceinline__ void decode_spfp2(const uint32_t* c, int s, uint32_t* A) {
+    const int q = s >> 1, h = s & 1;
+    const int P = 40 * q + 16 * h;                     // mantissa bit offset
+    const uint32_t e = window<5>(c, 40 * q + 32 + 4 * h) & 0xfu;
+    const uint32_t table = e * 0x404u + 0x9414u;       // [(e+5)<<2, ((e+5)<<2)|0x80, 0, 0]
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t sel = (window<5>(c, P - 4 + 2 * j) & 0x3030u) | 0x0202u;
+        A[j] = prmt(table, 0u, sel);
+    }
+}
+
+// FP3 (fp3_emu.py:47, :142-154): 8 codes of a 24-bit group, code i at bits 3i;
+// unscaled fp16 high bytes of (0,.5,1,1.5,-0,-.5,-1,-1.5) form an 8-byte table
+// (low bytes are zero), then one f16x2 multiply applies the e4m3 scale.
+__device__ __forceinline__ void decode_fp3(const uint32_t* c, uint32_t scale_word, int s, uint32_t* A) {
+    const uint32_t v = window<6>(c, 24 * s) & 0xffffffu;
+    const uint32_t sb = (scale_word >> (8 * (s >> 1))) & 0xffu;
+    const uint32_t s2 = e4m3x2_to_f16x2(sb * 0x101u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t sel = (((v >> (3 * j)) & 7u) << 4) | (((v >> (3 * j + 12)) & 7u) << 12);
+        A[j] = hmul2(prmt(0x3e3c3800u, 0xbebcb880u, sel), s2);
+    }
+}
+
+// NVFP4 (nvfp4_emu.py:109-123): codes are standard e2m1 nibbles (element 2k in
+// the low nibble); the hardware converter gives exact fp16, then the scale.
+__device__ __forceinline__ void decode_nvfp4(const uint32_t* c, uint32_t scale_word, int s, uint32_t* A) {
+    const uint32_t sb = (scale_word >> (8 * (s >> 1))) & 0xffu;
+    const uint32_t s2 = e4m3x2_to_f16x2(sb * 0x101u);
+    uint32_t u[4];
+    e2m1x8_to_f16x2(c[s], u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) A[j] = hmul2(u[j], s2);
+}
+
+// 2:4 SPFP2 (two_four.py:158-189): 28-bit slot per 16-block, 4 groups of 4
+// columns with a 4-bit position mode and two sign bits.
+__device__ __forceinline__ uint32_t tf_half(uint32_t H, uint32_t mode, uint32_t sg, int p) {
+    // byte of the fp16 high half at position p of the group
+    int a = -1, b = -1;
+    if (mode < 6u) {
+        a = mode < 3u ? 0 : (mode < 5u ? 1 : 2);
+        b = mode == 0u ? 1 : (mode == 1u ? 2 : ((mode == 2u || mode == 4u || mode == 5u) ? 3 : 2));
+    } else if (mode >= 8u && mode <= 11u) {
+        a = (int)mode - 8;
+    }
+    if (p == a) return (H | ((sg & 1u) << 7)) << 8;
+    if (p == b) return (H | ((sg >> 1) << 7)) << 8;
+    return 0u;
+}
+
+__device__ __forceinline__ void decode_twofour(const uint32_t* c, int s, uint32_t* A) {
+    const int q = s >> 2, slot = (s >> 1) & 1, half = s & 1;
+    const uint32_t w = window<7>(c, 56 * q + 28 * slot) & 0x0fffffffu;
+    const uint32_t H = (((w >> 24) & 0xfu) + 5u) << 2;
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg) {
+        const int g = 2 * half + gg;
+        const uint32_t mode = (w >> (4 * g)) & 0xfu;
+        const uint32_t sg = (w >> (16 + 2 * g)) & 3u;
+        A[2 * gg] = tf_half(H, mode, sg, 0) | (tf_half(H, mode, sg, 1) << 16);
+        A[2 * gg + 1] = tf_half(H, mode, sg, 2) | (tf_half(H, mode, sg, 3) << 16);
+    }
+}
+
+template <int FMT>
+__device__ __forceinline__ void decode_step(const uint32_t* c, uint32_t sw, int s, uint32_t* A) {
+    if constexpr (FMT == SPARK_FMT_SPFP2) decode_spfp2(c, s, A);
+    else if constexpr (FMT == SPARK_FMT_FP3) decode_fp3(c, sw, s, A);
+    else if constexpr (FMT == SPARK_FMT_NVFP4) decode_nvfp4(c, sw, s, A);
+    else decode_twofour(c, s, A);
+}
+
+// ---------------------------------------------------------------- kernel args
+struct GemvArgs {
+    const uint8_t* wq;
+    const uint8_t* scales;
+    const __half* xp;       // prepared x [M][ic] (fp16, permuted)
+    const float* sigma;     // [M] per-token scale of xp
+    const void* bias;
+    void* y;
+    float* partials;        // [T][2][NT*32*4]
+    int* counters;          // [n_rg]
+    int* err;
+    int64_t oc, ic, ldy;
+    int64_t row_bytes, scale_row_bytes;
+    int64_t n_rg, n_kc, units;
+    int M, bias_dtype, y_dtype;
+};
+
+// ---------------------------------------------------------------- prepare x
+// grid = M blocks.  sigma = 2^(floor(log2 max|x|) - 14) (1 when x is all zero
+// or has a non-finite value); xp[m][8b + p] = fp16(x[m][8b + perm[p]] / sigma).
+__global__ void __launch_bounds__(256) k_prepare_x(const void* __restrict__ x, int x_dtype, int64_t ldx, int64_t ic,
+                                                   int fmt, __half* __restrict__ xp, float* __restrict__ sigma) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    __shared__ float red[8];
+    __shared__ int bad[8];
+    const int m = blockIdx.x;
+    const int64_t row = (int64_t)m * ldx;
+    float mx = 0.0f;
+    int nonfinite = 0;
+    for (int64_t i = threadIdx.x; i < ic; i += blockDim.x) {
+        float a = fabsf(load_as_float(x, x_dtype, row + i));
+        nonfinite |= !(a <= 3.4028235e38f);
+        mx = fmaxf(mx, a);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, o);
+    }
+    if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = mx; bad[threadIdx.x >> 5] = nonfinite; }
+    __syncthreads();
+    float gmx = 0.0f;
+    int gbad = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { gmx = fmaxf(gmx, red[i]); gbad |= bad[i]; }
+    int k = 0;
+    if (!gbad && gmx > 0.0f) {
+        int e;
+        frexpf(gmx, &e);            // gmx = f * 2^e, f in [0.5, 1)
+        k = (e - 1) - 14;
+        k = k < -100 ? -100 : (k > 100 ? 100 : k);
+    }
+    const float inv = ldexpf(1.0f, -k);
+    if (threadIdx.x == 0) sigma[m] = ldexpf(1.0f, k);
+    for (int64_t i = threadIdx.x; i < ic; i += blockDim.x) {
+        const int64_t b = i >> 3;
+        const int p = (int)(i & 7);
+        const float v = load_as_float(x, x_dtype, row + 8 * b + perm_col(fmt, p));
+        xp[(int64_t)m * ic + i] = __float2half_rn(v * inv);
+    }
+}
+
+// ---------------------------------------------------------------- epilogue
+template <int NT>
+__device__ __forceinline__ void write_rows(const GemvArgs& a, int64_t rg, const float (*acc)[4], int lane) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int tok = nt * 8 + 2 * t + (i & 1);
+            const int64_t row = rg * 16 + g + ((i >> 1) ? 8 : 0);
+            if (tok < a.M && row < a.oc) {
+                float v = acc[nt][i] * a.sigma[tok];
+                if (a.bias) v += load_as_float(a.bias, a.bias_dtype, row);
+                store_from_float(a.y, a.y_dtype, (int64_t)tok * a.ldy + row, v);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- main kernel
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
+    using F = Fmt<FMT>;
+    constexpr int SB = stage_bytes<FMT>();
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    uint8_t* ring = smem + warp * kDepth * SB;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kDepth * SB) + warp * kDepth;
+
+    const int64_t T = (int64_t)gridDim.x * kWarps;
+    const int64_t gw = (int64_t)blockIdx.x * kWarps + warp;
+    const int64_t u0 = a.units * gw / T, u1 = a.units * (gw + 1) / T;
+
+    if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < kDepth; ++i) mbar_init(smem_addr(bars + i), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+
+    // issue the bulk copies of unit u into stage `st`
+    auto issue = [&](int64_t u, int st) {
+        const int64_t rg = u / a.n_kc, kc = u - rg * a.n_kc;
+        const int64_t rows = min((int64_t)16, a.oc - rg * 16);
+        const uint32_t bar = smem_addr(bars + st);
+        if (lane == 0) mbar_expect_tx(bar, (uint32_t)(rows * (F::kCodeBytes + F::kScaleBytes)));
+        __syncwarp();
+        uint8_t* dst = ring + st * SB;
+        if (lane < 16) {
+            if (lane < rows)
+                bulk_g2s(smem_addr(dst + lane * F::kStride),
+                         a.wq + (rg * 16 + lane) * a.row_bytes + kc * F::kCodeBytes, F::kCodeBytes, bar);
+        } else if (F::kScaleBytes) {
+            const int r = lane - 16;
+            if (r < rows)
+                bulk_g2s(smem_addr(dst + 16 * F::kStride + r * 16),
+                         a.scales + (rg * 16 + r) * a.scale_row_bytes + kc * 16, 16, bar);
+        }
+    };
+
+    const int64_t n = u1 - u0;
+    for (int i = 0; i < kDepth && i < n; ++i) issue(u0 + i, i);
+
+    // x is produced by k_prepare_x; wait for it (programmatic dependent launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nt][i] = 0.0f;
+
+    int64_t cur_rg = n > 0 ? u0 / a.n_kc : 0;
+    const __half* xrow0 = a.xp + (int64_t)g * a.ic;
+    const __half* xrow1 = a.xp + (int64_t)(g + 8) * a.ic;
+    const bool tok0 = g < a.M, tok1 = (g + 8) < a.M;
+
+    auto flush = [&](int64_t rg) {
+        const int64_t seg0 = max(u0, rg * a.n_kc), seg1 = min(u1, (rg + 1) * a.n_kc);
+        if (seg0 == rg * a.n_kc && seg1 == (rg + 1) * a.n_kc) {
+            write_rows<NT>(a, rg, acc, lane);
+            return;
+        }
+        // partial row group: publish, count, last arriver reduces in warp order
+        const int slot = (rg == u0 / a.n_kc) ? 0 : 1;
+        float* mine = a.partials + ((gw * 2 + slot) * NT * 32 + lane) * 4;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            __stcg(reinterpret_cast<float4*>(mine + nt * 128), make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
+        __threadfence();
+        __syncwarp();
+        // contributors: owners of the first and last unit of the row group
+        const int64_t first = rg * a.n_kc, last = (rg + 1) * a.n_kc - 1;
+        const int64_t w_lo = ((first + 1) * T - 1) / a.units, w_hi = ((last + 1) * T - 1) / a.units;
+        int old = 0;
+        if (lane == 0) old = atomicAdd(a.counters + rg, 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old != (int)(w_hi - w_lo)) return;
+        __threadfence();
+        float sum[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sum[nt][i] = 0.0f;
+        for (int64_t w = w_lo; w <= w_hi; ++w) {
+            const int64_t ws = a.units * w / T;
+            const int sl = (ws / a.n_kc == rg) ? 0 : 1;
+            const float* src = a.partials + ((w * 2 + sl) * NT * 32 + lane) * 4;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                float4 v = __ldcg(reinterpret_cast<const float4*>(src + nt * 128));
+                sum[nt][0] += v.x; sum[nt][1] += v.y; sum[nt][2] += v.z; sum[nt][3] += v.w;
+            }
+        }
+        write_rows<NT>(a, rg, sum, lane);
+        if (lane == 0) a.counters[rg] = 0;
+    };
+
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t u = u0 + i;
+        const int st = (int)(i % kDepth);
+        const uint32_t parity = (uint32_t)((i / kDepth) & 1);
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_addr(bars + st), parity));
+        if (!ok) {
+            if (lane == 0) report_device_error(a.err, 1);
+            // let the copies already issued land before the CTA retires
+            for (int64_t j = i + 1; j < min(n, i + kDepth); ++j)
+                mbar_wait(smem_addr(bars + (j % kDepth)), (uint32_t)((j / kDepth) & 1));
+            return;
+        }
+        const int64_t rg = u / a.n_kc, kc = u - rg * a.n_kc;
+        if (rg != cur_rg) {
+            flush(cur_rg);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[nt][q] = 0.0f;
+            cur_rg = rg;
+        }
+        // this thread's chunk of rows g and g+8
+        const uint8_t* stage = ring + st * SB;
+        uint32_t c0[F::kChunkWords], c1[F::kChunkWords];
+        const uint32_t* r0 = reinterpret_cast<const uint32_t*>(stage + g * F::kStride) + t * F::kChunkWords;
+        const uint32_t* r1 = reinterpret_cast<const uint32_t*>(stage + (g + 8) * F::kStride) + t * F::kChunkWords;
+#pragma unroll
+        for (int k = 0; k < F::kChunkWords; ++k) { c0[k] = r0[k]; c1[k] = r1[k]; }
+        uint32_t sw0 = 0, sw1 = 0;
+        if constexpr (F::kScaleBytes != 0) {
+            const uint32_t* sc = reinterpret_cast<const uint32_t*>(stage + 16 * F::kStride);
+            sw0 = sc[g * 4 + t];
+            sw1 = sc[(g + 8) * 4 + t];
+        }
+        const int64_t col0 = kc * F::kCols + t * (F::kCols / 4);
+#pragma unroll
+        for (int s = 0; s < F::kSteps; ++s) {
+            uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
+            if (tok0) x0 = ldg_nc_v4(xrow0 + col0 + 8 * s);
+            if (NT > 1 && tok1) x1 = ldg_nc_v4(xrow1 + col0 + 8 * s);
+            uint32_t A0[4], A1[4];
+            decode_step<FMT>(c0, sw0, s, A0);
+            decode_step<FMT>(c1, sw1, s, A1);
+            mma_16816(acc[0], A0[0], A1[0], A0[1], A1[1], x0.x, x0.y);
+            mma_16816(acc[0], A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
+            if (NT > 1) {
+                mma_16816(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
+                mma_16816(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
+            }
+        }
+        __syncwarp();
+        if (i + kDepth < n) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(u + kDepth, st);
+        }
+    }
+    if (n > 0) flush(cur_rg);
+}
+
+// ---------------------------------------------------------------- generic path
+// Any shape / alignment / format, one warp per output row: decode from global
+// memory with byte loads and accumulate in fp32.  Used when the fast path's
+// layout conditions do not hold (small or ragged layers, the v1 format).
+__device__ __forceinline__ float decode_generic(int fmt, const uint8_t* wq, const uint8_t* sc, int64_t ic,
+                                                int64_t r, int64_t c) {
+    if (fmt == SPARK_FMT_SPFP2 || fmt == SPARK_FMT_SPFP2_V1) {
+        // flattened block index over the row-major weight (pairs may straddle rows)
+        const int64_t k = r * ic + c;
+        const int64_t b = k >> 3;
+        const int i = (int)(k & 7);
+        uint32_t m, e;
+        if (fmt == SPARK_FMT_SPFP2) {
+            const uint8_t* q = wq + (b >> 1) * 5;
+            const int h = (int)(b & 1);
+            m = (uint32_t)q[2 * h] | ((uint32_t)q[2 * h + 1] << 8);
+            e = h ? (q[4] >> 4) : (q[4] & 0xfu);
+        } else {
+            const uint8_t* q = wq + b * 3;
+            m = (uint32_t)q[0] | ((uint32_t)q[1] << 8);
+            e = q[2] & 0xfu;
+        }
+        const uint32_t code = (m >> (2 * i)) & 3u;
+        const float s = spfp2_scale((int)e);
+        return code == 0 ? s : (code == 1 ? -s : 0.0f);
+    }
+    const int64_t nbr = (ic + 15) / 16;
+    const int64_t k = (r * nbr) * 16 + c;        // row-padded code index
+    if (fmt == SPARK_FMT_FP3) {
+        const int64_t gi = k >> 3;
+        const uint8_t* q = wq + gi * 3;
+        const uint32_t v = (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16);
+        const uint32_t code = (v >> (3 * (k & 7))) & 7u;
+        const float tbl[8] = {0.0f, 0.5f, 1.0f, 1.5f, -0.0f, -0.5f, -1.0f, -1.5f};
+        return tbl[code] * e4m3_to_f32(sc[k >> 4]);
+    }
+    if (fmt == SPARK_FMT_NVFP4) {
+        const uint32_t byte = wq[k >> 1];
+        const uint32_t code = (k & 1) ? (byte >> 4) : (byte & 0xfu);
+        const float pos[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+        const float v = code < 8 ? pos[code] : -pos[code - 8];
+        return v * e4m3_to_f32(sc[k >> 4]);
+    }
+    // 2:4: blocks of 16 over the row-padded flattening, pairs of blocks in 7 bytes
+    const int64_t b = k >> 4;
+    const int pos = (int)(k & 15);
+    const uint8_t* q = wq + (b >> 1) * 7;
+    uint64_t v = 0;
+    for (int i = 0; i < 7; ++i) v |= (uint64_t)q[i] << (8 * i);
+    const uint32_t w = (uint32_t)(v >> (28 * (b & 1))) & 0x0fffffffu;
+    const float s = spfp2_scale((int)((w >> 24) & 0xfu));
+    const int grp = pos >> 2, p = pos & 3;
+    const uint32_t mode = (w >> (4 * grp)) & 0xfu;
+    const float n0 = ((w >> (16 + 2 * grp)) & 1u) ? -s : s;
+    const float n1 = ((w >> (17 + 2 * grp)) & 1u) ? -s : s;
+    if (mode < 6u) {
+        const int pa = mode < 3u ? 0 : (mode < 5u ? 1 : 2);
+        const int pb = mode == 0u ? 1 : (mode == 1u ? 2 : ((mode == 2u || mode == 4u || mode == 5u) ? 3 : 2));
+        return p == pa ? n0 : (p == pb ? n1 : 0.0f);
+    }
+    if (mode >= 8u && mode <= 11u) return p == (int)mode - 8 ? n0 : 0.0f;
+    return 0.0f;
+}
+
+__global__ void __launch_bounds__(256) k_linear_generic(int fmt, const uint8_t* __restrict__ wq,
+                                                        const uint8_t* __restrict__ sc, const void* __restrict__ x,
+                                                        int x_dtype, int64_t M, int64_t oc, int64_t ic, int64_t ldx,
+                                                        const void* __restrict__ bias, int bias_dtype,
+                                                        void* __restrict__ y, int y_dtype, int64_t ldy) {
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= oc) return;
+    for (int64_t m0 = 0; m0 < M; m0 += 8) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int64_t c = lane; c < ic; c += 32) {
+            const float w = decode_generic(fmt, wq, sc, ic, r, c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (m0 + j < M) acc[j] += w * load_as_float(x, x_dtype, (m0 + j) * ldx + c);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float v = acc[j];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && m0 + j < M) {
+                if (bias) v += load_as_float(bias, bias_dtype, r);
+                store_from_float(y, y_dtype, (m0 + j) * ldy + r, v);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- host side
+struct DeviceInfo {
+    int sms = 0;
+    bool attrs_set[8] = {};
+};
+DeviceInfo g_dev[64];
+std::mutex g_mu;
+
+int sm_count(int dev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_dev[dev].sms == 0) cudaDeviceGetAttribute(&g_dev[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+    return g_dev[dev].sms;
+}
+
+template <int FMT, int NT>
+size_t gemv_smem() {
+    return (size_t)kWarps * kDepth * stage_bytes<FMT>() + (size_t)kWarps * kDepth * 8;
+}
+
+template <int FMT, int NT>
+int set_smem_attr(int dev) {
+    static bool done[64] = {};
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemv<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)gemv_smem<FMT, NT>());
+        if (e != cudaSuccess) return set_error((int)e, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        done[dev] = true;
+    }
+    return SPARK_OK;
+}
+
+int cols_per_unit(int fmt) { return fmt == SPARK_FMT_TWOFOUR ? 512 : 256; }
+
+// workspace layout (bytes)
+struct WsLayout {
+    size_t err = 0;        // int error word
+    size_t sigma = 256;    // float[16]
+    size_t xp = 512;       // half[16][ic]
+    size_t partials = 0;   // float[T][2][NT*32*4]
+    size_t counters = 0;   // int[n_rg]
+    size_t total = 0;
+};
+
+WsLayout ws_layout(int64_t ic, int64_t oc, int64_t T) {
+    WsLayout L;
+    L.partials = (L.xp + (size_t)kMaxTokens * ic * 2 + 255) / 256 * 256;
+    L.counters = L.partials + (size_t)T * 2 * 2 * 32 * 4 * sizeof(float);
+    L.total = (L.counters + (size_t)((oc + 15) / 16) * sizeof(int) + 255) / 256 * 256;
+    return L;
+}
+
+int64_t max_warps(int dev) { return (int64_t)sm_count(dev) * 2 * kWarps; }
+
+template <int FMT, int NT>
+int launch_gemv(const GemvArgs& a, int64_t T, cudaStream_t stream) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int rc = set_smem_attr<FMT, NT>(dev);
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(T / kWarps));
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = gemv_smem<FMT, NT>();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv<FMT, NT>, a);
+    if (e != cudaSuccess) return set_error((int)e, "k_gemv launch: %s", cudaGetErrorString(e));
+    return SPARK_OK;
+}
+
+template <int FMT>
+int launch_fmt(const GemvArgs& a, int NT, int64_t T, cudaStream_t s) {
+    return NT == 1 ? launch_gemv<FMT, 1>(a, T, s) : launch_gemv<FMT, 2>(a, T, s);
+}
+
+bool fast_path_ok(int fmt, const uint8_t* wq, const uint8_t* scales, int64_t oc, int64_t ic) {
+    if (fmt == SPARK_FMT_SPFP2_V1) return false;
+    if (ic % cols_per_unit(fmt) != 0) return false;
+    if (!aligned(wq, 16)) return false;
+    if ((fmt == SPARK_FMT_FP3 || fmt == SPARK_FMT_NVFP4) && !aligned(scales, 16)) return false;
+    const int64_t units = (oc + 15) / 16 * (ic / cols_per_unit(fmt));
+    return units >= kWarps;
+}
+
+}  // namespace
+
+}  // namespace spark
+
+// ====================================================================== C ABI
+using namespace spark;
+
+extern "C" {
+
+size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int64_t ic) {
+    (void)fmt;
+    (void)M;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return ws_layout(ic, oc, max_warps(dev)).total;
+}
+
+int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
+                 int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype,
+                 int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+    SPARK_REQUIRE(fmt >= SPARK_FMT_SPFP2 && fmt <= SPARK_FMT_TWOFOUR, SPARK_ERR_INVALID, "spark_linear: bad format %d", fmt);
+    SPARK_REQUIRE(wq && x && y, SPARK_ERR_INVALID, "spark_linear: null pointer");
+    SPARK_REQUIRE(M >= 0 && oc >= 0 && ic >= 0, SPARK_ERR_INVALID, "spark_linear: negative size");
+    SPARK_REQUIRE(ldx >= ic && ldy >= oc, SPARK_ERR_INVALID, "spark_linear: ldx %lld < ic or ldy %lld < oc",
+                  (long long)ldx, (long long)ldy);
+    SPARK_REQUIRE((fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4) || scales, SPARK_ERR_INVALID,
+                  "spark_linear: FP3/NVFP4 need scales");
+    SPARK_REQUIRE(x_dtype >= 0 && x_dtype <= 2 && y_dtype >= 0 && y_dtype <= 2 && bias_dtype >= 0 && bias_dtype <= 2,
+                  SPARK_ERR_INVALID, "spark_linear: bad dtype");
+    if (M == 0 || oc == 0) return SPARK_OK;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (!fast_path_ok(fmt, wq, scales, oc, ic)) {
+        k_linear_generic<<<(unsigned)((oc + 7) / 8), 256, 0, s>>>(fmt, wq, scales, x, x_dtype, M, oc, ic, ldx, bias,
+                                                                  bias_dtype, y, y_dtype, ldy);
+        return check_launch("spark_linear (generic)");
+    }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int64_t Tmax = max_warps(dev);
+    const WsLayout L = ws_layout(ic, oc, Tmax);
+    SPARK_REQUIRE(workspace && workspace_bytes >= L.total, SPARK_ERR_WORKSPACE,
+                  "spark_linear: workspace of %zu bytes needed (got %zu)", L.total, workspace_bytes);
+    SPARK_REQUIRE(aligned(workspace, 256), SPARK_ERR_ALIGNMENT, "spark_linear: workspace must be 256-byte aligned");
+
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const int64_t units = (oc + 15) / 16 * (ic / cols_per_unit(fmt));
+    int64_t T = std::min(Tmax, units) / kWarps * kWarps;
+    GemvArgs a = {};
+    a.wq = wq;
+    a.scales = scales;
+    a.xp = reinterpret_cast<const __half*>(ws + L.xp);
+    a.sigma = reinterpret_cast<const float*>(ws + L.sigma);
+    a.bias = bias;
+    a.partials = reinterpret_cast<float*>(ws + L.partials);
+    a.counters = reinterpret_cast<int*>(ws + L.counters);
+    a.err = reinterpret_cast<int*>(ws + L.err);
+    a.oc = oc;
+    a.ic = ic;
+    a.ldy = ldy;
+    a.bias_dtype = bias_dtype;
+    a.y_dtype = y_dtype;
+    a.n_rg = (oc + 15) / 16;
+    a.n_kc = ic / cols_per_unit(fmt);
+    a.units = units;
+    switch (fmt) {
+        case SPARK_FMT_SPFP2: a.row_bytes = Fmt<SPARK_FMT_SPFP2>::row_bytes(ic); break;
+        case SPARK_FMT_FP3: a.row_bytes = Fmt<SPARK_FMT_FP3>::row_bytes(ic); break;
+        case SPARK_FMT_NVFP4: a.row_bytes = Fmt<SPARK_FMT_NVFP4>::row_bytes(ic); break;
+        default: a.row_bytes = Fmt<SPARK_FMT_TWOFOUR>::row_bytes(ic); break;
+    }
+    a.scale_row_bytes = ic / 16;
+
+    for (int64_t m0 = 0; m0 < M; m0 += kMaxTokens) {
+        const int mc = (int)std::min<int64_t>(kMaxTokens, M - m0);
+        const uint8_t* xb = static_cast<const uint8_t*>(x) + m0 * ldx * (x_dtype == SPARK_DTYPE_F32 ? 4 : 2);
+        k_prepare_x<<<mc, 256, 0, s>>>(xb, x_dtype, ldx, ic, fmt, reinterpret_cast<__half*>(ws + L.xp),
+                                       reinterpret_cast<float*>(ws + L.sigma));
+        int rc = check_launch("spark_linear (prepare)");
+        if (rc) return rc;
+        a.M = mc;
+        a.y = static_cast<uint8_t*>(y) + m0 * ldy * (y_dtype == SPARK_DTYPE_F32 ? 4 : 2);
+        const int NT = mc > 8 ? 2 : 1;
+        switch (fmt) {
+            case SPARK_FMT_SPFP2: rc = launch_fmt<SPARK_FMT_SPFP2>(a, NT, T, s); break;
+            case SPARK_FMT_FP3: rc = launch_fmt<SPARK_FMT_FP3>(a, NT, T, s); break;
+            case SPARK_FMT_NVFP4: rc = launch_fmt<SPARK_FMT_NVFP4>(a, NT, T, s); break;
+            default: rc = launch_fmt<SPARK_FMT_TWOFOUR>(a, NT, T, s); break;
+        }
+        if (rc) return rc;
+    }
+    return SPARK_OK;
+}
+
+int spark_workspace_check(void* workspace, void* stream) {
+    SPARK_REQUIRE(workspace, SPARK_ERR_INVALID, "spark_workspace_check: null workspace");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int flag = 0;
+    cudaError_t e = cudaMemcpyAsync(&flag, workspace, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return set_error((int)e, "spark_workspace_check: %s", cudaGetErrorString(e));
+    if (flag != 0) {
+        cudaMemsetAsync(workspace, 0, sizeof(int), s);
+        return set_error(SPARK_ERR_DEVICE, "a kernel reported error %d (bounded wait expired)", flag);
+    }
+    return SPARK_OK;
+}
+
+}  // extern "C"

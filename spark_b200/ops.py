@@ -1,0 +1,249 @@
+"""torch-facing wrappers of the C ABI: allocate outputs, pass raw pointers and
+the current CUDA stream, raise on a non-zero status.
+
+Every function runs the sm_100a kernels; tensors on the CPU are copied to the
+current CUDA device first and results are returned on the input's device, so
+the functions can stand in for the reference emulators that take CPU tensors.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import (DTYPE_BF16, DTYPE_F16, DTYPE_F32, FMT_FP3, FMT_NVFP4, FMT_SPFP2, FMT_SPFP2_V1,
+                   FMT_TWOFOUR, call)
+
+_DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
+
+FORMATS = {"spfp2": FMT_SPFP2, "spfp2_v1": FMT_SPFP2_V1, "fp3": FMT_FP3, "nvfp4": FMT_NVFP4,
+           "twofour": FMT_TWOFOUR}
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32, bfloat16 or float16") from None
+
+
+def _cuda(t: torch.Tensor) -> torch.Tensor:
+    if not torch.cuda.is_available():
+        raise RuntimeError("spark_b200 needs a CUDA device (no CPU fallback)")
+    if not t.is_cuda:
+        t = t.to(torch.device("cuda", torch.cuda.current_device()))
+    return t.contiguous()
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _bytes(t: torch.Tensor) -> torch.Tensor:
+    """uint8 view of a packed buffer (uint8 or float8_e4m3fn)."""
+    t = _cuda(t)
+    return t.view(torch.uint8) if t.dtype != torch.uint8 else t
+
+
+def _home(out: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    return out if like.is_cuda else out.to(like.device)
+
+
+# ------------------------------------------------------------------ SPFP2
+def spfp2_pack(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """pack_blockwise_paired: (packed uint8[ceil(nb/2)*5], expv uint8[nb])."""
+    x = _cuda(w.detach())
+    n = x.numel()
+    nb = n // 8
+    packed = torch.empty(((nb + 1) // 2) * 5, dtype=torch.uint8, device=x.device)
+    expv = torch.empty(nb, dtype=torch.uint8, device=x.device)
+    call("spark_spfp2_pack", _p(x), _dt(x), n, _p(packed), _p(expv), _stream(x))
+    return _home(packed, w), _home(expv, w)
+
+
+def spfp2_pack_v1(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """pack_blockwise_search(window=2): (packed uint8[nb*3], expv uint8[nb])."""
+    x = _cuda(w.detach())
+    n = x.numel()
+    nb = n // 8
+    packed = torch.empty(nb * 3, dtype=torch.uint8, device=x.device)
+    expv = torch.empty(nb, dtype=torch.uint8, device=x.device)
+    call("spark_spfp2_pack_v1", _p(x), _dt(x), n, _p(packed), _p(expv), _stream(x))
+    return _home(packed, w), _home(expv, w)
+
+
+def spfp2_unpack(packed: torch.Tensor, n_elements: int, dtype=torch.float32) -> torch.Tensor:
+    """unpack_blockwise_paired."""
+    p = _bytes(packed)
+    out = torch.empty(n_elements, dtype=dtype, device=p.device)
+    if p.numel() < (n_elements + 15) // 16 * 5:
+        raise ValueError(f"packed has {p.numel()} bytes, {n_elements} elements need {(n_elements + 15) // 16 * 5}")
+    call("spark_spfp2_unpack", _p(p), n_elements, _p(out), _DT[dtype], _stream(p))
+    return _home(out, packed)
+
+
+def spfp2_unpack_v1(packed: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
+    """unpack_blockwise (3-byte blocks)."""
+    p = _bytes(packed)
+    nb = p.numel() // 3
+    out = torch.empty(nb * 8, dtype=dtype, device=p.device)
+    call("spark_spfp2_unpack_v1", _p(p), nb, _p(out), _DT[dtype], _stream(p))
+    return _home(out, packed)
+
+
+def spfp2_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    """channel_fake_quantize forward over the flattened tensor's 8-blocks."""
+    x = _cuda(w.detach())
+    out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    call("spark_spfp2_fake_quant", _p(x), _dt(x), x.numel(), _p(out), _dt(out), _stream(x))
+    return _home(out, w)
+
+
+# ------------------------------------------------------------------ FP3 / NVFP4
+def _codes_shapes(oc: int, ic: int):
+    nb = (ic + 15) // 16
+    return oc * nb, oc * nb * 16
+
+
+def fp3_pack(w: torch.Tensor, nibble: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp3_pack_3bit (nibble=False) or fp3_pack (nibble=True): (codes, scales e4m3fn)."""
+    x = _cuda(w.detach())
+    oc, ic = x.shape
+    nblk, n = _codes_shapes(oc, ic)
+    codes = torch.empty((n + 1) // 2 if nibble else (n + 7) // 8 * 3, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(nblk, dtype=torch.uint8, device=x.device)
+    call("spark_fp3_pack_nibble" if nibble else "spark_fp3_pack", _p(x), _dt(x), oc, ic, _p(codes), _p(scales),
+         _stream(x))
+    return _home(codes, w), _home(scales.view(torch.float8_e4m3fn), w)
+
+
+def fp3_unpack(codes: torch.Tensor, scales: torch.Tensor, oc: int, ic: int, nibble: bool = False,
+               dtype=torch.float32) -> torch.Tensor:
+    c, s = _bytes(codes), _bytes(scales)
+    out = torch.empty(oc, ic, dtype=dtype, device=c.device)
+    call("spark_fp3_unpack_nibble" if nibble else "spark_fp3_unpack", _p(c), _p(s), oc, ic, _p(out), _DT[dtype],
+         _stream(c))
+    return _home(out, codes)
+
+
+def fp3_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    x = _cuda(w.detach())
+    oc, ic = x.shape
+    out = torch.empty(oc, ic, dtype=out_dtype or torch.float32, device=x.device)
+    call("spark_fp3_fake_quant", _p(x), _dt(x), oc, ic, _p(out), _dt(out), _stream(x))
+    return _home(out, w)
+
+
+def nvfp4_pack(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    x = _cuda(w.detach())
+    oc, ic = x.shape
+    nblk, n = _codes_shapes(oc, ic)
+    codes = torch.empty((n + 1) // 2, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(nblk, dtype=torch.uint8, device=x.device)
+    call("spark_nvfp4_pack", _p(x), _dt(x), oc, ic, _p(codes), _p(scales), _stream(x))
+    return _home(codes, w), _home(scales.view(torch.float8_e4m3fn), w)
+
+
+def nvfp4_unpack(codes: torch.Tensor, scales: torch.Tensor, oc: int, ic: int, dtype=torch.float32) -> torch.Tensor:
+    c, s = _bytes(codes), _bytes(scales)
+    out = torch.empty(oc, ic, dtype=dtype, device=c.device)
+    call("spark_nvfp4_unpack", _p(c), _p(s), oc, ic, _p(out), _DT[dtype], _stream(c))
+    return _home(out, codes)
+
+
+def nvfp4_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    x = _cuda(w.detach())
+    oc, ic = x.shape
+    out = torch.empty(oc, ic, dtype=out_dtype or torch.float32, device=x.device)
+    call("spark_nvfp4_fake_quant", _p(x), _dt(x), oc, ic, _p(out), _dt(out), _stream(x))
+    return _home(out, w)
+
+
+# ------------------------------------------------------------------ 2:4
+def twofour_pack(w: torch.Tensor) -> torch.Tensor:
+    x = _cuda(w.detach())
+    oc, ic = x.shape
+    nblk, _ = _codes_shapes(oc, ic)
+    packed = torch.empty((nblk + 1) // 2 * 7, dtype=torch.uint8, device=x.device)
+    call("spark_twofour_pack", _p(x), _dt(x), oc, ic, _p(packed), _stream(x))
+    return _home(packed, w)
+
+
+def twofour_unpack(packed: torch.Tensor, n_elements: int, dtype=torch.float32) -> torch.Tensor:
+    p = _bytes(packed)
+    out = torch.empty(n_elements, dtype=dtype, device=p.device)
+    call("spark_twofour_unpack", _p(p), n_elements, _p(out), _DT[dtype], _stream(p))
+    return _home(out, packed)
+
+
+def twofour_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    x = _cuda(w.detach())
+    out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    call("spark_twofour_fake_quant", _p(x), _dt(x), x.numel(), _p(out), _dt(out), _stream(x))
+    return _home(out, w)
+
+
+# ------------------------------------------------------------------ linear
+_ws_lock = threading.Lock()
+_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def workspace(device: torch.device, nbytes: int, stream=None) -> torch.Tensor:
+    """Zero-initialised scratch for spark_linear, one per (device, stream)."""
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    key = (device.index if device.index is not None else torch.cuda.current_device(), s.cuda_stream)
+    with _ws_lock:
+        buf = _ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _ws[key] = buf
+    return buf
+
+
+def workspace_size(fmt: int, M: int, oc: int, ic: int) -> int:
+    return int(_lib.lib().spark_linear_workspace_size(fmt, M, oc, ic))
+
+
+def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bias=None, out_dtype=None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[..., oc] = x[..., ic] . decode(W)^T (+ bias) with W packed in `fmt`."""
+    f = FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+    if not x.is_cuda:
+        raise RuntimeError("spark_b200.linear: x must be a CUDA tensor")
+    lead = x.shape[:-1]
+    if x.shape[-1] != ic:
+        raise ValueError(f"x has {x.shape[-1]} features, the weight has {ic}")
+    x2 = x.reshape(-1, ic)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    w = _bytes(wq)
+    s = _bytes(scales) if scales is not None else None
+    b = bias.contiguous() if bias is not None else None
+    y = out if out is not None else torch.empty(M, oc, dtype=out_dtype or x.dtype, device=x.device)
+    nbytes = workspace_size(f, M, oc, ic)
+    ws = workspace(x.device, nbytes)
+    call("spark_linear", f, _p(w), _p(s), _p(x2), _dt(x2), M, oc, ic, x2.stride(0), _p(b),
+         _dt(b) if b is not None else DTYPE_F32, _p(y), _dt(y), y.stride(0), _p(ws), ws.numel(), _stream(x))
+    return y.reshape(*lead, oc)
+
+
+def check_device_errors(device=None) -> None:
+    """Raise if a kernel left an error in a workspace (synchronises)."""
+    for (dev, sh), buf in list(_ws.items()):
+        if device is not None and dev != device:
+            continue
+        call("spark_workspace_check", _p(buf), ctypes.c_void_p(sh))
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    g, u = gate.contiguous(), up.contiguous()
+    out = torch.empty_like(g)
+    call("spark_silu_mul", _p(g), _p(u), _p(out), _dt(g), g.numel(), _stream(g))
+    return out
