@@ -1,0 +1,428 @@
+"""Benchmark of SPARK's online-dequant linear path on B200.
+
+Metric: dequant-GEMV HBM GB/s at M=1 (and prefill TFLOP/s).
+
+Workload: the tiered decode linears of one hybrid-attention
+layer at 4B-like shapes -- gate/up [9728,2560] and down [2560,9728] in SPFP2,
+q/k/v [4096,2560] in FP3 E1M1, out_proj [2560,4096] in NVFP4 -- random
+N(0, 0.02) weights packed on the GPU, bf16 N(0,1) activations, M = 1.
+One step runs one token through L = 8 distinct copies of that layer
+(56 linears, 344 MB of packed weights: more than the 126 MB L2, so every
+step streams its weights from HBM).  `value` is algorithmic bytes (packed
+weights + scales + x + y) per second with everything resident in HBM, the
+step replayed as a CUDA graph.  `e2e` is the same metric through the public
+layer API (spark_b200.inference_v3.V3PackedLinear) with the token read from
+pinned host memory and every output copied back to the host inside the
+timed region.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+With torchrun (N > 1) every rank runs its own replica (weak scaling); the
+step time is the max over ranks.  `--impl reference` times the reference's
+CPU path (decode + fp32 matmul per call, ported to C in oracle/) on the host
+cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS = 8                     # distinct layer copies per step
+SHAPES = [                     # (name, fmt, oc, ic)
+    ("gate_proj", "spfp2", 9728, 2560),
+    ("up_proj", "spfp2", 9728, 2560),
+    ("down_proj", "spfp2", 2560, 9728),
+    ("q_proj", "fp3", 4096, 2560),
+    ("k_proj", "fp3", 4096, 2560),
+    ("v_proj", "fp3", 4096, 2560),
+    ("out_proj", "nvfp4", 2560, 4096),
+]
+CONFIG = {
+    "workload": "BASELINE config 2: tiered decode linears of one 4B-like hybrid-attention layer "
+                "(SPFP2 gate/up/down, FP3 q/k/v, NVFP4 out_proj), M=1, one token through 8 layer copies per step",
+    "M": 1,
+    "layers_per_step": LAYERS,
+    "l2": "weights rotate over 8 distinct layer copies (344 MB) > 126 MB L2",
+    "graph": "each step replayed as one CUDA graph",
+}
+METRIC = "dequant-GEMV HBM GB/s (% of 8 TB/s) at M=1; prefill dequant-GEMM TFLOP/s"
+
+
+def weight_bytes(fmt, oc, ic):
+    if fmt == "spfp2":
+        return oc * ic // 16 * 5
+    if fmt == "fp3":
+        return oc * ic // 8 * 3 + oc * ic // 16
+    if fmt == "nvfp4":
+        return oc * ic // 2 + oc * ic // 16
+    raise ValueError(fmt)
+
+
+def linear_bytes(fmt, oc, ic, M=1, act_bytes=2):
+    return weight_bytes(fmt, oc, ic) + M * ic * act_bytes + M * oc * act_bytes
+
+
+STEP_BYTES = LAYERS * sum(linear_bytes(f, oc, ic) for _, f, oc, ic in SHAPES)
+SPFP2_BYTES = LAYERS * sum(linear_bytes(f, oc, ic) for _, f, oc, ic in SHAPES if f == "spfp2")
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ distributed
+def dist_setup(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ GPU arm
+def build_layers(device):
+    from spark_b200 import ops
+    layers = []
+    g = torch.Generator(device=device)
+    for li in range(LAYERS):
+        g.manual_seed(1000 + li)
+        L = {}
+        for name, fmt, oc, ic in SHAPES:
+            W = torch.randn(oc, ic, device=device, generator=g) * 0.02
+            if fmt == "spfp2":
+                wq, _ = ops.spfp2_pack(W)
+                L[name] = (fmt, wq, None, oc, ic)
+            elif fmt == "fp3":
+                wq, s = ops.fp3_pack(W)
+                L[name] = (fmt, wq, s, oc, ic)
+            else:
+                wq, s = ops.nvfp4_pack(W)
+                L[name] = (fmt, wq, s, oc, ic)
+            del W
+        layers.append(L)
+    torch.cuda.synchronize()
+    return layers
+
+
+def run_gpu(args, rank, world, local):
+    from spark_b200 import ops
+    device = torch.device("cuda", local)
+    layers = build_layers(device)
+    g = torch.Generator(device=device).manual_seed(7)
+    x = {ic: torch.randn(1, ic, device=device, generator=g).bfloat16() for ic in (2560, 4096, 9728)}
+    outs = {}
+    stream = torch.cuda.Stream(device)
+    max_ws = max(ops.workspace_size(ops.FORMATS[f], 1, oc, ic) for _, f, oc, ic in SHAPES)
+    ops.workspace(device, max_ws, stream=stream)
+
+    def step(only=None):
+        for L in layers:
+            for name, (fmt, wq, s, oc, ic) in L.items():
+                if only and fmt != only:
+                    continue
+                key = (name, id(L))
+                outs[key] = ops.linear(fmt, wq, s, x[ic], oc, ic, out=outs.get(key))
+
+    # warm every path once eagerly (allocates outputs), then capture
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+            step("spfp2")
+    torch.cuda.synchronize()
+    graph, graph_spfp2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.graph(graph_spfp2, stream=stream):
+        step("spfp2")
+    torch.cuda.synchronize()
+
+    def timed(gr, k):
+        for _ in range(args.warmup):
+            gr.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(k):
+                gr.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        barrier(world)
+        torch.cuda.synchronize()
+        return max_over_ranks(ms, world)
+
+    with Clocks(local) as clk:
+        ms_total = timed(graph, args.steps)
+    ms_spfp2 = timed(graph_spfp2, args.steps)
+    ops.check_device_errors()
+
+    # ---------------- e2e through the public layer API with host buffers
+    from spark_b200.inference_v3 import V3PackedLinear
+    mods = [{name: V3PackedLinear.from_packed(fmt, wq, s, oc, ic) for name, (fmt, wq, s, oc, ic) in L.items()}
+            for L in layers]
+    xh = {ic: x[ic].cpu().pin_memory() for ic in x}
+    yh = {}
+    for L in mods:
+        for name, m in L.items():
+            yh[(name, id(L))] = torch.empty(1, m.out_features, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * 2 for t in xh.values())
+    d2h = sum(t.numel() * 2 for t in yh.values())
+
+    def e2e_step():
+        xd = {ic: xh[ic].to(device, non_blocking=True) for ic in xh}
+        for L in mods:
+            for name, m in L.items():
+                yh[(name, id(L))].copy_(m(xd[m.in_features]), non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 1)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1), world)
+    barrier(world)
+
+    peak, peak_kind = peaks()
+    value = world * STEP_BYTES * args.steps / (ms_total * 1e-3) / 1e9
+    spfp2_gbs = SPFP2_BYTES * args.steps / (ms_spfp2 * 1e-3) / 1e9
+    e2e_gbs = world * STEP_BYTES * args.steps / (ms_e2e * 1e-3) / 1e9
+    launches = args.steps * LAYERS * len(SHAPES) * 2    # prepare + GEMV per linear
+    traffic = load_traffic()
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_total / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, packed 2.5/3.5/4.5-bit weights, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) bf16 activations)",
+        "config": {**CONFIG, "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "hbm_frac": round(value / world / peak, 4),
+        "roofline": {"bound": "hbm", "kernel": "k_gemv<SPFP2> (+ its k_prepare_x), gate/up/down at M=1",
+                     "achieved": round(spfp2_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(spfp2_gbs / peak, 4), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
+                     if peak_kind == "measured" else "fallback 6650 GB/s",
+                     "traffic": traffic},
+        "gpu_launches": launches,
+        "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "spark_b200.inference_v3.V3PackedLinear, eager, pinned host I/O"},
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(args, budget_s=args.cpu_budget)
+        print(json.dumps(line), flush=True)
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "gemv_spfp2_m1.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------ CPU (reference) arm
+def cpu_layer(seed):
+    """One layer's packed weights for the CPU path (packed by the oracle)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, fmt, oc, ic in SHAPES:
+        W = (rng.standard_normal((oc, ic), dtype=np.float32) * 0.02).astype(np.float32)
+        if fmt == "spfp2":
+            out[name] = (fmt, O.pack_blockwise_paired(W)[0], None, oc, ic)
+        elif fmt == "fp3":
+            c, s = O.fp3_pack_3bit(W)
+            out[name] = (fmt, c, s, oc, ic)
+        else:
+            c, s = O.nvfp4_pack(W)
+            out[name] = (fmt, c, s, oc, ic)
+    return out
+
+
+def cpu_step(layer, xs):
+    from oracle import oracle as O
+    for name, (fmt, wq, s, oc, ic) in layer.items():
+        x = xs[ic]
+        if fmt == "spfp2":
+            O.cpu_spfp2_linear(wq, x, oc, ic)
+        elif fmt == "fp3":
+            O.cpu_fp3_linear(wq, s, x, oc, ic)
+        else:
+            O.cpu_nvfp4_linear(wq, s, x, oc, ic)
+
+
+def cpu_baseline(args, budget_s=15.0):
+    """Time the reference's CPU path (decode + fp32 matmul per call) on a bounded sample."""
+    from oracle import oracle as O
+    layer = cpu_layer(1)
+    rng = np.random.default_rng(2)
+    xs = {ic: rng.standard_normal((1, ic)).astype(np.float32) for ic in (2560, 4096, 9728)}
+    cpu_step(layer, xs)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and n < 200:
+        cpu_step(layer, xs)
+        n += 1
+    dt = time.perf_counter() - t0
+    per_layer = STEP_BYTES / LAYERS
+    return {"value": round(per_layer * n / dt / 1e9, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{n} passes over one config-2 layer (7 linears) at M=1 in {dt:.1f} s: "
+                      "decode + fp32 matmul per call, rows split over OpenMP threads"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    layer = cpu_layer(1)
+    rng = np.random.default_rng(2)
+    xs = {ic: rng.standard_normal((1, ic)).astype(np.float32) for ic in (2560, 4096, 9728)}
+    for _ in range(args.warmup):
+        cpu_step(layer, xs)
+    # a CPU step is a bounded sample of the GPU step: one token through ONE layer
+    # copy (7 linears, 43 MB of packed weights) instead of eight
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(layer, xs)
+    dt = time.perf_counter() - t0
+    value = STEP_BYTES / LAYERS * args.steps / dt / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (reference CPU emulator path)",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)", "config": CONFIG, "impl": "reference",
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+                         "sample": f"{args.steps} steps, each one token through one config-2 layer (7 linears), "
+                                   "decode + fp32 matmul per call (oracle/spark_oracle.c port of the reference's "
+                                   "CPU path)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="spark_b200", choices=["spark_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        run_reference(args, rank, world)
+        return
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        run_gpu(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

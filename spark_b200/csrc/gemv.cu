@@ -288,9 +288,11 @@ struct GemvArgs {
 
 // ---------------------------------------------------------------- prepare x
 // grid = M blocks.  sigma = 2^(floor(log2 max|x|) - 14) (1 when x is all zero
-// or has a non-finite value); xp[m][8b + p] = fp16(x[m][8b + perm[p]] / sigma).
+// or has a non-finite value); xp[m][8b + p] = fp16(x[m][8b + perm[p]] / sigma),
+// and with `split` xp[16 + m][.] holds the fp16 remainder.
 __global__ void __launch_bounds__(256) k_prepare_x(const void* __restrict__ x, int x_dtype, int64_t ldx, int64_t ic,
-                                                   int fmt, __half* __restrict__ xp, float* __restrict__ sigma) {
+                                                   int fmt, __half* __restrict__ xp, float* __restrict__ sigma,
+                                                   int split) {
     asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float red[8];
     __shared__ int bad[8];
@@ -325,8 +327,12 @@ __global__ void __launch_bounds__(256) k_prepare_x(const void* __restrict__ x, i
     for (int64_t i = threadIdx.x; i < ic; i += blockDim.x) {
         const int64_t b = i >> 3;
         const int p = (int)(i & 7);
-        const float v = load_as_float(x, x_dtype, row + 8 * b + perm_col(fmt, p));
-        xp[(int64_t)m * ic + i] = __float2half_rn(v * inv);
+        const float v = load_as_float(x, x_dtype, row + 8 * b + perm_col(fmt, p)) * inv;
+        const __half hi = __float2half_rn(v);
+        xp[(int64_t)m * ic + i] = hi;
+        // fp32 / fp16 activations carry more bits than one fp16 holds after
+        // scaling: keep the remainder as a second fp16 part
+        if (split) xp[(int64_t)(kMaxTokens + m) * ic + i] = __float2half_rn(v - __half2float(hi));
     }
 }
 
@@ -350,7 +356,7 @@ __device__ __forceinline__ void write_rows(const GemvArgs& a, int64_t rg, const 
 }
 
 // ---------------------------------------------------------------- main kernel
-template <int FMT, int NT>
+template <int FMT, int NT, int XS>
 __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
     using F = Fmt<FMT>;
     constexpr int SB = stage_bytes<FMT>();
@@ -486,17 +492,21 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
         const int64_t col0 = kc * F::kCols + t * (F::kCols / 4);
 #pragma unroll
         for (int s = 0; s < F::kSteps; ++s) {
-            uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
-            if (tok0) x0 = ldg_nc_v4(xrow0 + col0 + 8 * s);
-            if (NT > 1 && tok1) x1 = ldg_nc_v4(xrow1 + col0 + 8 * s);
             uint32_t A0[4], A1[4];
             decode_step<FMT>(c0, sw0, s, A0);
             decode_step<FMT>(c1, sw1, s, A1);
-            mma_16816(acc[0], A0[0], A1[0], A0[1], A1[1], x0.x, x0.y);
-            mma_16816(acc[0], A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
-            if (NT > 1) {
-                mma_16816(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
-                mma_16816(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
+#pragma unroll
+            for (int part = 0; part < XS; ++part) {
+                const int64_t po = (int64_t)part * kMaxTokens * a.ic;
+                uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
+                if (tok0) x0 = ldg_nc_v4(xrow0 + po + col0 + 8 * s);
+                if (NT > 1 && tok1) x1 = ldg_nc_v4(xrow1 + po + col0 + 8 * s);
+                mma_16816(acc[0], A0[0], A1[0], A0[1], A1[1], x0.x, x0.y);
+                mma_16816(acc[0], A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
+                if (NT > 1) {
+                    mma_16816(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
+                    mma_16816(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
+                }
             }
         }
         __syncwarp();
@@ -615,18 +625,18 @@ int sm_count(int dev) {
     return g_dev[dev].sms;
 }
 
-template <int FMT, int NT>
+template <int FMT>
 size_t gemv_smem() {
     return (size_t)kWarps * kDepth * stage_bytes<FMT>() + (size_t)kWarps * kDepth * 8;
 }
 
-template <int FMT, int NT>
+template <int FMT, int NT, int XS>
 int set_smem_attr(int dev) {
     static bool done[64] = {};
     std::lock_guard<std::mutex> lk(g_mu);
     if (!done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemv<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)gemv_smem<FMT, NT>());
+        cudaError_t e = cudaFuncSetAttribute(k_gemv<FMT, NT, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)gemv_smem<FMT>());
         if (e != cudaSuccess) return set_error((int)e, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         done[dev] = true;
     }
@@ -635,50 +645,55 @@ int set_smem_attr(int dev) {
 
 int cols_per_unit(int fmt) { return fmt == SPARK_FMT_TWOFOUR ? 512 : 256; }
 
-// workspace layout (bytes)
+// Workspace layout (bytes).  Everything whose contents must survive from one
+// call to the next (the self-resetting row-group counters) sits at an offset
+// that does not depend on the problem shape; only the prepared activations,
+// which every call rewrites, grow with ic.
+constexpr int64_t kMaxRowGroups = 1 << 16;   // oc <= 1,048,576
 struct WsLayout {
-    size_t err = 0;        // int error word
-    size_t sigma = 256;    // float[16]
-    size_t xp = 512;       // half[16][ic]
-    size_t partials = 0;   // float[T][2][NT*32*4]
-    size_t counters = 0;   // int[n_rg]
+    size_t err = 0;                            // int error word
+    size_t sigma = 256;                        // float[16]
+    size_t counters = 512;                     // int[kMaxRowGroups]
+    size_t partials = 0;                       // float[T][2][2*32*4]
+    size_t xp = 0;                             // half[2][16][ic] (hi, lo parts)
     size_t total = 0;
 };
 
-WsLayout ws_layout(int64_t ic, int64_t oc, int64_t T) {
+WsLayout ws_layout(int64_t ic, int64_t T) {
     WsLayout L;
-    L.partials = (L.xp + (size_t)kMaxTokens * ic * 2 + 255) / 256 * 256;
-    L.counters = L.partials + (size_t)T * 2 * 2 * 32 * 4 * sizeof(float);
-    L.total = (L.counters + (size_t)((oc + 15) / 16) * sizeof(int) + 255) / 256 * 256;
+    L.partials = L.counters + (size_t)kMaxRowGroups * sizeof(int);
+    L.xp = L.partials + (size_t)T * 2 * 2 * 32 * 4 * sizeof(float);
+    L.total = (L.xp + (size_t)2 * kMaxTokens * ic * 2 + 255) / 256 * 256;
     return L;
 }
 
 int64_t max_warps(int dev) { return (int64_t)sm_count(dev) * 2 * kWarps; }
 
-template <int FMT, int NT>
+template <int FMT, int NT, int XS>
 int launch_gemv(const GemvArgs& a, int64_t T, cudaStream_t stream) {
     int dev = 0;
     cudaGetDevice(&dev);
-    int rc = set_smem_attr<FMT, NT>(dev);
+    int rc = set_smem_attr<FMT, NT, XS>(dev);
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(T / kWarps));
     cfg.blockDim = dim3(kWarps * 32);
-    cfg.dynamicSmemBytes = gemv_smem<FMT, NT>();
+    cfg.dynamicSmemBytes = gemv_smem<FMT>();
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv<FMT, NT>, a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv<FMT, NT, XS>, a);
     if (e != cudaSuccess) return set_error((int)e, "k_gemv launch: %s", cudaGetErrorString(e));
     return SPARK_OK;
 }
 
 template <int FMT>
-int launch_fmt(const GemvArgs& a, int NT, int64_t T, cudaStream_t s) {
-    return NT == 1 ? launch_gemv<FMT, 1>(a, T, s) : launch_gemv<FMT, 2>(a, T, s);
+int launch_fmt(const GemvArgs& a, int NT, int XS, int64_t T, cudaStream_t s) {
+    if (XS == 1) return NT == 1 ? launch_gemv<FMT, 1, 1>(a, T, s) : launch_gemv<FMT, 2, 1>(a, T, s);
+    return NT == 1 ? launch_gemv<FMT, 1, 2>(a, T, s) : launch_gemv<FMT, 2, 2>(a, T, s);
 }
 
 bool fast_path_ok(int fmt, const uint8_t* wq, const uint8_t* scales, int64_t oc, int64_t ic) {
@@ -704,7 +719,7 @@ size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int64_t ic) {
     (void)M;
     int dev = 0;
     cudaGetDevice(&dev);
-    return ws_layout(ic, oc, max_warps(dev)).total;
+    return ws_layout(ic, max_warps(dev)).total;
 }
 
 int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
@@ -729,10 +744,12 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
     int dev = 0;
     cudaGetDevice(&dev);
     const int64_t Tmax = max_warps(dev);
-    const WsLayout L = ws_layout(ic, oc, Tmax);
+    const WsLayout L = ws_layout(ic, Tmax);
     SPARK_REQUIRE(workspace && workspace_bytes >= L.total, SPARK_ERR_WORKSPACE,
                   "spark_linear: workspace of %zu bytes needed (got %zu)", L.total, workspace_bytes);
     SPARK_REQUIRE(aligned(workspace, 256), SPARK_ERR_ALIGNMENT, "spark_linear: workspace must be 256-byte aligned");
+    SPARK_REQUIRE((oc + 15) / 16 <= kMaxRowGroups, SPARK_ERR_UNSUPPORTED, "spark_linear: oc %lld above %lld",
+                  (long long)oc, (long long)(16 * kMaxRowGroups));
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const int64_t units = (oc + 15) / 16 * (ic / cols_per_unit(fmt));
@@ -765,18 +782,19 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
     for (int64_t m0 = 0; m0 < M; m0 += kMaxTokens) {
         const int mc = (int)std::min<int64_t>(kMaxTokens, M - m0);
         const uint8_t* xb = static_cast<const uint8_t*>(x) + m0 * ldx * (x_dtype == SPARK_DTYPE_F32 ? 4 : 2);
+        const int XS = x_dtype == SPARK_DTYPE_BF16 ? 1 : 2;
         k_prepare_x<<<mc, 256, 0, s>>>(xb, x_dtype, ldx, ic, fmt, reinterpret_cast<__half*>(ws + L.xp),
-                                       reinterpret_cast<float*>(ws + L.sigma));
+                                       reinterpret_cast<float*>(ws + L.sigma), XS == 2);
         int rc = check_launch("spark_linear (prepare)");
         if (rc) return rc;
         a.M = mc;
         a.y = static_cast<uint8_t*>(y) + m0 * ldy * (y_dtype == SPARK_DTYPE_F32 ? 4 : 2);
         const int NT = mc > 8 ? 2 : 1;
         switch (fmt) {
-            case SPARK_FMT_SPFP2: rc = launch_fmt<SPARK_FMT_SPFP2>(a, NT, T, s); break;
-            case SPARK_FMT_FP3: rc = launch_fmt<SPARK_FMT_FP3>(a, NT, T, s); break;
-            case SPARK_FMT_NVFP4: rc = launch_fmt<SPARK_FMT_NVFP4>(a, NT, T, s); break;
-            default: rc = launch_fmt<SPARK_FMT_TWOFOUR>(a, NT, T, s); break;
+            case SPARK_FMT_SPFP2: rc = launch_fmt<SPARK_FMT_SPFP2>(a, NT, XS, T, s); break;
+            case SPARK_FMT_FP3: rc = launch_fmt<SPARK_FMT_FP3>(a, NT, XS, T, s); break;
+            case SPARK_FMT_NVFP4: rc = launch_fmt<SPARK_FMT_NVFP4>(a, NT, XS, T, s); break;
+            default: rc = launch_fmt<SPARK_FMT_TWOFOUR>(a, NT, XS, T, s); break;
         }
         if (rc) return rc;
     }

@@ -277,6 +277,10 @@ __device__ __forceinline__ uint8_t block_scale(const float* v, float top, float*
 __constant__ float kFp3Table[8] = {0.0f, 0.5f, 1.0f, 1.5f, -0.0f, -0.5f, -1.0f, -1.5f};  // fp3_emu.py:47
 __constant__ float kE2m1Pos[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};      // nvfp4_emu.py:20
 
+// code value times block scale.  A NaN scale propagates its own bits, as the
+// x86 multiply behind the reference does (the GPU would return a canonical NaN).
+__device__ __forceinline__ float scaled(float v, float s) { return (s != s) ? s : __fmul_rn(v, s); }
+
 // FP3 codes of one 16-block (sign<<2 | mag)
 __device__ __forceinline__ void fp3_codes16(const float* v, float s, uint32_t* c) {
 #pragma unroll
@@ -347,7 +351,7 @@ __global__ void __launch_bounds__(kThreads) k_fp3_unpack(const uint8_t* __restri
     const int64_t r = b / nbr, c0 = (b % nbr) * 16;
 #pragma unroll
     for (int i = 0; i < 16; ++i)
-        if (c0 + i < ic) store_from_float(out, dtype, r * ic + c0 + i, __fmul_rn(kFp3Table[c[i]], s));
+        if (c0 + i < ic) store_from_float(out, dtype, r * ic + c0 + i, scaled(kFp3Table[c[i]], s));
 }
 
 __global__ void __launch_bounds__(kThreads) k_fp3_fake_quant(const void* __restrict__ w, int in_dtype, int64_t oc,
@@ -364,7 +368,7 @@ __global__ void __launch_bounds__(kThreads) k_fp3_fake_quant(const void* __restr
     fp3_codes16(v, s, c);
 #pragma unroll
     for (int i = 0; i < 16; ++i)
-        if (c0 + i < ic) store_from_float(out, out_dtype, r * ic + c0 + i, __fmul_rn(kFp3Table[c[i]], s));
+        if (c0 + i < ic) store_from_float(out, out_dtype, r * ic + c0 + i, scaled(kFp3Table[c[i]], s));
 }
 
 __global__ void __launch_bounds__(kThreads) k_nvfp4_pack(const void* __restrict__ w, int dtype, int64_t oc,
@@ -407,7 +411,7 @@ __global__ void __launch_bounds__(kThreads) k_nvfp4_unpack(const uint8_t* __rest
     for (int i = 0; i < 16; ++i) {
         uint32_t code = (i & 1) ? (q[i / 2] >> 4) : (q[i / 2] & 0xf);
         float v = code < 8 ? kE2m1Pos[code] : -kE2m1Pos[code - 8];
-        if (c0 + i < ic) store_from_float(out, dtype, r * ic + c0 + i, __fmul_rn(v, s));
+        if (c0 + i < ic) store_from_float(out, dtype, r * ic + c0 + i, scaled(v, s));
     }
 }
 
@@ -427,7 +431,7 @@ __global__ void __launch_bounds__(kThreads) k_nvfp4_fake_quant(const void* __res
         float xs = __fdiv_rn(v[i], s);
         float q = kE2m1Pos[e2m1_idx(fabsf(xs))];
         float sg = xs > 0.0f ? 1.0f : (xs < 0.0f ? -1.0f : 0.0f);
-        if (c0 + i < ic) store_from_float(out, out_dtype, r * ic + c0 + i, __fmul_rn(__fmul_rn(sg, q), s));
+        if (c0 + i < ic) store_from_float(out, out_dtype, r * ic + c0 + i, scaled(__fmul_rn(sg, q), s));
     }
 }
 

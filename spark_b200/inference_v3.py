@@ -1,0 +1,108 @@
+"""Packed-weight-resident inference layers (mirror of 04_scripts/inference_v3.py).
+
+The reference's ``V3SPFP2Layer`` (inference_v3.py:33-57) keeps the SPFP2 bytes
+on the GPU and calls a JIT-built kernel on fp16 activations; its kernel reads
+the 3-byte block layout although containers hold the paired 5-byte layout
+(quant_linear.py:258-271 -> block_fp2_emu.py:231-267).  Here the layer reads
+the container's paired bytes, takes bf16/fp16/fp32 activations, returns
+x.dtype, and dispatches to the sm_100a decode GEMV / GEMM.  ``V3PackedLinear``
+extends the same idea to the FP3, NVFP4 and 2:4 tiers.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import ops
+
+_FMT_KEYS = {
+    "spfp2": ("_packed", None),
+    "fp3": ("_fp3_codes", "_fp3_scales"),
+    "nvfp4": ("_nvfp4_codes", "_nvfp4_scales"),
+    "twofour": ("_packed", None),
+}
+
+
+class V3PackedLinear(nn.Module):
+    """y = x . decode(W)^T + bias with W kept packed in HBM.
+
+    fmt: "spfp2" (paired 5 B / 16 w), "spfp2_v1" (3 B / 8 w), "fp3" (3-bit codes +
+    e4m3 scales), "nvfp4" (e2m1 nibbles + e4m3 scales) or "twofour" (7 B / 32 w).
+    """
+
+    def __init__(self, fmt: str, packed: torch.Tensor, out_features: int, in_features: int,
+                 scales: torch.Tensor | None = None, bias: torch.Tensor | None = None):
+        super().__init__()
+        if fmt not in ops.FORMATS:
+            raise ValueError(f"unknown format {fmt!r}")
+        self.fmt = fmt
+        self.out_features = out_features
+        self.in_features = in_features
+        self.register_buffer("w_packed", packed)
+        self.register_buffer("w_scales", scales.view(torch.uint8) if scales is not None else None)
+        self.register_buffer("bias", bias)
+
+    @classmethod
+    def from_packed(cls, fmt, packed, scales, out_features, in_features, bias=None):
+        return cls(fmt, packed, out_features, in_features, scales=scales, bias=bias)
+
+    @classmethod
+    def from_state(cls, state: dict, name: str, fmt: str, device="cuda"):
+        """Build from a SPARK state dict entry (<name>_packed / _fp3_codes / ... + _meta)."""
+        codes_key, scales_key = _FMT_KEYS[fmt]
+        oc, ic = (int(v) for v in state[name + "_meta"][:2])
+        packed = state[name + codes_key].to(device)
+        scales = state[name + scales_key].to(device) if scales_key else None
+        b = state.get(f"param::{name}.bias")
+        return cls(fmt, packed, oc, ic, scales=scales, bias=b.to(device) if b is not None else None)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        ic = self.in_features
+        if self.fmt in ("spfp2", "spfp2_v1") and ic % 8:
+            # the layer classes pack rows padded to whole 8-blocks (quant_linear.py:183-192)
+            pad = (ic + 7) // 8 * 8
+            x = torch.nn.functional.pad(x, (0, pad - ic))
+            ic = pad
+        return ops.linear(self.fmt, self.w_packed, self.w_scales, x, self.out_features, ic,
+                          bias=self.bias, out_dtype=x.dtype)
+
+    def extra_repr(self) -> str:
+        return f"fmt={self.fmt}, in_features={self.in_features}, out_features={self.out_features}"
+
+
+class V3SPFP2Layer(V3PackedLinear):
+    """Drop-in for inference_v3.V3SPFP2Layer(packed_weight, out_features, in_features, bias)."""
+
+    def __init__(self, packed_weight, out_features, in_features, bias=None):
+        if bias is not None and bias.numel() == 0:
+            bias = None
+        super().__init__("spfp2", packed_weight, out_features, in_features, bias=bias)
+
+
+def build_v3_layers(model: nn.Module, state: dict, device="cuda") -> int:
+    """Replace every nn.Linear that has packed weights in `state` by a packed-
+    resident layer (the reference's build_v3_model, inference_v3.py:60-105,
+    extended from MLP SPFP2 to every tier).  Returns the number replaced."""
+    n = 0
+    for name, module in list(model.named_modules()):
+        if not isinstance(module, nn.Linear):
+            continue
+        fmt = None
+        if name + "_fp3_codes" in state:
+            fmt = "fp3"
+        elif name + "_nvfp4_codes" in state:
+            fmt = "nvfp4"
+        elif name + "_packed" in state:
+            meta = state.get(name + "_meta")
+            if meta is None:
+                continue
+            oc, ic = int(meta[0]), int(meta[1])
+            nb = oc * ((ic + 7) // 8)
+            fmt = "spfp2" if state[name + "_packed"].numel() == (nb + 1) // 2 * 5 else "spfp2_v1"
+        if fmt is None or name + "_meta" not in state:
+            continue
+        layer = V3PackedLinear.from_state(state, name, fmt, device=device)
+        parent = model.get_submodule(".".join(name.split(".")[:-1])) if "." in name else model
+        setattr(parent, name.split(".")[-1], layer)
+        n += 1
+    return n
