@@ -180,14 +180,13 @@ def build_layers(device):
         for name, fmt, oc, ic in SHAPES:
             W = torch.randn(oc, ic, device=device, generator=g) * 0.02
             if fmt == "spfp2":
-                wq, _ = ops.spfp2_pack(W)
-                L[name] = (fmt, wq, None, oc, ic)
+                wq, s = ops.spfp2_pack(W)[0], None
             elif fmt == "fp3":
                 wq, s = ops.fp3_pack(W)
-                L[name] = (fmt, wq, s, oc, ic)
             else:
                 wq, s = ops.nvfp4_pack(W)
-                L[name] = (fmt, wq, s, oc, ic)
+            # the layer API keeps the fragment-major copy for the GEMV
+            L[name] = (fmt, wq, s, oc, ic, ops.tile_weights(fmt, wq, s, oc, ic))
             del W
         layers.append(L)
     torch.cuda.synchronize()
@@ -207,11 +206,11 @@ def run_gpu(args, rank, world, local):
 
     def step(only=None):
         for L in layers:
-            for name, (fmt, wq, s, oc, ic) in L.items():
+            for name, (fmt, wq, s, oc, ic, wt) in L.items():
                 if only and fmt != only:
                     continue
                 key = (name, id(L))
-                outs[key] = ops.linear(fmt, wq, s, x[ic], oc, ic, out=outs.get(key))
+                outs[key] = ops.linear(fmt, wt, None, x[ic], oc, ic, out=outs.get(key), tiled=True)
 
     # warm every path once eagerly (allocates outputs), then capture
     with torch.cuda.stream(stream):
@@ -251,7 +250,7 @@ def run_gpu(args, rank, world, local):
 
     # ---------------- e2e through the public layer API with host buffers
     from spark_b200.inference_v3 import V3PackedLinear
-    mods = [{name: V3PackedLinear.from_packed(fmt, wq, s, oc, ic) for name, (fmt, wq, s, oc, ic) in L.items()}
+    mods = [{name: V3PackedLinear.from_packed(fmt, wq, s, oc, ic) for name, (fmt, wq, s, oc, ic, _) in L.items()}
             for L in layers]
     xh = {ic: x[ic].cpu().pin_memory() for ic in x}
     yh = {}
@@ -295,7 +294,7 @@ def run_gpu(args, rank, world, local):
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) bf16 activations)",
         "config": {**CONFIG, "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "hbm_frac": round(value / world / peak, 4),
-        "roofline": {"bound": "hbm", "kernel": "k_gemv<SPFP2> (+ its k_prepare_x), gate/up/down at M=1",
+        "roofline": {"bound": "hbm", "kernel": "k_gemv_tiled<SPFP2> (+ its k_prepare_x), gate/up/down at M=1",
                      "achieved": round(spfp2_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(spfp2_gbs / peak, 4), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
                      if peak_kind == "measured" else "fallback 6650 GB/s",
@@ -400,6 +399,45 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_profile(args):
+    """A few plain launches of one linear (for ncu captures; prints timing only)."""
+    from spark_b200 import ops
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    shapes = {"spfp2": (9728, 2560), "fp3": (4096, 2560), "nvfp4": (2560, 4096), "twofour": (2560, 9728)}
+    oc, ic = shapes[args.profile]
+    oc = args.oc or oc
+    ic = args.ic or ic
+    g = torch.Generator(device=device).manual_seed(3)
+    W = torch.randn(oc, ic, device=device, generator=g) * 0.02
+    s = None
+    if args.profile == "spfp2":
+        wq, _ = ops.spfp2_pack(W)
+    elif args.profile == "fp3":
+        wq, s = ops.fp3_pack(W)
+    elif args.profile == "nvfp4":
+        wq, s = ops.nvfp4_pack(W)
+    else:
+        wq = ops.twofour_pack(W)
+    x = torch.randn(args.M, ic, device=device, generator=g).bfloat16()
+    wt = ops.tile_weights(args.profile, wq, s, oc, ic)
+    y = None
+    for _ in range(2):
+        y = ops.linear(args.profile, wt, None, x, oc, ic, out=y, tiled=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        y = ops.linear(args.profile, wt, None, x, oc, ic, out=y, tiled=True)
+    e1.record()
+    torch.cuda.synchronize()
+    ops.check_device_errors()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    nbytes = weight_bytes(args.profile, oc, ic) if args.profile != "twofour" else oc * ic // 32 * 7
+    print(json.dumps({"profile": args.profile, "M": args.M, "oc": oc, "ic": ic, "launches": args.steps,
+                      "us_per_call": round(us, 2), "weight_GBps": round(nbytes / us / 1e3, 1)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -408,7 +446,15 @@ def main():
     ap.add_argument("--impl", default="spark_b200", choices=["spark_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--profile", choices=["spfp2", "fp3", "nvfp4", "twofour"],
+                    help="run a few plain launches of one linear (ncu captures)")
+    ap.add_argument("--M", type=int, default=1)
+    ap.add_argument("--oc", type=int, default=0, help="profile mode: output features")
+    ap.add_argument("--ic", type=int, default=0, help="profile mode: input features")
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args)
+        return
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

@@ -50,6 +50,9 @@ extern "C" {
 #define SPARK_FMT_FP3 2      /* 3-bit codes + e4m3 scales (the container's *_fp3_codes/_fp3_scales) */
 #define SPARK_FMT_NVFP4 3    /* e2m1 nibbles + e4m3 scales (*_nvfp4_codes/_nvfp4_scales) */
 #define SPARK_FMT_TWOFOUR 4  /* 2:4-sparse SPFP2, 7 B / 32 weights ("v3-24") */
+/* OR'ed into a format: the weight buffer holds the fragment-major ("tiled")
+ * copy made by spark_tile_weights (scales embedded) instead of the reference layout */
+#define SPARK_LAYOUT_TILED 0x100
 
 SPARK_API const char* spark_last_error(void);
 SPARK_API int spark_version(void);
@@ -127,6 +130,16 @@ SPARK_API size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int
 SPARK_API int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
                  int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype,
                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fragment-major copy of a packed weight for spark_linear(fmt | SPARK_LAYOUT_TILED):
+ * the same bytes (codes and, for FP3/NVFP4, scales) permuted so every thread of the
+ * decode GEMV reads its MMA fragments with coalesced 16-byte loads.  No counterpart
+ * in the reference; it is built once when a layer is loaded.  spark_tiled_bytes
+ * returns the size, or 0 when the shape has no tiled layout (ic not a multiple of
+ * 256, 512 for 2:4). */
+SPARK_API size_t spark_tiled_bytes(int fmt, int64_t oc, int64_t ic);
+SPARK_API int spark_tile_weights(int fmt, const uint8_t* wq, const uint8_t* scales, int64_t oc, int64_t ic,
+                                 uint8_t* tiled, void* stream);
 
 /* Reads (and clears) the error word a kernel leaves in `workspace` when one of its
  * bounded waits expires; synchronises `stream`.  Returns SPARK_OK or SPARK_ERR_DEVICE. */

@@ -23,6 +23,7 @@ ERR_DEVICE = -5
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 FMT_SPFP2, FMT_SPFP2_V1, FMT_FP3, FMT_NVFP4, FMT_TWOFOUR = 0, 1, 2, 3, 4
+LAYOUT_TILED = 0x100
 
 
 class SparkError(RuntimeError):
@@ -60,6 +61,8 @@ _SIGNATURES = {
     "spark_linear_workspace_size": (_sz, [_i, _i64, _i64, _i64]),
     "spark_linear": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p]),
     "spark_workspace_check": (_i, [_p, _p]),
+    "spark_tiled_bytes": (_sz, [_i, _i64, _i64]),
+    "spark_tile_weights": (_i, [_i, _p, _p, _i64, _i64, _p, _p]),
     "spark_silu_mul": (_i, [_p, _p, _p, _i, _i64, _p]),
 }
 

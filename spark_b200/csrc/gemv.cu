@@ -75,6 +75,18 @@ template <> struct Fmt<SPARK_FMT_TWOFOUR> {
     static int64_t row_bytes(int64_t ic) { return ic / 32 * 7; }
 };
 
+// Fragment-major ("tiled") layout: per unit, thread (g, t) owns kFragWords
+// words = [chunk of row g][scale word of row g][chunk of row g+8][scale word of
+// row g+8]; the unit is stored as kFragWords/4 lane-interleaved 16-byte vectors
+// followed by one lane-interleaved 8-byte tail (kFragWords % 4 == 2 for every
+// format), so a warp fetches a unit with fully coalesced vector copies.
+template <int FMT>
+__host__ __device__ constexpr int frag_words() {
+    return 2 * (Fmt<FMT>::kChunkWords + (Fmt<FMT>::kScaleBytes ? 1 : 0));
+}
+template <int FMT>
+__host__ __device__ constexpr int unit_bytes_tiled() { return 32 * frag_words<FMT>() * 4; }
+
 template <int FMT>
 __host__ __device__ constexpr int stage_bytes() {
     return 16 * Fmt<FMT>::kStride + (Fmt<FMT>::kScaleBytes ? 16 * 16 : 0);
@@ -82,9 +94,13 @@ __host__ __device__ constexpr int stage_bytes() {
 
 // Column permutation inside each 8-column block: position p of the prepared x
 // holds original column perm[p].  Decoders emit A registers in this order.
-__host__ __device__ constexpr int perm_col(int fmt, int p) {
-    // SPFP2 and FP3 pair code j with code j+4 in one fp16x2 register
-    return (fmt == SPARK_FMT_SPFP2 || fmt == SPARK_FMT_FP3) ? ((p & 1) ? 4 + (p >> 1) : (p >> 1)) : p;
+//   kPermNatural  tiled SPFP2 (codes re-ordered at tile time), NVFP4, 2:4
+//   kPermSpfp2    SPFP2 in the reference layout: registers hold codes (0,2) (1,3) (4,6) (5,7)
+//   kPermFp3      FP3: registers hold codes (0,4) (1,5) (2,6) (3,7)
+constexpr int kPermNatural = 0, kPermSpfp2 = 1, kPermFp3 = 2;
+__host__ __device__ constexpr int perm_col(int perm, int p) {
+    return perm == kPermSpfp2 ? ((p & 4) | ((p & 1) << 1) | ((p >> 1) & 1))
+         : perm == kPermFp3 ? ((p & 1) ? 4 + (p >> 1) : (p >> 1)) : p;
 }
 
 // ---------------------------------------------------------------- PTX helpers
@@ -125,8 +141,7 @@ __device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t* o) {
 
 __device__ __forceinline__ void mma_16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -140,12 +155,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// try_wait with a suspend-time hint: the warp sleeps until the phase completes
+// (or ~20 us pass) instead of spinning through issue slots
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(20000u)
         : "memory");
     return ok != 0;
 }
@@ -156,7 +173,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     const uint64_t deadline = globaltimer_ns() + kWaitNs;
     for (uint32_t i = 0;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63u) == 63u && globaltimer_ns() > deadline) return false;
+        if (globaltimer_ns() > deadline) return false;
     }
 }
 
@@ -169,7 +186,7 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
     uint4 v;
-    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
@@ -191,19 +208,23 @@ __device__ __forceinline__ uint32_t window(const uint32_t* c, int pos) {
 // four fp16x2 A registers A[0..3]; A[j] covers prepared columns 2j, 2j+1.
 
 // SPFP2 (block_fp2_emu.py:36, :270-308): value = table(+1,-1,0,0)[code] *
-// 2^(e-10).  fp16 of +-2^k has a zero low byte and high byte sign|(k+15)<<2, so
-// one byte permute of the block table [H, H|0x80, 0, 0] decodes two weights:
-// selector nibbles (2, code j, 2, code j+4).
+// 2^(e-10).  fp16 of +-2^k has a zero low byte and high byte
+// sign | (k+15) << 2, so one byte permute of the block table
+// [H, H|0x80, 0, 0] turns four codes (selector nibbles = codes, upper two
+// bits clear) into four high bytes; two constant permutes interleave them
+// with zero low bytes.  Registers hold codes (0,2) (1,3) (4,6) (5,7).
 __device__ __forceinline__ void decode_spfp2(const uint32_t* c, int s, uint32_t* A) {
     const int q = s >> 1, h = s & 1;
     const int P = 40 * q + 16 * h;                     // mantissa bit offset
     const uint32_t e = window<5>(c, 40 * q + 32 + 4 * h) & 0xfu;
     const uint32_t table = e * 0x404u + 0x9414u;       // [(e+5)<<2, ((e+5)<<2)|0x80, 0, 0]
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t sel = (window<5>(c, P - 4 + 2 * j) & 0x3030u) | 0x0202u;
-        A[j] = prmt(table, 0u, sel);
-    }
+    const uint32_t m = window<5>(c, P);
+    const uint32_t he = prmt(table, 0u, m & 0x3333u);          // high bytes of codes 0,2,4,6
+    const uint32_t ho = prmt(table, 0u, (m >> 2) & 0x3333u);   // codes 1,3,5,7
+    A[0] = prmt(he, 0u, 0x1404u);
+    A[1] = prmt(ho, 0u, 0x1404u);
+    A[2] = prmt(he, 0u, 0x3424u);
+    A[3] = prmt(ho, 0u, 0x3424u);
 }
 
 // FP3 (fp3_emu.py:47, :142-154): 8 codes of a 24-bit group, code i at bits 3i;
@@ -232,9 +253,29 @@ __device__ __forceinline__ void decode_nvfp4(const uint32_t* c, uint32_t scale_w
 }
 
 // 2:4 SPFP2 (two_four.py:158-189): 28-bit slot per 16-block, 4 groups of 4
-// columns with a 4-bit position mode and two sign bits.
-__device__ __forceinline__ uint32_t tf_half(uint32_t H, uint32_t mode, uint32_t sg, int p) {
-    // byte of the fp16 high half at position p of the group
+// columns with a 4-bit position mode and two sign bits (decode_twofour_t).
+// bf16 variants for SPFP2 and 2:4 (weights +-2^(e-10), e in [0,15]).  bf16 of
+// +-2^k has biased exponent E = 117 + e: high byte sign | E >> 1, low byte
+// (E & 1) << 7.  A 16-entry shared-memory table holds, per e, the byte tables
+// [H, H|0x80, 0, 0] and [L, L, 0, 0]; the tiled layout stores each mantissa
+// word with codes (1,2) and (5,6) swapped so the registers come out in
+// natural column order (0,1) (2,3) (4,5) (6,7).
+__device__ __forceinline__ void decode_spfp2_bf16(const uint32_t* c, int s, const uint2* lut, uint32_t* A) {
+    const int q = s >> 1, h = s & 1;
+    const int P = 40 * q + 16 * h;
+    const uint2 tab = *reinterpret_cast<const uint2*>(
+        reinterpret_cast<const uint8_t*>(lut) + (window<5>(c, 40 * q + 32 + 4 * h - 3) & 0x78u));
+    const uint32_t m = window<5>(c, P);
+    const uint32_t se = m & 0x3333u, so = (m >> 2) & 0x3333u;
+    const uint32_t he = prmt(tab.x, 0u, se), ho = prmt(tab.x, 0u, so);
+    const uint32_t le = prmt(tab.y, 0u, se), lo = prmt(tab.y, 0u, so);
+    A[0] = prmt(le, he, 0x5140u);
+    A[1] = prmt(lo, ho, 0x5140u);
+    A[2] = prmt(le, he, 0x7362u);
+    A[3] = prmt(lo, ho, 0x7362u);
+}
+
+__device__ __forceinline__ uint32_t tf_val(uint32_t H16, uint32_t mode, uint32_t sg, int p) {
     int a = -1, b = -1;
     if (mode < 6u) {
         a = mode < 3u ? 0 : (mode < 5u ? 1 : 2);
@@ -242,23 +283,34 @@ __device__ __forceinline__ uint32_t tf_half(uint32_t H, uint32_t mode, uint32_t 
     } else if (mode >= 8u && mode <= 11u) {
         a = (int)mode - 8;
     }
-    if (p == a) return (H | ((sg & 1u) << 7)) << 8;
-    if (p == b) return (H | ((sg >> 1) << 7)) << 8;
+    if (p == a) return H16 | ((sg & 1u) << 15);
+    if (p == b) return H16 | ((sg >> 1) << 15);
     return 0u;
 }
 
-__device__ __forceinline__ void decode_twofour(const uint32_t* c, int s, uint32_t* A) {
+// 2:4 with either fp16 or bf16 magnitude bits
+template <bool BF>
+__device__ __forceinline__ void decode_twofour_t(const uint32_t* c, int s, uint32_t* A) {
     const int q = s >> 2, slot = (s >> 1) & 1, half = s & 1;
     const uint32_t w = window<7>(c, 56 * q + 28 * slot) & 0x0fffffffu;
-    const uint32_t H = (((w >> 24) & 0xfu) + 5u) << 2;
+    const uint32_t e = (w >> 24) & 0xfu;
+    const uint32_t H16 = BF ? (117u + e) << 7 : (e + 5u) << 10;
 #pragma unroll
     for (int gg = 0; gg < 2; ++gg) {
         const int g = 2 * half + gg;
         const uint32_t mode = (w >> (4 * g)) & 0xfu;
         const uint32_t sg = (w >> (16 + 2 * g)) & 3u;
-        A[2 * gg] = tf_half(H, mode, sg, 0) | (tf_half(H, mode, sg, 1) << 16);
-        A[2 * gg + 1] = tf_half(H, mode, sg, 2) | (tf_half(H, mode, sg, 3) << 16);
+        A[2 * gg] = tf_val(H16, mode, sg, 0) | (tf_val(H16, mode, sg, 1) << 16);
+        A[2 * gg + 1] = tf_val(H16, mode, sg, 2) | (tf_val(H16, mode, sg, 3) << 16);
     }
+}
+
+__device__ __forceinline__ void mma_16816_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 template <int FMT>
@@ -266,7 +318,7 @@ __device__ __forceinline__ void decode_step(const uint32_t* c, uint32_t sw, int 
     if constexpr (FMT == SPARK_FMT_SPFP2) decode_spfp2(c, s, A);
     else if constexpr (FMT == SPARK_FMT_FP3) decode_fp3(c, sw, s, A);
     else if constexpr (FMT == SPARK_FMT_NVFP4) decode_nvfp4(c, sw, s, A);
-    else decode_twofour(c, s, A);
+    else decode_twofour_t<false>(c, s, A);
 }
 
 // ---------------------------------------------------------------- kernel args
@@ -274,6 +326,8 @@ struct GemvArgs {
     const uint8_t* wq;
     const uint8_t* scales;
     const __half* xp;       // prepared x [M][ic] (fp16, permuted)
+    const void* x_raw;      // caller's bf16 x (kernels that stage x themselves)
+    int64_t ldx;
     const float* sigma;     // [M] per-token scale of xp
     const void* bias;
     void* y;
@@ -287,24 +341,78 @@ struct GemvArgs {
 };
 
 // ---------------------------------------------------------------- prepare x
-// grid = M blocks.  sigma = 2^(floor(log2 max|x|) - 14) (1 when x is all zero
-// or has a non-finite value); xp[m][8b + p] = fp16(x[m][8b + perm[p]] / sigma),
-// and with `split` xp[16 + m][.] holds the fp16 remainder.
-__global__ void __launch_bounds__(256) k_prepare_x(const void* __restrict__ x, int x_dtype, int64_t ldx, int64_t ic,
-                                                   int fmt, __half* __restrict__ xp, float* __restrict__ sigma,
-                                                   int split) {
+// grid = M blocks of kPrepThreads.  sigma = 2^(floor(log2 max|x|) - 14) (1 when
+// x is all zero or has a non-finite value); xp[m][8b + p] =
+// fp16(x[m][8b + perm[p]] / sigma), and with `split` xp[16 + m][.] holds the
+// fp16 remainder (fp32 / fp16 activations carry more bits than one fp16 after
+// scaling).  One pass: each thread keeps its 8-element blocks in registers
+// between the max reduction and the conversion.
+constexpr int kPrepThreads = 512;
+constexpr int kPrepBlocks = 4;   // 8-element blocks per thread kept in registers
+
+__device__ __forceinline__ void load8(const void* x, int dt, int64_t off, float* v) {
+    if (dt == SPARK_DTYPE_BF16 || dt == SPARK_DTYPE_F16) {
+        const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (dt == SPARK_DTYPE_BF16) {
+                v[2 * i] = __uint_as_float(w[i] << 16);
+                v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+            } else {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                v[2 * i] = f.x;
+                v[2 * i + 1] = f.y;
+            }
+        }
+    } else {
+        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
+        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + off + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+}
+
+__global__ void __launch_bounds__(kPrepThreads) k_prepare_x(const void* __restrict__ x, int x_dtype, int64_t ldx,
+                                                            int64_t ic, int fmt, __half* __restrict__ xp,
+                                                            float* __restrict__ sigma, int split) {
+    // launched as a programmatic dependent of the previous kernel on the stream:
+    // x may be that kernel's output, so wait for it before reading; let the
+    // GEMV that consumes this kernel's output launch right away
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
-    __shared__ float red[8];
-    __shared__ int bad[8];
+    __shared__ float red[kPrepThreads / 32];
+    __shared__ int bad[kPrepThreads / 32];
     const int m = blockIdx.x;
     const int64_t row = (int64_t)m * ldx;
+    const int64_t nblk = ic / 8;
+    const bool vec = ((ldx & 7) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    float v[kPrepBlocks][8];
     float mx = 0.0f;
     int nonfinite = 0;
-    for (int64_t i = threadIdx.x; i < ic; i += blockDim.x) {
-        float a = fabsf(load_as_float(x, x_dtype, row + i));
-        nonfinite |= !(a <= 3.4028235e38f);
-        mx = fmaxf(mx, a);
+#pragma unroll
+    for (int k = 0; k < kPrepBlocks; ++k) {
+        const int64_t b = threadIdx.x + (int64_t)k * kPrepThreads;
+        if (b < nblk) {
+            if (vec) load8(x, x_dtype, row + 8 * b, v[k]);
+            else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[k][i] = load_as_float(x, x_dtype, row + 8 * b + i);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float a = fabsf(v[k][i]);
+                nonfinite |= !(a <= 3.4028235e38f);
+                mx = fmaxf(mx, a);
+            }
+        }
     }
+    // columns beyond kPrepBlocks * kPrepThreads * 8 (very wide layers): second pass
+    for (int64_t b = threadIdx.x + (int64_t)kPrepBlocks * kPrepThreads; b < nblk; b += kPrepThreads)
+        for (int i = 0; i < 8; ++i) {
+            const float a = fabsf(load_as_float(x, x_dtype, row + 8 * b + i));
+            nonfinite |= !(a <= 3.4028235e38f);
+            mx = fmaxf(mx, a);
+        }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -314,31 +422,49 @@ __global__ void __launch_bounds__(256) k_prepare_x(const void* __restrict__ x, i
     __syncthreads();
     float gmx = 0.0f;
     int gbad = 0;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { gmx = fmaxf(gmx, red[i]); gbad |= bad[i]; }
-    int k = 0;
+#pragma unroll
+    for (int i = 0; i < kPrepThreads / 32; ++i) { gmx = fmaxf(gmx, red[i]); gbad |= bad[i]; }
+    int k2 = 0;
     if (!gbad && gmx > 0.0f) {
         int e;
         frexpf(gmx, &e);            // gmx = f * 2^e, f in [0.5, 1)
-        k = (e - 1) - 14;
-        k = k < -100 ? -100 : (k > 100 ? 100 : k);
+        k2 = (e - 1) - 14;
+        k2 = k2 < -100 ? -100 : (k2 > 100 ? 100 : k2);
     }
-    const float inv = ldexpf(1.0f, -k);
-    if (threadIdx.x == 0) sigma[m] = ldexpf(1.0f, k);
-    for (int64_t i = threadIdx.x; i < ic; i += blockDim.x) {
-        const int64_t b = i >> 3;
-        const int p = (int)(i & 7);
-        const float v = load_as_float(x, x_dtype, row + 8 * b + perm_col(fmt, p)) * inv;
-        const __half hi = __float2half_rn(v);
-        xp[(int64_t)m * ic + i] = hi;
-        // fp32 / fp16 activations carry more bits than one fp16 holds after
-        // scaling: keep the remainder as a second fp16 part
-        if (split) xp[(int64_t)(kMaxTokens + m) * ic + i] = __float2half_rn(v - __half2float(hi));
+    const float inv = ldexpf(1.0f, -k2);
+    if (threadIdx.x == 0) sigma[m] = ldexpf(1.0f, k2);
+    auto emit = [&](int64_t b, const float* vb) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int p = 0; p < 8; p += 2) {
+            const float a0 = vb[perm_col(fmt, p)] * inv, a1 = vb[perm_col(fmt, p + 1)] * inv;  // fmt = perm id
+            const __half2 h2 = __floats2half2_rn(a0, a1);
+            hi[p / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+            const float2 back = __half22float2(h2);
+            const __half2 l2 = __floats2half2_rn(a0 - back.x, a1 - back.y);
+            lo[p / 2] = *reinterpret_cast<const uint32_t*>(&l2);
+        }
+        *reinterpret_cast<uint4*>(xp + (int64_t)m * ic + 8 * b) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        if (split)
+            *reinterpret_cast<uint4*>(xp + (int64_t)(kMaxTokens + m) * ic + 8 * b) =
+                make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    };
+#pragma unroll
+    for (int k = 0; k < kPrepBlocks; ++k) {
+        const int64_t b = threadIdx.x + (int64_t)k * kPrepThreads;
+        if (b < nblk) emit(b, v[k]);
+    }
+    for (int64_t b = threadIdx.x + (int64_t)kPrepBlocks * kPrepThreads; b < nblk; b += kPrepThreads) {
+        float vb[8];
+        for (int i = 0; i < 8; ++i) vb[i] = load_as_float(x, x_dtype, row + 8 * b + i);
+        emit(b, vb);
     }
 }
 
 // ---------------------------------------------------------------- epilogue
 template <int NT>
-__device__ __forceinline__ void write_rows(const GemvArgs& a, int64_t rg, const float (*acc)[4], int lane) {
+__device__ __forceinline__ void write_rows(const GemvArgs& a, int64_t rg, const float (*acc)[4], int lane,
+                                           const float* sig) {
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -347,7 +473,7 @@ __device__ __forceinline__ void write_rows(const GemvArgs& a, int64_t rg, const 
             const int tok = nt * 8 + 2 * t + (i & 1);
             const int64_t row = rg * 16 + g + ((i >> 1) ? 8 : 0);
             if (tok < a.M && row < a.oc) {
-                float v = acc[nt][i] * a.sigma[tok];
+                float v = sig ? acc[nt][i] * sig[tok] : acc[nt][i];
                 if (a.bias) v += load_as_float(a.bias, a.bias_dtype, row);
                 store_from_float(a.y, a.y_dtype, (int64_t)tok * a.ldy + row, v);
             }
@@ -357,7 +483,7 @@ __device__ __forceinline__ void write_rows(const GemvArgs& a, int64_t rg, const 
 
 // ---------------------------------------------------------------- main kernel
 template <int FMT, int NT, int XS>
-__global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, 2) k_gemv(const GemvArgs a) {
     using F = Fmt<FMT>;
     constexpr int SB = stage_bytes<FMT>();
     extern __shared__ __align__(128) uint8_t smem[];
@@ -366,9 +492,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
     uint8_t* ring = smem + warp * kDepth * SB;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kDepth * SB) + warp * kDepth;
 
-    const int64_t T = (int64_t)gridDim.x * kWarps;
-    const int64_t gw = (int64_t)blockIdx.x * kWarps + warp;
-    const int64_t u0 = a.units * gw / T, u1 = a.units * (gw + 1) / T;
+    // all unit bookkeeping in 32-bit integers (units < 2^31 is checked on the host)
+    const int T = (int)gridDim.x * kWarps;
+    const int gw = (int)blockIdx.x * kWarps + warp;
+    const int U = (int)a.units, nkc = (int)a.n_kc;
+    const int u0 = (int)((int64_t)U * gw / T), u1 = (int)((int64_t)U * (gw + 1) / T);
+    const int n = u1 - u0;
 
     if (lane == 0) {
 #pragma unroll
@@ -377,28 +506,35 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
     }
     __syncwarp();
 
-    // issue the bulk copies of unit u into stage `st`
-    auto issue = [&](int64_t u, int st) {
-        const int64_t rg = u / a.n_kc, kc = u - rg * a.n_kc;
-        const int64_t rows = min((int64_t)16, a.oc - rg * 16);
+    // producer cursor: (rg, kc) of the next unit to copy
+    int prg = u0 / nkc, pkc = u0 - prg * nkc;
+    const uint8_t* wrow = a.wq + ((int64_t)prg * 16 + (lane & 15)) * a.row_bytes;
+    const uint8_t* srow = a.scales + ((int64_t)prg * 16 + (lane & 15)) * a.scale_row_bytes;
+    auto issue = [&](int st) {
+        const int rows = min(16, (int)(a.oc - (int64_t)prg * 16));
         const uint32_t bar = smem_addr(bars + st);
         if (lane == 0) mbar_expect_tx(bar, (uint32_t)(rows * (F::kCodeBytes + F::kScaleBytes)));
         __syncwarp();
         uint8_t* dst = ring + st * SB;
         if (lane < 16) {
             if (lane < rows)
-                bulk_g2s(smem_addr(dst + lane * F::kStride),
-                         a.wq + (rg * 16 + lane) * a.row_bytes + kc * F::kCodeBytes, F::kCodeBytes, bar);
+                bulk_g2s(smem_addr(dst + lane * F::kStride), wrow + pkc * F::kCodeBytes, F::kCodeBytes, bar);
         } else if (F::kScaleBytes) {
-            const int r = lane - 16;
-            if (r < rows)
-                bulk_g2s(smem_addr(dst + 16 * F::kStride + r * 16),
-                         a.scales + (rg * 16 + r) * a.scale_row_bytes + kc * 16, 16, bar);
+            if (lane - 16 < rows)
+                bulk_g2s(smem_addr(dst + 16 * F::kStride + (lane - 16) * 16), srow + pkc * 16, 16, bar);
+        }
+        if (++pkc == nkc) {
+            pkc = 0;
+            ++prg;
+            wrow += 16 * a.row_bytes;
+            srow += 16 * a.scale_row_bytes;
         }
     };
 
-    const int64_t n = u1 - u0;
-    for (int i = 0; i < kDepth && i < n; ++i) issue(u0 + i, i);
+    for (int i = 0; i < kDepth && i < n; ++i) issue(i);
+    // the next kernel on the stream may launch now and stage its own weights;
+    // it waits (griddepcontrol.wait) for this grid before touching shared data
+    asm volatile("griddepcontrol.launch_dependents;");
 
     // x is produced by k_prepare_x; wait for it (programmatic dependent launch)
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -409,72 +545,64 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[nt][i] = 0.0f;
 
-    int64_t cur_rg = n > 0 ? u0 / a.n_kc : 0;
-    const __half* xrow0 = a.xp + (int64_t)g * a.ic;
-    const __half* xrow1 = a.xp + (int64_t)(g + 8) * a.ic;
+    const __half* xrow0 = a.xp + (int64_t)g * a.ic + t * (F::kCols / 4);
+    const __half* xrow1 = a.xp + (int64_t)(g + 8) * a.ic + t * (F::kCols / 4);
     const bool tok0 = g < a.M, tok1 = (g + 8) < a.M;
+    const int rg_first = u0 / nkc;
 
-    auto flush = [&](int64_t rg) {
-        const int64_t seg0 = max(u0, rg * a.n_kc), seg1 = min(u1, (rg + 1) * a.n_kc);
-        if (seg0 == rg * a.n_kc && seg1 == (rg + 1) * a.n_kc) {
-            write_rows<NT>(a, rg, acc, lane);
+    auto flush = [&](int rg, int seg0, int seg1) {
+        if (seg0 == rg * nkc && seg1 == (rg + 1) * nkc) {
+            write_rows<NT>(a, rg, acc, lane, a.sigma);
             return;
         }
         // partial row group: publish, count, last arriver reduces in warp order
-        const int slot = (rg == u0 / a.n_kc) ? 0 : 1;
-        float* mine = a.partials + ((gw * 2 + slot) * NT * 32 + lane) * 4;
+        const int slot = (rg == rg_first) ? 0 : 1;
+        float* mine = a.partials + (((int64_t)gw * 2 + slot) * NT * 32 + lane) * 4;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
             __stcg(reinterpret_cast<float4*>(mine + nt * 128), make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
         __threadfence();
         __syncwarp();
         // contributors: owners of the first and last unit of the row group
-        const int64_t first = rg * a.n_kc, last = (rg + 1) * a.n_kc - 1;
-        const int64_t w_lo = ((first + 1) * T - 1) / a.units, w_hi = ((last + 1) * T - 1) / a.units;
+        const int64_t first = (int64_t)rg * nkc, last = (int64_t)(rg + 1) * nkc - 1;
+        const int w_lo = (int)(((first + 1) * T - 1) / U), w_hi = (int)(((last + 1) * T - 1) / U);
         int old = 0;
         if (lane == 0) old = atomicAdd(a.counters + rg, 1);
         old = __shfl_sync(0xffffffffu, old, 0);
-        if (old != (int)(w_hi - w_lo)) return;
+        if (old != w_hi - w_lo) return;
         __threadfence();
         float sum[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int i = 0; i < 4; ++i) sum[nt][i] = 0.0f;
-        for (int64_t w = w_lo; w <= w_hi; ++w) {
-            const int64_t ws = a.units * w / T;
-            const int sl = (ws / a.n_kc == rg) ? 0 : 1;
-            const float* src = a.partials + ((w * 2 + sl) * NT * 32 + lane) * 4;
+        for (int w = w_lo; w <= w_hi; ++w) {
+            const int ws = (int)((int64_t)U * w / T);
+            const int sl = (ws / nkc == rg) ? 0 : 1;
+            const float* src = a.partials + (((int64_t)w * 2 + sl) * NT * 32 + lane) * 4;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 float4 v = __ldcg(reinterpret_cast<const float4*>(src + nt * 128));
                 sum[nt][0] += v.x; sum[nt][1] += v.y; sum[nt][2] += v.z; sum[nt][3] += v.w;
             }
         }
-        write_rows<NT>(a, rg, sum, lane);
+        write_rows<NT>(a, rg, sum, lane, a.sigma);
         if (lane == 0) a.counters[rg] = 0;
     };
 
-    for (int64_t i = 0; i < n; ++i) {
-        const int64_t u = u0 + i;
-        const int st = (int)(i % kDepth);
+    // consumer cursor
+    int crg = rg_first, ckc = u0 - rg_first * nkc;
+    int seg0 = u0;
+    for (int i = 0; i < n; ++i) {
+        const int st = i % kDepth;
         const uint32_t parity = (uint32_t)((i / kDepth) & 1);
         const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_addr(bars + st), parity));
         if (!ok) {
             if (lane == 0) report_device_error(a.err, 1);
             // let the copies already issued land before the CTA retires
-            for (int64_t j = i + 1; j < min(n, i + kDepth); ++j)
+            for (int j = i + 1; j < min(n, i + kDepth); ++j)
                 mbar_wait(smem_addr(bars + (j % kDepth)), (uint32_t)((j / kDepth) & 1));
             return;
-        }
-        const int64_t rg = u / a.n_kc, kc = u - rg * a.n_kc;
-        if (rg != cur_rg) {
-            flush(cur_rg);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) acc[nt][q] = 0.0f;
-            cur_rg = rg;
         }
         // this thread's chunk of rows g and g+8
         const uint8_t* stage = ring + st * SB;
@@ -489,7 +617,15 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
             sw0 = sc[g * 4 + t];
             sw1 = sc[(g + 8) * 4 + t];
         }
-        const int64_t col0 = kc * F::kCols + t * (F::kCols / 4);
+        // the stage must be fully read into registers before the bulk copy of
+        // unit i + kDepth overwrites it: consume every loaded word, then sync
+#pragma unroll
+        for (int k = 0; k < F::kChunkWords; ++k) asm volatile("" ::"r"(c0[k]), "r"(c1[k]));
+        asm volatile("" ::"r"(sw0), "r"(sw1));
+        __syncwarp();
+        if (i + kDepth < n) issue(st);
+
+        const int64_t col0 = (int64_t)ckc * F::kCols;
 #pragma unroll
         for (int s = 0; s < F::kSteps; ++s) {
             uint32_t A0[4], A1[4];
@@ -497,10 +633,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
             decode_step<FMT>(c1, sw1, s, A1);
 #pragma unroll
             for (int part = 0; part < XS; ++part) {
-                const int64_t po = (int64_t)part * kMaxTokens * a.ic;
+                const int64_t po = (int64_t)part * kMaxTokens * a.ic + col0 + 8 * s;
                 uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
-                if (tok0) x0 = ldg_nc_v4(xrow0 + po + col0 + 8 * s);
-                if (NT > 1 && tok1) x1 = ldg_nc_v4(xrow1 + po + col0 + 8 * s);
+                if (tok0) x0 = ldg_nc_v4(xrow0 + po);
+                if (NT > 1 && tok1) x1 = ldg_nc_v4(xrow1 + po);
                 mma_16816(acc[0], A0[0], A1[0], A0[1], A1[1], x0.x, x0.y);
                 mma_16816(acc[0], A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
                 if (NT > 1) {
@@ -509,13 +645,277 @@ __global__ void __launch_bounds__(kWarps * 32, 1) k_gemv(const GemvArgs a) {
                 }
             }
         }
-        __syncwarp();
-        if (i + kDepth < n) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(u + kDepth, st);
+        // advance the consumer cursor; flush at the end of a row group
+        const int u = u0 + i;
+        if (++ckc == nkc || i + 1 == n) {
+            flush(crg, seg0, u + 1);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[nt][q] = 0.0f;
+            if (ckc == nkc) { ckc = 0; ++crg; }
+            seg0 = u + 1;
         }
     }
-    if (n > 0) flush(cur_rg);
+}
+
+// ---------------------------------------------------------------- tiled layout
+// thread = (unit, lane): gather the lane's fragment words from the reference
+// layout and store them in fragment-major order
+template <int FMT>
+__global__ void __launch_bounds__(256) k_tile(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ scales,
+                                              int64_t oc, int64_t row_bytes, int64_t scale_row_bytes, int64_t n_kc,
+                                              int64_t units, uint8_t* __restrict__ tiled) {
+    using F = Fmt<FMT>;
+    constexpr int FW = frag_words<FMT>();
+    constexpr int NV = FW / 4;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t u = idx >> 5;
+    const int lane = (int)(idx & 31);
+    if (u >= units) return;
+    const int64_t rg = u / n_kc, kc = u - rg * n_kc;
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t w[FW];
+    int k = 0;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int64_t row = rg * 16 + g + 8 * half;
+        const bool ok = row < oc;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(wq + row * row_bytes + kc * F::kCodeBytes) +
+                              t * F::kChunkWords;
+#pragma unroll
+        for (int j = 0; j < F::kChunkWords; ++j) {
+            uint32_t v = 0u;
+            if (ok) v = src[j];
+            w[k++] = v;
+        }
+        if constexpr (F::kScaleBytes != 0) {
+            uint32_t v = 0u;
+            if (ok) v = reinterpret_cast<const uint32_t*>(scales + row * scale_row_bytes + kc * 16)[t];
+            w[k++] = v;
+        }
+    }
+    if constexpr (FMT == SPARK_FMT_SPFP2) {
+        // swap codes (1,2) and (5,6) of every 16-bit mantissa word so the
+        // decoders emit registers in natural column order
+        uint8_t* b = reinterpret_cast<uint8_t*>(w);
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+            for (int pr = 0; pr < 4; ++pr)
+#pragma unroll
+                for (int mw = 0; mw < 2; ++mw) {
+                    uint8_t* q = b + half * 20 + pr * 5 + mw * 2;
+                    const uint32_t m = (uint32_t)q[0] | ((uint32_t)q[1] << 8);
+                    const uint32_t mp = (m & 0xc3c3u) | ((m & 0x0c0cu) << 2) | ((m & 0x3030u) >> 2);
+                    q[0] = (uint8_t)mp;
+                    q[1] = (uint8_t)(mp >> 8);
+                }
+    }
+    uint8_t* dst = tiled + u * unit_bytes_tiled<FMT>();
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+        reinterpret_cast<uint4*>(dst)[v * 32 + lane] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+    reinterpret_cast<uint2*>(dst + NV * 512)[lane] = make_uint2(w[4 * NV], w[4 * NV + 1]);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// GEMV over tiled weights.  Every thread copies its own fragment vectors of
+// the next kDepthT units into a private shared-memory ring (cp.async), so no
+// synchronisation beyond the thread's own wait_group is needed.
+constexpr int kDepthT = 4;
+
+// acquire-release counter bump: the partials written before it are visible to
+// whoever observes the count, and the last arriver sees everybody's partials
+__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// BF: bf16 MMA with the caller's bf16 x read directly (SPFP2 and 2:4, whose
+// weights are exact in bf16); otherwise fp16 MMA on the prepared x.
+template <int FMT, int NT, int XS, bool BF>
+__global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a) {
+    using F = Fmt<FMT>;
+    constexpr int FW = frag_words<FMT>();
+    constexpr int NV = FW / 4;
+    constexpr int UB = unit_bytes_tiled<FMT>();
+    static_assert(!BF || FMT == SPARK_FMT_SPFP2 || FMT == SPARK_FMT_TWOFOUR, "bf16 path: SPFP2 / 2:4 only");
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint2 lut[16];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    // ring slot (stage, vector) of this thread: 16 bytes each
+    uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * kDepthT * (NV + 1) * 32 + lane;
+
+    const int T = (int)gridDim.x * kWarps;
+    const int gw = (int)blockIdx.x * kWarps + warp;
+    const int U = (int)a.units, nkc = (int)a.n_kc;
+    const int u0 = (int)((int64_t)U * gw / T), u1 = (int)((int64_t)U * (gw + 1) / T);
+    const int n = u1 - u0;
+
+    auto issue = [&](int u, int st) {
+        if (u < u1) {
+            const uint8_t* src = a.wq + (int64_t)u * UB;
+            uint4* dst = ring + st * (NV + 1) * 32;
+#pragma unroll
+            for (int v = 0; v < NV; ++v) cp_async16(smem_addr(dst + v * 32), src + (v * 32 + lane) * 16);
+            cp_async8(smem_addr(dst + NV * 32), src + NV * 512 + lane * 8);
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int i = 0; i < kDepthT; ++i) issue(u0 + i, i);
+    if constexpr (BF && FMT == SPARK_FMT_SPFP2) {
+        if (threadIdx.x < 16) {
+            const uint32_t E = 117u + threadIdx.x;
+            const uint32_t H = E >> 1, L = (E & 1u) << 7;
+            lut[threadIdx.x] = make_uint2(H * 0x101u + 0x8000u, L * 0x101u);
+        }
+        __syncthreads();
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nt][i] = 0.0f;
+
+    const __half* xrow0 = a.xp + (int64_t)g * a.ic + t * (F::kCols / 4);
+    const __half* xrow1 = a.xp + (int64_t)(g + 8) * a.ic + t * (F::kCols / 4);
+    const uint16_t* xb0 = static_cast<const uint16_t*>(a.x_raw) + (int64_t)g * a.ldx + t * (F::kCols / 4);
+    const uint16_t* xb1 = static_cast<const uint16_t*>(a.x_raw) + (int64_t)(g + 8) * a.ldx + t * (F::kCols / 4);
+    const bool tok0 = g < a.M, tok1 = (g + 8) < a.M;
+    const int rg_first = u0 / nkc;
+    const float* sig = BF ? nullptr : a.sigma;
+
+    auto flush = [&](int rg, int seg0, int seg1) {
+        if (seg0 == rg * nkc && seg1 == (rg + 1) * nkc) {
+            write_rows<NT>(a, rg, acc, lane, sig);
+            return;
+        }
+        const int slot = (rg == rg_first) ? 0 : 1;
+        float* mine = a.partials + (((int64_t)gw * 2 + slot) * NT * 32 + lane) * 4;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            __stcg(reinterpret_cast<float4*>(mine + nt * 128), make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
+        __syncwarp();
+        const int64_t first = (int64_t)rg * nkc, last = (int64_t)(rg + 1) * nkc - 1;
+        const int w_lo = (int)(((first + 1) * T - 1) / U), w_hi = (int)(((last + 1) * T - 1) / U);
+        int old = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            old = atomic_add_acq_rel(a.counters + rg, 1);
+        }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old != w_hi - w_lo) return;
+        float sum[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sum[nt][i] = 0.0f;
+        for (int w = w_lo; w <= w_hi; ++w) {
+            const int ws = (int)((int64_t)U * w / T);
+            const int sl = (ws / nkc == rg) ? 0 : 1;
+            const float* src = a.partials + (((int64_t)w * 2 + sl) * NT * 32 + lane) * 4;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                float4 v = __ldcg(reinterpret_cast<const float4*>(src + nt * 128));
+                sum[nt][0] += v.x; sum[nt][1] += v.y; sum[nt][2] += v.z; sum[nt][3] += v.w;
+            }
+        }
+        write_rows<NT>(a, rg, sum, lane, sig);
+        if (lane == 0) a.counters[rg] = 0;
+    };
+
+    int crg = rg_first, ckc = u0 - rg_first * nkc;
+    int seg0 = u0;
+    for (int i = 0; i < n; ++i) {
+        const int st = i % kDepthT;
+        cp_async_wait<kDepthT - 1>();
+        uint32_t fw[FW];
+        const uint4* slot = ring + st * (NV + 1) * 32;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const uint4 q = slot[v * 32];
+            fw[4 * v] = q.x; fw[4 * v + 1] = q.y; fw[4 * v + 2] = q.z; fw[4 * v + 3] = q.w;
+        }
+        {
+            const uint2 q = *reinterpret_cast<const uint2*>(slot + NV * 32);
+            fw[4 * NV] = q.x; fw[4 * NV + 1] = q.y;
+        }
+        // the slot is reused by the copy issued next: consume the words first
+#pragma unroll
+        for (int k = 0; k < FW; ++k) asm volatile("" ::"r"(fw[k]));
+        issue(u0 + i + kDepthT, st);
+
+        const uint32_t* c0 = fw;
+        const uint32_t* c1 = fw + FW / 2;
+        uint32_t sw0 = 0, sw1 = 0;
+        if constexpr (F::kScaleBytes != 0) { sw0 = fw[F::kChunkWords]; sw1 = fw[FW / 2 + F::kChunkWords]; }
+        const int64_t col0 = (int64_t)ckc * F::kCols;
+#pragma unroll
+        for (int s = 0; s < F::kSteps; ++s) {
+            uint32_t A0[4], A1[4];
+            if constexpr (BF) {
+                if constexpr (FMT == SPARK_FMT_SPFP2) {
+                    decode_spfp2_bf16(c0, s, lut, A0);
+                    decode_spfp2_bf16(c1, s, lut, A1);
+                } else {
+                    decode_twofour_t<true>(c0, s, A0);
+                    decode_twofour_t<true>(c1, s, A1);
+                }
+                uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
+                if (tok0) x0 = ldg_nc_v4(xb0 + col0 + 8 * s);
+                if (NT > 1 && tok1) x1 = ldg_nc_v4(xb1 + col0 + 8 * s);
+                mma_16816_bf16(acc[0], A0[0], A1[0], A0[1], A1[1], x0.x, x0.y);
+                mma_16816_bf16(acc[0], A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
+                if (NT > 1) {
+                    mma_16816_bf16(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
+                    mma_16816_bf16(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
+                }
+            } else {
+                decode_step<FMT>(c0, sw0, s, A0);
+                decode_step<FMT>(c1, sw1, s, A1);
+#pragma unroll
+                for (int part = 0; part < XS; ++part) {
+                    const int64_t po = (int64_t)part * kMaxTokens * a.ic + col0 + 8 * s;
+                    uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
+                    if (tok0) x0 = ldg_nc_v4(xrow0 + po);
+                    if (NT > 1 && tok1) x1 = ldg_nc_v4(xrow1 + po);
+                    mma_16816(acc[0], A0[0], A1[0], A0[1], A1[1], x0.x, x0.y);
+                    mma_16816(acc[0], A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
+                    if (NT > 1) {
+                        mma_16816(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
+                        mma_16816(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
+                    }
+                }
+            }
+        }
+        const int u = u0 + i;
+        if (++ckc == nkc || i + 1 == n) {
+            flush(crg, seg0, u + 1);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[nt][q] = 0.0f;
+            if (ckc == nkc) { ckc = 0; ++crg; }
+            seg0 = u + 1;
+        }
+    }
+    cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------- generic path
@@ -696,6 +1096,81 @@ int launch_fmt(const GemvArgs& a, int NT, int XS, int64_t T, cudaStream_t s) {
     return NT == 1 ? launch_gemv<FMT, 1, 2>(a, T, s) : launch_gemv<FMT, 2, 2>(a, T, s);
 }
 
+template <int FMT>
+size_t gemv_tiled_smem() {
+    return (size_t)kWarps * kDepthT * (frag_words<FMT>() / 4 + 1) * 32 * 16;
+}
+
+template <int FMT, int NT, int XS, bool BF>
+int launch_gemv_tiled(const GemvArgs& a, int64_t T, cudaStream_t stream) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t smem = gemv_tiled_smem<FMT>();
+    {
+        static bool done[64] = {};
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!done[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(k_gemv_tiled<FMT, NT, XS, BF>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return set_error((int)e, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+            done[dev] = true;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(T / kWarps));
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_tiled<FMT, NT, XS, BF>, a);
+    if (e != cudaSuccess) return set_error((int)e, "k_gemv_tiled launch: %s", cudaGetErrorString(e));
+    return SPARK_OK;
+}
+
+template <int FMT>
+int launch_fmt_tiled(const GemvArgs& a, int NT, int XS, bool bf, int64_t T, cudaStream_t s) {
+    if constexpr (FMT == SPARK_FMT_SPFP2 || FMT == SPARK_FMT_TWOFOUR) {
+        if (bf) return NT == 1 ? launch_gemv_tiled<FMT, 1, 1, true>(a, T, s) : launch_gemv_tiled<FMT, 2, 1, true>(a, T, s);
+    }
+    if (XS == 1) return NT == 1 ? launch_gemv_tiled<FMT, 1, 1, false>(a, T, s) : launch_gemv_tiled<FMT, 2, 1, false>(a, T, s);
+    return NT == 1 ? launch_gemv_tiled<FMT, 1, 2, false>(a, T, s) : launch_gemv_tiled<FMT, 2, 2, false>(a, T, s);
+}
+
+int launch_prepare(const void* x, int x_dtype, int64_t ldx, int64_t ic, int fmt, __half* xp, float* sigma, int split,
+                   int mc, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)mc);
+    cfg.blockDim = dim3(kPrepThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_prepare_x, x, x_dtype, ldx, ic, fmt, xp, sigma, split);
+    if (e != cudaSuccess) return set_error((int)e, "k_prepare_x launch: %s", cudaGetErrorString(e));
+    return SPARK_OK;
+}
+
+int64_t tiled_bytes(int fmt, int64_t oc, int64_t ic) {
+    if (fmt != SPARK_FMT_SPFP2 && fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4 && fmt != SPARK_FMT_TWOFOUR) return 0;
+    if (oc <= 0 || ic <= 0 || ic % cols_per_unit(fmt) != 0) return 0;
+    const int64_t units = (oc + 15) / 16 * (ic / cols_per_unit(fmt));
+    if (units < kWarps) return 0;
+    int ub = 0;
+    switch (fmt) {
+        case SPARK_FMT_SPFP2: ub = unit_bytes_tiled<SPARK_FMT_SPFP2>(); break;
+        case SPARK_FMT_FP3: ub = unit_bytes_tiled<SPARK_FMT_FP3>(); break;
+        case SPARK_FMT_NVFP4: ub = unit_bytes_tiled<SPARK_FMT_NVFP4>(); break;
+        default: ub = unit_bytes_tiled<SPARK_FMT_TWOFOUR>(); break;
+    }
+    return units * ub;
+}
+
 bool fast_path_ok(int fmt, const uint8_t* wq, const uint8_t* scales, int64_t oc, int64_t ic) {
     if (fmt == SPARK_FMT_SPFP2_V1) return false;
     if (ic % cols_per_unit(fmt) != 0) return false;
@@ -725,18 +1200,24 @@ size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int64_t ic) {
 int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
                  int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype,
                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+    const bool tiled = (fmt & SPARK_LAYOUT_TILED) != 0;
+    fmt &= ~SPARK_LAYOUT_TILED;
     SPARK_REQUIRE(fmt >= SPARK_FMT_SPFP2 && fmt <= SPARK_FMT_TWOFOUR, SPARK_ERR_INVALID, "spark_linear: bad format %d", fmt);
+    SPARK_REQUIRE(!tiled || tiled_bytes(fmt, oc, ic) > 0, SPARK_ERR_INVALID,
+                  "spark_linear: no tiled layout for format %d [%lld, %lld]", fmt, (long long)oc, (long long)ic);
     SPARK_REQUIRE(wq && x && y, SPARK_ERR_INVALID, "spark_linear: null pointer");
     SPARK_REQUIRE(M >= 0 && oc >= 0 && ic >= 0, SPARK_ERR_INVALID, "spark_linear: negative size");
     SPARK_REQUIRE(ldx >= ic && ldy >= oc, SPARK_ERR_INVALID, "spark_linear: ldx %lld < ic or ldy %lld < oc",
                   (long long)ldx, (long long)ldy);
-    SPARK_REQUIRE((fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4) || scales, SPARK_ERR_INVALID,
+    SPARK_REQUIRE(tiled || (fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4) || scales, SPARK_ERR_INVALID,
                   "spark_linear: FP3/NVFP4 need scales");
     SPARK_REQUIRE(x_dtype >= 0 && x_dtype <= 2 && y_dtype >= 0 && y_dtype <= 2 && bias_dtype >= 0 && bias_dtype <= 2,
                   SPARK_ERR_INVALID, "spark_linear: bad dtype");
     if (M == 0 || oc == 0) return SPARK_OK;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (!fast_path_ok(fmt, wq, scales, oc, ic)) {
+    if (tiled) {
+        SPARK_REQUIRE(aligned(wq, 16), SPARK_ERR_ALIGNMENT, "spark_linear: tiled weights must be 16-byte aligned");
+    } else if (!fast_path_ok(fmt, wq, scales, oc, ic)) {
         k_linear_generic<<<(unsigned)((oc + 7) / 8), 256, 0, s>>>(fmt, wq, scales, x, x_dtype, M, oc, ic, ldx, bias,
                                                                   bias_dtype, y, y_dtype, ldy);
         return check_launch("spark_linear (generic)");
@@ -753,6 +1234,7 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const int64_t units = (oc + 15) / 16 * (ic / cols_per_unit(fmt));
+    SPARK_REQUIRE(units < (1ll << 30), SPARK_ERR_UNSUPPORTED, "spark_linear: layer too large for one launch");
     int64_t T = std::min(Tmax, units) / kWarps * kWarps;
     GemvArgs a = {};
     a.wq = wq;
@@ -783,13 +1265,29 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
         const int mc = (int)std::min<int64_t>(kMaxTokens, M - m0);
         const uint8_t* xb = static_cast<const uint8_t*>(x) + m0 * ldx * (x_dtype == SPARK_DTYPE_F32 ? 4 : 2);
         const int XS = x_dtype == SPARK_DTYPE_BF16 ? 1 : 2;
-        k_prepare_x<<<mc, 256, 0, s>>>(xb, x_dtype, ldx, ic, fmt, reinterpret_cast<__half*>(ws + L.xp),
-                                       reinterpret_cast<float*>(ws + L.sigma), XS == 2);
-        int rc = check_launch("spark_linear (prepare)");
+        // SPFP2 / 2:4 on tiled weights with bf16 x: bf16 MMA straight on x, no prepare
+        const bool bf = tiled && x_dtype == SPARK_DTYPE_BF16 &&
+                        (fmt == SPARK_FMT_SPFP2 || fmt == SPARK_FMT_TWOFOUR) && (ldx % 8) == 0 && aligned(x, 16);
+        a.x_raw = xb;
+        a.ldx = ldx;
+        const int perm = fmt == SPARK_FMT_FP3 ? kPermFp3 : (fmt == SPARK_FMT_SPFP2 && !tiled ? kPermSpfp2 : kPermNatural);
+        int rc = SPARK_OK;
+        if (!bf) rc = launch_prepare(xb, x_dtype, ldx, ic, perm, reinterpret_cast<__half*>(ws + L.xp),
+                                reinterpret_cast<float*>(ws + L.sigma), XS == 2, mc, s);
         if (rc) return rc;
         a.M = mc;
         a.y = static_cast<uint8_t*>(y) + m0 * ldy * (y_dtype == SPARK_DTYPE_F32 ? 4 : 2);
         const int NT = mc > 8 ? 2 : 1;
+        if (tiled) {
+            switch (fmt) {
+                case SPARK_FMT_SPFP2: rc = launch_fmt_tiled<SPARK_FMT_SPFP2>(a, NT, XS, bf, T, s); break;
+                case SPARK_FMT_FP3: rc = launch_fmt_tiled<SPARK_FMT_FP3>(a, NT, XS, bf, T, s); break;
+                case SPARK_FMT_NVFP4: rc = launch_fmt_tiled<SPARK_FMT_NVFP4>(a, NT, XS, bf, T, s); break;
+                default: rc = launch_fmt_tiled<SPARK_FMT_TWOFOUR>(a, NT, XS, bf, T, s); break;
+            }
+            if (rc) return rc;
+            continue;
+        }
         switch (fmt) {
             case SPARK_FMT_SPFP2: rc = launch_fmt<SPARK_FMT_SPFP2>(a, NT, XS, T, s); break;
             case SPARK_FMT_FP3: rc = launch_fmt<SPARK_FMT_FP3>(a, NT, XS, T, s); break;
@@ -799,6 +1297,43 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
         if (rc) return rc;
     }
     return SPARK_OK;
+}
+
+size_t spark_tiled_bytes(int fmt, int64_t oc, int64_t ic) { return (size_t)tiled_bytes(fmt, oc, ic); }
+
+int spark_tile_weights(int fmt, const uint8_t* wq, const uint8_t* scales, int64_t oc, int64_t ic, uint8_t* tiled,
+                       void* stream) {
+    SPARK_REQUIRE(wq && tiled, SPARK_ERR_INVALID, "spark_tile_weights: null pointer");
+    SPARK_REQUIRE(tiled_bytes(fmt, oc, ic) > 0, SPARK_ERR_UNSUPPORTED,
+                  "spark_tile_weights: format %d [%lld, %lld] has no tiled layout (ic %% %d != 0 or too small)", fmt,
+                  (long long)oc, (long long)ic, fmt == SPARK_FMT_TWOFOUR ? 512 : 256);
+    SPARK_REQUIRE((fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4) || scales, SPARK_ERR_INVALID,
+                  "spark_tile_weights: FP3/NVFP4 need scales");
+    SPARK_REQUIRE(aligned(wq, 16) && aligned(tiled, 16) && (!scales || aligned(scales, 4)), SPARK_ERR_ALIGNMENT,
+                  "spark_tile_weights: buffers must be 16-byte aligned");
+    const int64_t n_kc = ic / cols_per_unit(fmt);
+    const int64_t units = (oc + 15) / 16 * n_kc;
+    const unsigned grid = (unsigned)((units * 32 + 255) / 256);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (fmt) {
+        case SPARK_FMT_SPFP2:
+            k_tile<SPARK_FMT_SPFP2><<<grid, 256, 0, s>>>(wq, scales, oc, Fmt<SPARK_FMT_SPFP2>::row_bytes(ic), ic / 16,
+                                                          n_kc, units, tiled);
+            break;
+        case SPARK_FMT_FP3:
+            k_tile<SPARK_FMT_FP3><<<grid, 256, 0, s>>>(wq, scales, oc, Fmt<SPARK_FMT_FP3>::row_bytes(ic), ic / 16, n_kc,
+                                                        units, tiled);
+            break;
+        case SPARK_FMT_NVFP4:
+            k_tile<SPARK_FMT_NVFP4><<<grid, 256, 0, s>>>(wq, scales, oc, Fmt<SPARK_FMT_NVFP4>::row_bytes(ic), ic / 16,
+                                                          n_kc, units, tiled);
+            break;
+        default:
+            k_tile<SPARK_FMT_TWOFOUR><<<grid, 256, 0, s>>>(wq, scales, oc, Fmt<SPARK_FMT_TWOFOUR>::row_bytes(ic),
+                                                            ic / 16, n_kc, units, tiled);
+            break;
+    }
+    return check_launch("spark_tile_weights");
 }
 
 int spark_workspace_check(void* workspace, void* stream) {

@@ -41,6 +41,11 @@ class V3PackedLinear(nn.Module):
         self.register_buffer("w_packed", packed)
         self.register_buffer("w_scales", scales.view(torch.uint8) if scales is not None else None)
         self.register_buffer("bias", bias)
+        # fragment-major copy for the decode GEMV when the shape allows it; the
+        # reference-layout bytes are kept for export and for the other paths
+        self.register_buffer("w_tiled", ops.tile_weights(fmt, packed, scales, out_features, in_features)
+                             if packed.is_cuda and fmt in ("spfp2", "fp3", "nvfp4", "twofour") else None,
+                             persistent=False)
 
     @classmethod
     def from_packed(cls, fmt, packed, scales, out_features, in_features, bias=None):
@@ -63,6 +68,9 @@ class V3PackedLinear(nn.Module):
             pad = (ic + 7) // 8 * 8
             x = torch.nn.functional.pad(x, (0, pad - ic))
             ic = pad
+        if self.w_tiled is not None and ic == self.in_features:
+            return ops.linear(self.fmt, self.w_tiled, None, x, self.out_features, ic, bias=self.bias,
+                              out_dtype=x.dtype, tiled=True)
         return ops.linear(self.fmt, self.w_packed, self.w_scales, x, self.out_features, ic,
                           bias=self.bias, out_dtype=x.dtype)
 

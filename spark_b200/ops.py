@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 from ._lib import (DTYPE_BF16, DTYPE_F16, DTYPE_F32, FMT_FP3, FMT_NVFP4, FMT_SPFP2, FMT_SPFP2_V1,
-                   FMT_TWOFOUR, call)
+                   FMT_TWOFOUR, LAYOUT_TILED, call)
 
 _DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
 
@@ -210,10 +210,33 @@ def workspace_size(fmt: int, M: int, oc: int, ic: int) -> int:
     return int(_lib.lib().spark_linear_workspace_size(fmt, M, oc, ic))
 
 
-def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bias=None, out_dtype=None,
-           out: torch.Tensor | None = None) -> torch.Tensor:
-    """y[..., oc] = x[..., ic] . decode(W)^T (+ bias) with W packed in `fmt`."""
+def tiled_bytes(fmt, oc: int, ic: int) -> int:
     f = FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+    return int(_lib.lib().spark_tiled_bytes(f, oc, ic))
+
+
+def tile_weights(fmt, wq: torch.Tensor, scales, oc: int, ic: int) -> torch.Tensor | None:
+    """Fragment-major copy of a packed weight for the decode GEMV (None when the
+    shape has no tiled layout).  Same bytes, permuted; scales embedded."""
+    f = FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+    n = tiled_bytes(f, oc, ic)
+    if n == 0:
+        return None
+    w = _bytes(wq)
+    s = _bytes(scales) if scales is not None else None
+    out = torch.empty(n, dtype=torch.uint8, device=w.device)
+    call("spark_tile_weights", f, _p(w), _p(s), oc, ic, _p(out), _stream(w))
+    return out
+
+
+def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bias=None, out_dtype=None,
+           out: torch.Tensor | None = None, tiled: bool = False) -> torch.Tensor:
+    """y[..., oc] = x[..., ic] . decode(W)^T (+ bias) with W packed in `fmt`
+    (reference layout, or the tile_weights copy with tiled=True)."""
+    f = FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+    if tiled:
+        f |= LAYOUT_TILED
+        scales = None
     if not x.is_cuda:
         raise RuntimeError("spark_b200.linear: x must be a CUDA tensor")
     lead = x.shape[:-1]
@@ -227,7 +250,7 @@ def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bia
     s = _bytes(scales) if scales is not None else None
     b = bias.contiguous() if bias is not None else None
     y = out if out is not None else torch.empty(M, oc, dtype=out_dtype or x.dtype, device=x.device)
-    nbytes = workspace_size(f, M, oc, ic)
+    nbytes = workspace_size(f & ~LAYOUT_TILED, M, oc, ic)
     ws = workspace(x.device, nbytes)
     call("spark_linear", f, _p(w), _p(s), _p(x2), _dt(x2), M, oc, ic, x2.stride(0), _p(b),
          _dt(b) if b is not None else DTYPE_F32, _p(y), _dt(y), y.stride(0), _p(ws), ws.numel(), _stream(x))

@@ -48,12 +48,16 @@ def make(fmt, oc, ic, seed, std=0.02):
     raise ValueError(fmt)
 
 
-def check(fmt, oc, ic, M, seed=0, bias=False, out_dtype=torch.float32, x_dtype=torch.bfloat16):
+def check(fmt, oc, ic, M, seed=0, bias=False, out_dtype=torch.float32, x_dtype=torch.bfloat16, tiled=False):
     wq, s, dec = make(fmt, oc, ic, seed)
+    if tiled:
+        wq, s = ops().tile_weights(fmt, wq, s, oc, ic), None
+        assert wq is not None
     g = torch.Generator().manual_seed(seed + 1)
     x = torch.randn(M, ic, generator=g).to(x_dtype)
     b = (torch.randn(oc, generator=g) * 0.1) if bias else None
-    y = ops().linear(fmt, wq, s, x.cuda(), oc, ic, bias=b.cuda() if b is not None else None, out_dtype=out_dtype)
+    y = ops().linear(fmt, wq, s, x.cuda(), oc, ic, bias=b.cuda() if b is not None else None, out_dtype=out_dtype,
+                     tiled=tiled)
     torch.cuda.synchronize()
     y64 = O.linear_f64(x.float().numpy(), dec, b.numpy() if b is not None else None)
     err = np.abs(y.float().cpu().numpy().astype(np.float64) - y64)
@@ -72,6 +76,19 @@ FAST = [("spfp2", 9728, 2560), ("spfp2", 2560, 9728), ("fp3", 4096, 2560), ("nvf
 @pytest.mark.parametrize("M", [1, 4, 16])
 def test_linear_fast_path(fmt, oc, ic, M):
     check(fmt, oc, ic, M)
+
+
+@pytest.mark.parametrize("fmt,oc,ic", FAST)
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_linear_tiled(fmt, oc, ic, M):
+    check(fmt, oc, ic, M, tiled=True)
+
+
+@pytest.mark.parametrize("fmt", ["spfp2", "fp3", "nvfp4", "twofour"])
+def test_linear_tiled_chunks_bias_dtypes(fmt):
+    check(fmt, 1024, 1024, 17, bias=True, tiled=True)
+    check(fmt, 1024, 1024, 3, seed=4, x_dtype=torch.float32, bias=True, tiled=True)
+    check(fmt, 1000, 1024, 5, seed=6, x_dtype=torch.float16, out_dtype=torch.float16, tiled=True)
 
 
 @pytest.mark.parametrize("fmt", ["spfp2", "fp3", "nvfp4", "twofour"])
