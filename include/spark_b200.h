@@ -131,6 +131,27 @@ SPARK_API int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, co
                  int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype,
                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
+/* spark_linear without a workspace argument, for callers that may not allocate
+ * device memory when they run a linear (a runtime whose memory plan is fixed
+ * before the first token, a C host with no device allocator).  No counterpart in
+ * the reference.  Same arguments, formats and results as spark_linear; it
+ * allocates nothing.  Its scratch is one static 8 MiB array per device inside
+ * the library, so ic is limited to what fits (spark_linear_workspace_size(fmt,
+ * M, oc, ic) <= 8 MiB: ic <= 51,192 on a 148-SM GPU); a larger ic returns
+ * SPARK_ERR_WORKSPACE.
+ *   - The first call on a device (with that device current) looks the scratch
+ *     up, clears it and synchronises `stream`; make it before any stream capture
+ *     (during a capture it returns SPARK_ERR_INVALID).
+ *   - All calls on one device share the scratch: calls that overlap on the GPU
+ *     (other streams, other threads) race, and the scratch keeps the last call's
+ *     contents.  Order them on one stream.
+ *   - Device-side wait expiries are recorded in the shared scratch's error word,
+ *     which no entry point reads; callers that need that report use spark_linear
+ *     with their own workspace and spark_workspace_check. */
+SPARK_API int spark_linear_noalloc(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype,
+                                   int64_t M, int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype,
+                                   void* y, int y_dtype, int64_t ldy, void* stream);
+
 /* Fragment-major copy of a packed weight for spark_linear(fmt | SPARK_LAYOUT_TILED):
  * the same bytes (codes and, for FP3/NVFP4, scales) permuted so every thread of the
  * decode GEMV reads its MMA fragments with coalesced 16-byte loads.  No counterpart

@@ -1351,3 +1351,77 @@ int spark_workspace_check(void* workspace, void* stream) {
 }
 
 }  // extern "C"
+
+// ====================================================================== no-allocation entry point
+// Some callers may not allocate device memory when they run a linear: an
+// inference runtime whose memory plan is fixed before the first token, a host
+// that hands its whole budget to a caching allocator it cannot re-enter from
+// the decode loop, or a C caller with no allocator at all.  The stream-K GEMV
+// still needs scratch (error word, row-group counters, split partials,
+// per-token scales and prepared activations).  spark_linear_noalloc takes
+// that scratch from one statically sized array in this module (one copy per
+// device) instead of a caller-provided workspace, and allocates nothing.
+namespace spark {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of this device's scratch.  The first call on a device looks
+// the symbol up with that device current and clears the part whose contents
+// must start at zero: the error word and the row-group counters (the kernels
+// return the counters to zero themselves; everything after them is written
+// before it is read).  The clear is synchronised so that later calls on any
+// stream see it.
+int noalloc_scratch(int dev, cudaStream_t s, void** out) {
+    SPARK_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, SPARK_ERR_UNSUPPORTED,
+                  "spark_linear_noalloc: device ordinal %d above %d", dev, kNoAllocMaxDevices - 1);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaError_t e = cudaStreamIsCapturing(s, &cs);
+        if (e != cudaSuccess) return set_error((int)e, "spark_linear_noalloc: %s", cudaGetErrorString(e));
+        SPARK_REQUIRE(cs == cudaStreamCaptureStatusNone, SPARK_ERR_INVALID,
+                      "spark_linear_noalloc: the first call on device %d sets up its scratch and must come before "
+                      "any stream capture",
+                      dev);
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(e != cudaSuccess ? (int)e : SPARK_ERR_DEVICE, "spark_linear_noalloc: scratch lookup: %s",
+                             cudaGetErrorString(e));
+        e = cudaMemsetAsync(p, 0, ws_layout(0, 0).partials, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return set_error((int)e, "spark_linear_noalloc: scratch clear: %s", cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return SPARK_OK;
+}
+
+}  // namespace
+}  // namespace spark
+
+extern "C" int spark_linear_noalloc(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype,
+                                    int64_t M, int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype,
+                                    void* y, int y_dtype, int64_t ldy, void* stream) {
+    SPARK_REQUIRE(ic >= 0, SPARK_ERR_INVALID, "spark_linear_noalloc: negative size");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error((int)e, "spark_linear_noalloc: %s", cudaGetErrorString(e));
+    const size_t need = ws_layout(ic, max_warps(dev)).total;
+    SPARK_REQUIRE(need <= kNoAllocScratchBytes, SPARK_ERR_WORKSPACE,
+                  "spark_linear_noalloc: ic = %lld needs %zu bytes of scratch, above the static %zu bytes "
+                  "(use spark_linear with a caller-provided workspace)",
+                  (long long)ic, need, kNoAllocScratchBytes);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(dev, s, &scratch);
+    if (rc) return rc;
+    return spark_linear(fmt, wq, scales, x, x_dtype, M, oc, ic, ldx, bias, bias_dtype, y, y_dtype, ldy, scratch,
+                        kNoAllocScratchBytes, stream);
+}
