@@ -400,7 +400,12 @@ def run_reference(args, rank, world):
 
 
 def run_profile(args):
-    """A few plain launches of one linear (for ncu captures; prints timing only)."""
+    """Timing of one linear shape on its own (also the target of ncu captures).
+
+    Weight copies rotate so their total exceeds L2 (126 MB) unless --copies is
+    given; one pass over the copies is captured as a CUDA graph and replayed
+    --steps times.  Prints per-call time, weight GB/s and, for M >= 64,
+    TFLOP/s (2*M*oc*ic per call)."""
     from spark_b200 import ops
     torch.cuda.set_device(0)
     device = torch.device("cuda", 0)
@@ -408,34 +413,58 @@ def run_profile(args):
     oc, ic = shapes[args.profile]
     oc = args.oc or oc
     ic = args.ic or ic
+    nbytes = weight_bytes(args.profile, oc, ic) if args.profile != "twofour" else oc * ic // 32 * 7
+    copies = args.copies or max(1, min(64, -(-300_000_000 // nbytes)))
     g = torch.Generator(device=device).manual_seed(3)
-    W = torch.randn(oc, ic, device=device, generator=g) * 0.02
-    s = None
-    if args.profile == "spfp2":
-        wq, _ = ops.spfp2_pack(W)
-    elif args.profile == "fp3":
-        wq, s = ops.fp3_pack(W)
-    elif args.profile == "nvfp4":
-        wq, s = ops.nvfp4_pack(W)
-    else:
-        wq = ops.twofour_pack(W)
+    ws = []
+    for _ in range(copies):
+        W = torch.randn(oc, ic, device=device, generator=g) * 0.02
+        s = None
+        if args.profile == "spfp2":
+            wq, _ = ops.spfp2_pack(W)
+        elif args.profile == "fp3":
+            wq, s = ops.fp3_pack(W)
+        elif args.profile == "nvfp4":
+            wq, s = ops.nvfp4_pack(W)
+        else:
+            wq = ops.twofour_pack(W)
+        if args.path == "tiled":
+            wq, s = ops.tile_weights(args.profile, wq, s, oc, ic), None
+        ws.append((wq, s))
+        del W
     x = torch.randn(args.M, ic, device=device, generator=g).bfloat16()
-    wt = ops.tile_weights(args.profile, wq, s, oc, ic)
-    y = None
-    for _ in range(2):
-        y = ops.linear(args.profile, wt, None, x, oc, ic, out=y, tiled=True)
+    ys = [torch.empty(args.M, oc, device=device, dtype=torch.bfloat16) for _ in range(copies)]
+    stream = torch.cuda.Stream(device)
+
+    def one_pass():
+        for (wq, s), y in zip(ws, ys):
+            ops.linear(args.profile, wq, s, x, oc, ic, out=y, tiled=args.path == "tiled", tcgen05=args.path == "tc")
+
+    with torch.cuda.stream(stream):
+        one_pass()
+        one_pass()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        one_pass()
+    for _ in range(3):
+        graph.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        y = ops.linear(args.profile, wt, None, x, oc, ic, out=y, tiled=True)
-    e1.record()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
     torch.cuda.synchronize()
     ops.check_device_errors()
-    us = e0.elapsed_time(e1) * 1e3 / args.steps
-    nbytes = weight_bytes(args.profile, oc, ic) if args.profile != "twofour" else oc * ic // 32 * 7
-    print(json.dumps({"profile": args.profile, "M": args.M, "oc": oc, "ic": ic, "launches": args.steps,
-                      "us_per_call": round(us, 2), "weight_GBps": round(nbytes / us / 1e3, 1)}))
+    calls = args.steps * copies
+    us = e0.elapsed_time(e1) * 1e3 / calls
+    out = {"profile": args.profile, "path": args.path, "M": args.M, "oc": oc, "ic": ic, "copies": copies,
+           "calls": calls, "us_per_call": round(us, 3), "weight_GBps": round(nbytes / us / 1e3, 1)}
+    if args.M >= 64:
+        out["TFLOPs"] = round(2.0 * args.M * oc * ic / us / 1e6, 1)
+    print(json.dumps(out))
 
 
 def main():
@@ -449,6 +478,9 @@ def main():
     ap.add_argument("--profile", choices=["spfp2", "fp3", "nvfp4", "twofour"],
                     help="run a few plain launches of one linear (ncu captures)")
     ap.add_argument("--M", type=int, default=1)
+    ap.add_argument("--path", default="tiled", choices=["tiled", "tc", "plain"],
+                    help="profile mode: tiled-layout GEMV, tcgen05 kernel, or reference-layout GEMV")
+    ap.add_argument("--copies", type=int, default=0, help="profile mode: weight copies to rotate over")
     ap.add_argument("--oc", type=int, default=0, help="profile mode: output features")
     ap.add_argument("--ic", type=int, default=0, help="profile mode: input features")
     args = ap.parse_args()

@@ -53,6 +53,10 @@ extern "C" {
 /* OR'ed into a format: the weight buffer holds the fragment-major ("tiled")
  * copy made by spark_tile_weights (scales embedded) instead of the reference layout */
 #define SPARK_LAYOUT_TILED 0x100
+/* spark_linear flag: run the tcgen05 kernel (SPFP2 reference layout, bf16 x,
+ * ic a multiple of 256, 16-byte aligned weights and x, ldx a multiple of 8);
+ * SPARK_ERR_UNSUPPORTED when the call does not meet those conditions. */
+#define SPARK_PATH_TCGEN05 0x200
 
 SPARK_API const char* spark_last_error(void);
 SPARK_API int spark_version(void);

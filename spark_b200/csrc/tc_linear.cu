@@ -1,0 +1,674 @@
+// tc_linear.cu -- SPFP2 online-dequant linear on the 5th-generation tensor cores.
+//
+// y[M, oc] = x[M, ic] . decode(W)^T, W in the reference's paired SPFP2 layout
+// (block_fp2_emu.py:231-267: per 16 weights, mantissa words m0, m1 as u16 LE
+// then one byte e0 | e1 << 4), read in place: no load-time re-layout.
+//
+// Work unit: 128 weight rows x 256 columns (one TMA box of 128 x 80 bytes),
+// for one tile of N tokens; a job is all units of one (token tile, row
+// block).  One CTA per SM.  Decode (M <= 16, N = 16) splits the units of all
+// jobs evenly over the CTAs (stream-K): a CTA whose unit range starts or ends
+// inside a job publishes a partial sum and, per 32-row slice, the last
+// contributor adds them in CTA order, so the result does not depend on
+// timing.  Prefill (N = 64, 128 or 256) hands whole jobs to the CTAs in turn.
+//
+// Roles inside a CTA (320 threads):
+//   warps 0-7  decode: warps w and w + 4 share TMEM lane quadrant w; thread r
+//              (mod 128) owns weight row r of the row block = TMEM lane r.
+//              Per 64 columns a thread turns 20 packed bytes into 32 bf16x2
+//              registers (prmt table lookups; the weights are +-2^(e-10),
+//              exact in bf16) and stores them to a TMEM A stage with one
+//              tcgen05.st; warps 0-3 take column steps 0 and 2 of each unit,
+//              warps 4-7 steps 1 and 3.  After a job's last unit warps 0-3 read
+//              the fp32 accumulators back with tcgen05.ld and write y.
+//   warp 8     allocates TMEM; lane 0 issues tcgen05.mma (kind::f16, A from
+//              TMEM, B = x from shared memory, D fp32 in TMEM) and commits
+//              each stage back to its producer.
+//   warp 9     lane 0 issues the TMA loads: weight tiles (before the
+//              programmatic-launch wait, since weights never depend on the
+//              previous kernel) and x tiles (128-byte swizzled, K-major).
+//
+// Every mbarrier wait is bounded (%globaltimer, 2 s); an expired wait records
+// an error in the workspace word and the thread leaves its loop, so the CTA
+// still reaches the final barrier and frees its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace spark {
+namespace tc {
+
+constexpr int kRows = 128;            // weight rows per unit = MMA M = TMEM lanes
+constexpr int kUnitCols = 256;        // columns per unit
+constexpr int kRowBytes = 80;         // SPFP2 bytes of one row in one unit (16 pairs x 5 B)
+constexpr int kUnitBytes = kRows * kRowBytes;
+constexpr int kSub = 4;               // 64-column sub-steps per unit (one A stage each)
+constexpr int kWStages = 6;
+constexpr int kDecThreads = 256;      // 8 decode warps: two per TMEM lane quadrant
+constexpr int kMmaWarp = 8;
+constexpr int kProducerWarp = 9;
+constexpr int kThreads = 320;
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+template <int N>
+struct Cfg {
+    // A stages (64 columns each) and the D buffers share the CTA's TMEM.
+    static constexpr int kAStages = N == 16 ? 6 : 8;
+    static constexpr int kDBuf = N <= 128 ? 2 : 1;
+    static constexpr int kDCols = kDBuf * N;
+    static constexpr uint32_t kTmemCols = kDCols + kAStages * 32 <= 256 ? 256u : 512u;
+    static constexpr int kXStages = N <= 64 ? 8 : (N == 128 ? 6 : 4);
+    static constexpr int kXBytes = N * 128;                  // N rows x 64 bf16
+    // dynamic shared memory (offsets from a 1024-aligned base)
+    static constexpr int kX = 0;
+    static constexpr int kW = kX + kXStages * kXBytes;
+    static constexpr int kLut = kW + kWStages * kUnitBytes;
+    static constexpr int kBar = kLut + 256 * 16;
+    static constexpr int kNumBars = 2 * kWStages + 2 * kXStages + 2 * kAStages + 2 * kDBuf;
+    static constexpr int kBytes = kBar + kNumBars * 8 + 16;
+    static constexpr int kAlloc = kBytes + 1024;             // slack for aligning the base
+};
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+// Wait for the phase with the given parity to complete; false after kWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t deadline = globaltimer_ns() + kWaitNs;
+    while (!mbar_try(bar, parity))
+        if (globaltimer_ns() > deadline) return false;
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive 32-bit TMEM columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 16 consecutive fp32 TMEM columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// D[tmem] (+)= A[tmem] . B[smem]^T, kind::f16, M = 128, no lanes disabled
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// Instruction descriptor: D f32, A and B bf16, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (stride byte offset); the leading byte offset is unused
+// for swizzled K-major layouts and set to 16 bytes.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3fffu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
+           ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
+__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// ------------------------------------------------------------------ SPFP2 decode
+// lut[b] for an exponent byte b = e0 | e1 << 4: {x0, y0, x1, y1} where, for a
+// block exponent e and E = 117 + e the bf16 biased exponent of 2^(e-10),
+// x = bytes [E >> 1, (E >> 1) | 0x80, 0, 0] (high bytes of +w, -w, 0, 0 for
+// codes 0..3, block_fp2_emu.py:36) and y = bytes [(E & 1) << 7, same, 0, 0].
+__device__ __forceinline__ uint2 exp_tables(uint32_t e) {
+    const uint32_t E = 117u + e;
+    return make_uint2((E >> 1) * 0x101u + 0x8000u, ((E & 1u) << 7) * 0x101u);
+}
+
+// Eight codes of one block -> four bf16x2 registers.  With selectors se
+// (codes 0,1,4,5) and so (codes 2,3,6,7), see decode_pair, the output is in
+// natural column order.
+__device__ __forceinline__ void decode8(uint32_t se, uint32_t so, uint32_t tx, uint32_t ty, uint32_t* A) {
+    const uint32_t he = prmt(tx, 0u, se), ho = prmt(tx, 0u, so);
+    const uint32_t le = prmt(ty, 0u, se), lo = prmt(ty, 0u, so);
+    A[0] = prmt(le, he, 0x5140u);
+    A[1] = prmt(lo, ho, 0x5140u);
+    A[2] = prmt(le, he, 0x7362u);
+    A[3] = prmt(lo, ho, 0x7362u);
+}
+
+// One pair (16 weights): mantissa word mw = m0 | m1 << 16 (code i of a block
+// at bits 2i), exponent tables t.  Swapping codes 1<->2 of every byte makes
+// the nibble selectors (w & 0x3333) and (w >> 2 & 0x3333) pick codes
+// (0,1,4,5) and (2,3,6,7), which decode8 interleaves into columns 0..7.
+__device__ __forceinline__ void decode_pair(uint32_t mw, uint4 t, uint32_t* A) {
+    const uint32_t inner = ((mw << 2) & 0x30303030u) | ((mw >> 2) & 0x0c0c0c0cu);
+    const uint32_t w = (mw & 0xc3c3c3c3u) | inner;
+    const uint32_t se = w & 0x33333333u, so = (w >> 2) & 0x33333333u;
+    decode8(se, so, t.x, t.y, A);
+    decode8(se >> 16, so >> 16, t.z, t.w, A + 4);
+}
+
+// ------------------------------------------------------------------ kernel
+struct Params {
+    const void* bias;
+    void* y;
+    float* partials;      // stream-K: [2 * grid][N][128]
+    int* counters;        // stream-K: [jobs][4], zero between calls
+    int* err;
+    int64_t oc, ldy;
+    int M, n_rb, n_kc, jobs, units, grid, stream_k, bias_dtype, y_dtype;
+};
+
+__device__ __forceinline__ int unit_begin(int c, const Params& p) {
+    return (int)(((int64_t)c * p.units) / p.grid);
+}
+// CTA that owns unit u (stream-K)
+__device__ __forceinline__ int unit_owner(int u, const Params& p) {
+    return (int)((((int64_t)u + 1) * p.grid - 1) / p.units);
+}
+
+// One segment: column blocks [ka, kb) of job `job` (= token tile * n_rb + row block).
+struct Seg {
+    int job, ka, kb;
+};
+
+// The segments of one CTA, identical for every role.  Stream-K: the CTA's
+// contiguous unit range cut at job boundaries.  Job mode: whole jobs
+// c, c + grid, c + 2 grid, ...
+struct SegIter {
+    int u, u1, job;
+    __device__ SegIter(int c, const Params& p) : u(unit_begin(c, p)), u1(unit_begin(c + 1, p)), job(c) {}
+    __device__ bool next(Seg& s, const Params& p) {
+        if (p.stream_k) {
+            if (u >= u1) return false;
+            s.job = u / p.n_kc;
+            s.ka = u - s.job * p.n_kc;
+            const int e = min(u1, (s.job + 1) * p.n_kc);
+            s.kb = e - s.job * p.n_kc;
+            u = e;
+            return true;
+        }
+        if (job >= p.jobs) return false;
+        s.job = job;
+        s.ka = 0;
+        s.kb = p.n_kc;
+        job += p.grid;
+        return true;
+    }
+};
+
+// Flattened (job, column block) sequence of one CTA, for the producer.
+struct UnitIter {
+    SegIter it;
+    Seg s;
+    int kc;
+    __device__ UnitIter(int c, const Params& p) : it(c, p), kc(0) { s.kb = 0; }
+    __device__ bool next(const Params& p, int& job, int& col_block) {
+        while (kc >= s.kb) {
+            if (!it.next(s, p)) return false;
+            kc = s.ka;
+        }
+        job = s.job;
+        col_block = kc++;
+        return true;
+    }
+};
+
+template <int N>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_tc_spfp2(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const Params p) {
+    using C = Cfg<N>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint32_t tmem_base_s;
+    uint4* lut = reinterpret_cast<uint4*>(smem + C::kLut);
+    const uint32_t bar0 = smem_u32(smem + C::kBar);
+    auto w_full = [&](int s) { return bar0 + 8u * s; };
+    auto w_empty = [&](int s) { return bar0 + 8u * (kWStages + s); };
+    auto x_full = [&](int s) { return bar0 + 8u * (2 * kWStages + s); };
+    auto x_empty = [&](int s) { return bar0 + 8u * (2 * kWStages + C::kXStages + s); };
+    auto a_full = [&](int s) { return bar0 + 8u * (2 * kWStages + 2 * C::kXStages + s); };
+    auto a_empty = [&](int s) { return bar0 + 8u * (2 * kWStages + 2 * C::kXStages + C::kAStages + s); };
+    auto d_full = [&](int s) { return bar0 + 8u * (2 * kWStages + 2 * C::kXStages + 2 * C::kAStages + s); };
+    auto d_empty = [&](int s) {
+        return bar0 + 8u * (2 * kWStages + 2 * C::kXStages + 2 * C::kAStages + C::kDBuf + s);
+    };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kWStages; ++s) { mbar_init(w_full(s), 1); mbar_init(w_empty(s), kDecThreads); }
+        for (int s = 0; s < C::kXStages; ++s) { mbar_init(x_full(s), 1); mbar_init(x_empty(s), 1); }
+        for (int s = 0; s < C::kAStages; ++s) { mbar_init(a_full(s), kRows); mbar_init(a_empty(s), 1); }
+        for (int s = 0; s < C::kDBuf; ++s) { mbar_init(d_full(s), 1); mbar_init(d_empty(s), kRows); }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kProducerWarp && lane == 0) { prefetch_map(&wmap); prefetch_map(&xmap); }
+    for (int i = threadIdx.x; i < 256; i += kThreads) {
+        const uint2 a = exp_tables(i & 15), b = exp_tables(i >> 4);
+        lut[i] = make_uint4(a.x, a.y, b.x, b.y);
+    }
+    if (warp == kMmaWarp) tmem_alloc(smem_u32(&tmem_base_s), C::kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // Every CTA holds its TMEM now: the next kernel in the stream may start.
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const uint32_t tbase = tmem_base_s;
+    const uint32_t a_col0 = C::kDCols;
+    bool ok = true;
+
+    if (warp == kProducerWarp) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            UnitIter wi(cta, p), xi(cta, p);
+            int iw = 0, job, kc;
+            auto issue_w = [&](int i, int jb, int k) -> bool {
+                const int s = i % kWStages;
+                if (!mbar_wait(w_empty(s), ((i / kWStages) & 1) ^ 1)) return false;
+                mbar_expect_tx(w_full(s), kUnitBytes);
+                tma_load_2d(smem_u32(smem + C::kW + s * kUnitBytes), &wmap, k * kRowBytes, (jb % p.n_rb) * kRows,
+                            w_full(s));
+                return true;
+            };
+            while (ok && iw < kWStages && wi.next(p, job, kc)) ok = issue_w(iw++, job, kc);
+            // x and everything after it may depend on the previous kernel
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int i = 0; ok && xi.next(p, job, kc); ++i) {
+                const int tb = job / p.n_rb;
+                for (int j = 0; j < kSub && ok; ++j) {
+                    const int ix = i * kSub + j, s = ix % C::kXStages;
+                    ok = mbar_wait(x_empty(s), ((ix / C::kXStages) & 1) ^ 1);
+                    if (!ok) break;
+                    mbar_expect_tx(x_full(s), C::kXBytes);
+                    tma_load_2d(smem_u32(smem + C::kX + s * C::kXBytes), &xmap, kc * kUnitCols + j * 64, tb * N,
+                                x_full(s));
+                }
+                int jb, k;
+                if (ok && wi.next(p, jb, k)) ok = issue_w(iw++, jb, k);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(N);
+            SegIter it(cta, p);
+            Seg sg;
+            int i = 0;
+            for (int seg = 0; ok && it.next(sg, p); ++seg) {
+                const int buf = seg % C::kDBuf;
+                ok = mbar_wait(d_empty(buf), ((seg / C::kDBuf) & 1) ^ 1);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tbase + (uint32_t)(buf * N);
+                for (int kc = sg.ka; kc < sg.kb && ok; ++kc, ++i) {
+                    for (int j = 0; j < kSub; ++j) {
+                        const int ia = i * kSub + j, sa = ia % C::kAStages, sx = ia % C::kXStages;
+                        ok = mbar_wait(a_full(sa), (ia / C::kAStages) & 1) &&
+                             mbar_wait(x_full(sx), (ia / C::kXStages) & 1);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t xb = smem_u32(smem + C::kX + sx * C::kXBytes);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_ts(d_tmem, tbase + a_col0 + (uint32_t)(sa * 32 + kk * 8), sdesc_sw128(xb + kk * 32),
+                                   idesc, (kc == sg.ka && j == 0 && kk == 0) ? 0u : 1u);
+                        mma_commit(a_empty(sa));
+                        mma_commit(x_empty(sx));
+                    }
+                }
+                if (ok) mma_commit(d_full(buf));
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ decode (+ epilogue in half 0)
+        const int half = warp >> 2, quad = warp & 3;
+        const int r = threadIdx.x & (kRows - 1);          // row in the block = TMEM lane
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        SegIter it(cta, p);
+        Seg sg;
+        int i = 0;
+        for (int seg = 0; ok && it.next(sg, p); ++seg) {
+            for (int kc = sg.ka; kc < sg.kb && ok; ++kc, ++i) {
+                const int sw = i % kWStages;
+                ok = __all_sync(0xffffffffu, mbar_wait(w_full(sw), (i / kWStages) & 1));
+                if (!ok) break;
+                // this half's two 64-column sub-steps: words 5j .. 5j+4 for j = half, half + 2
+                uint32_t q[10];
+                {
+                    const uint32_t* src =
+                        reinterpret_cast<const uint32_t*>(smem + C::kW + sw * kUnitBytes + r * kRowBytes);
+#pragma unroll
+                    for (int k = 0; k < 5; ++k) {
+                        q[k] = src[5 * half + k];
+                        q[5 + k] = src[5 * (half + 2) + k];
+                    }
+                }
+                mbar_arrive(w_empty(sw));
+                uint32_t A[2][32];
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    const int j = half + 2 * jj, ia = i * kSub + j, sa = ia % C::kAStages;
+                    if (!__all_sync(0xffffffffu, mbar_wait(a_empty(sa), ((ia / C::kAStages) & 1) ^ 1))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t* w = q + 5 * jj;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        uint32_t mw, eb;
+                        if (k == 0) { mw = w[0]; eb = w[1] & 0xffu; }
+                        else if (k == 1) { mw = __funnelshift_r(w[1], w[2], 8); eb = (w[2] >> 8) & 0xffu; }
+                        else if (k == 2) { mw = __funnelshift_r(w[2], w[3], 16); eb = (w[3] >> 16) & 0xffu; }
+                        else { mw = __funnelshift_r(w[3], w[4], 24); eb = w[4] >> 24; }
+                        decode_pair(mw, lut[eb], A[jj] + 8 * k);
+                    }
+                    if (jj == 1) {
+                        // the first store finished while the second half-chunk decoded
+                        tmem_st_wait();
+                        tc_fence_before();
+                        mbar_arrive(a_full((ia - 2) % C::kAStages));
+                    }
+                    tmem_st32(tbase + lane_addr + a_col0 + (uint32_t)(sa * 32), A[jj]);
+                }
+                if (!ok) break;
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(a_full((i * kSub + half + 2) % C::kAStages));
+            }
+            if (!ok || half != 0) continue;
+
+            // ---------------- epilogue (half 0: warps 0-3, thread r = row r)
+            const int buf = seg % C::kDBuf;
+            ok = __all_sync(0xffffffffu, mbar_wait(d_full(buf), (seg / C::kDBuf) & 1));
+            if (!ok) break;
+            tc_fence_after();
+            const int job = sg.job;
+            const int rb = job % p.n_rb, tb = job / p.n_rb;
+            const int64_t row = (int64_t)rb * kRows + r;
+            const int m0 = tb * N;
+            const int mcount = min(N, p.M - m0);
+            const uint32_t d_addr = tbase + lane_addr + (uint32_t)(buf * N);
+            const float bias = (p.bias && row < p.oc) ? load_as_float(p.bias, p.bias_dtype, row) : 0.0f;
+            if (sg.ka == 0 && sg.kb == p.n_kc) {
+                for (int c = 0; c < N; c += 16) {
+                    float v[16];
+                    tmem_ld16(d_addr + c, v);
+                    if (row < p.oc)
+#pragma unroll
+                        for (int t = 0; t < 16; ++t)
+                            if (c + t < mcount)
+                                store_from_float(p.y, p.y_dtype, (int64_t)(m0 + c + t) * p.ldy + row, v[t] + bias);
+                }
+                tc_fence_before();
+                mbar_arrive(d_empty(buf));
+            } else if constexpr (N == 16) {
+                // Partial sum (stream-K, N = 16): publish it; per 32-row slice,
+                // the warp that arrives last over all contributors adds every
+                // contributor's partial in CTA order (same order on every call).
+                const int slot = 2 * cta + (seg == 0 ? 0 : 1);
+                float* mine = p.partials + (int64_t)slot * N * kRows + r;
+                for (int c = 0; c < N; c += 16) {
+                    float v[16];
+                    tmem_ld16(d_addr + c, v);
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) __stcg(mine + (c + t) * kRows, v[t]);
+                }
+                tc_fence_before();
+                mbar_arrive(d_empty(buf));
+                __threadfence();
+                __syncwarp();
+                const int job_u0 = job * p.n_kc;
+                const int cA = unit_owner(job_u0, p), cB = unit_owner(job_u0 + p.n_kc - 1, p);
+                int last = 0;
+                if (lane == 0) last = atomic_add_acq_rel(p.counters + 4 * job + quad, 1) == cB - cA;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    if (row < p.oc) {
+                        float acc[N];
+#pragma unroll
+                        for (int t = 0; t < N; ++t) acc[t] = 0.0f;
+                        for (int cc = cA; cc <= cB; ++cc) {
+                            const int sl = 2 * cc + (unit_begin(cc, p) >= job_u0 ? 0 : 1);
+                            const float* src = p.partials + (int64_t)sl * N * kRows + r;
+                            float v[N];
+#pragma unroll
+                            for (int t = 0; t < N; ++t) v[t] = t < mcount ? __ldcg(src + t * kRows) : 0.0f;
+#pragma unroll
+                            for (int t = 0; t < N; ++t) acc[t] += v[t];
+                        }
+#pragma unroll
+                        for (int t = 0; t < N; ++t)
+                            if (t < mcount)
+                                store_from_float(p.y, p.y_dtype, (int64_t)(m0 + t) * p.ldy + row, acc[t] + bias);
+                    }
+                    if (lane == 0) p.counters[4 * job + quad] = 0;
+                }
+            }
+        }
+    }
+    if (!ok) report_device_error(p.err, 3);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tbase, C::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_mu;
+
+int get_encoder() {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_encode) return SPARK_OK;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return set_error(SPARK_ERR_DEVICE, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(e));
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return SPARK_OK;
+}
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SPARK_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SPARK_OK;
+}
+
+int sm_count_cached(int dev) {
+    static int cnt[64] = {};
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cnt[dev]) cudaDeviceGetAttribute(&cnt[dev], cudaDevAttrMultiProcessorCount, dev);
+    return cnt[dev] > 0 ? cnt[dev] : 148;
+}
+
+template <int N>
+int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, Params p, cudaStream_t s) {
+    using Cf = Cfg<N>;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        static bool done[64] = {};
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!done[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(k_tc_spfp2<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kAlloc);
+            if (e != cudaSuccess) return set_error((int)e, "k_tc_spfp2 attribute: %s", cudaGetErrorString(e));
+            done[dev] = true;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)p.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cf::kAlloc;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_tc_spfp2<N>, wmap, xmap, p);
+    if (e != cudaSuccess) return set_error((int)e, "k_tc_spfp2 launch: %s", cudaGetErrorString(e));
+    return SPARK_OK;
+}
+
+int token_tile(int64_t M) { return M <= 16 ? 16 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)); }
+
+}  // namespace tc
+
+// Workspace bytes of the tcgen05 path beyond the error word and counters:
+// two partial slots of 16 x 128 fp32 per CTA (stream-K runs only for M <= 16).
+size_t tc_partials_bytes(int dev, int64_t M) {
+    (void)M;
+    return (size_t)2 * tc::sm_count_cached(dev) * 16 * tc::kRows * sizeof(float);
+}
+
+bool tc_spfp2_ok(const void* wq, const void* x, int x_dtype, int64_t ic, int64_t ldx) {
+    return x_dtype == SPARK_DTYPE_BF16 && ic % tc::kUnitCols == 0 && aligned(wq, 16) && aligned(x, 16) &&
+           (ldx % 8) == 0;
+}
+
+// SPFP2 linear through k_tc_spfp2.  `counters` must hold max_counters zero
+// ints (4 per job are used); `partials` tc_partials_bytes(dev, M) bytes.
+int tc_spfp2_linear(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int64_t ic, int64_t ldx,
+                    const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err, int* counters,
+                    int64_t max_counters, float* partials, cudaStream_t s) {
+    SPARK_REQUIRE(tc_spfp2_ok(wq, x, SPARK_DTYPE_BF16, ic, ldx), SPARK_ERR_ALIGNMENT,
+                  "tcgen05 SPFP2 path: ic %% 256, 16-byte aligned weights and x, ldx %% 8 required");
+    int rc = tc::get_encoder();
+    if (rc) return rc;
+    const int N = tc::token_tile(M);
+    const int64_t n_rb = (oc + tc::kRows - 1) / tc::kRows, n_kc = ic / tc::kUnitCols, n_tb = (M + N - 1) / N;
+    const int64_t jobs = n_rb * n_tb;
+    SPARK_REQUIRE(4 * jobs <= max_counters, SPARK_ERR_UNSUPPORTED, "tcgen05 SPFP2 path: %lld jobs above %lld",
+                  (long long)jobs, (long long)(max_counters / 4));
+    const int64_t units = jobs * n_kc;
+    SPARK_REQUIRE(units < (1ll << 31) / 1024, SPARK_ERR_UNSUPPORTED, "tcgen05 SPFP2 path: problem too large");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int ctas = tc::sm_count_cached(dev);
+    alignas(64) CUtensorMap wmap, xmap;
+    rc = tc::encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)(ic / 16 * 5), (uint64_t)oc,
+                       (uint64_t)(ic / 16 * 5), tc::kRowBytes, tc::kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = tc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)ic, (uint64_t)M, (uint64_t)ldx * 2, 64,
+                       (uint32_t)N, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    tc::Params p = {};
+    p.bias = bias;
+    p.y = y;
+    p.partials = partials;
+    p.counters = counters;
+    p.err = err;
+    p.oc = oc;
+    p.ldy = ldy;
+    p.M = (int)M;
+    p.n_rb = (int)n_rb;
+    p.n_kc = (int)n_kc;
+    p.jobs = (int)jobs;
+    p.units = (int)units;
+    // Decode: units split evenly over the CTAs (stream-K, 16-token partials).
+    // Larger token tiles: whole jobs in turn, no partial sums.
+    p.stream_k = N == 16 ? 1 : 0;
+    p.grid = (int)(p.stream_k ? std::min<int64_t>(units, ctas) : std::min<int64_t>(jobs, ctas));
+    p.bias_dtype = bias_dtype;
+    p.y_dtype = y_dtype;
+    switch (N) {
+        case 16: return tc::launch<16>(wmap, xmap, p, s);
+        case 64: return tc::launch<64>(wmap, xmap, p, s);
+        case 128: return tc::launch<128>(wmap, xmap, p, s);
+        default: return tc::launch<256>(wmap, xmap, p, s);
+    }
+}
+
+}  // namespace spark

@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 from ._lib import (DTYPE_BF16, DTYPE_F16, DTYPE_F32, FMT_FP3, FMT_NVFP4, FMT_SPFP2, FMT_SPFP2_V1,
-                   FMT_TWOFOUR, LAYOUT_TILED, call)
+                   FMT_TWOFOUR, LAYOUT_TILED, PATH_TCGEN05, call)
 
 _DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
 
@@ -230,10 +230,13 @@ def tile_weights(fmt, wq: torch.Tensor, scales, oc: int, ic: int) -> torch.Tenso
 
 
 def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bias=None, out_dtype=None,
-           out: torch.Tensor | None = None, tiled: bool = False) -> torch.Tensor:
+           out: torch.Tensor | None = None, tiled: bool = False, tcgen05: bool = False) -> torch.Tensor:
     """y[..., oc] = x[..., ic] . decode(W)^T (+ bias) with W packed in `fmt`
-    (reference layout, or the tile_weights copy with tiled=True)."""
+    (reference layout, or the tile_weights copy with tiled=True).  tcgen05=True
+    runs the tensor-memory kernel (SPFP2 reference layout, bf16 x)."""
     f = FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+    if tcgen05:
+        f |= PATH_TCGEN05
     if tiled:
         f |= LAYOUT_TILED
         scales = None
@@ -250,7 +253,7 @@ def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bia
     s = _bytes(scales) if scales is not None else None
     b = bias.contiguous() if bias is not None else None
     y = out if out is not None else torch.empty(M, oc, dtype=out_dtype or x.dtype, device=x.device)
-    nbytes = workspace_size(f & ~LAYOUT_TILED, M, oc, ic)
+    nbytes = workspace_size(f & 0xff, M, oc, ic)
     ws = workspace(x.device, nbytes)
     call("spark_linear", f, _p(w), _p(s), _p(x2), _dt(x2), M, oc, ic, x2.stride(0), _p(b),
          _dt(b) if b is not None else DTYPE_F32, _p(y), _dt(y), y.stride(0), _p(ws), ws.numel(), _stream(x))

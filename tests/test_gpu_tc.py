@@ -1,0 +1,99 @@
+"""The tcgen05 SPFP2 linear (A = decoded weights in tensor memory, B = x in
+shared memory, fp32 accumulation in tensor memory) against an fp64
+accumulation of the oracle-decoded weights: max |y - y_ref| <= 5e-4 for fp32
+output (bf16 output within its own rounding).  Covers the decode shape
+(M <= 16, stream-K split with partial sums), every token tile (16, 64, 128,
+256), ragged row blocks and several token tiles."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 5e-4
+
+
+def ops():
+    from spark_b200 import ops as _ops
+    return _ops
+
+
+def run(oc, ic, M, seed=0, bias=False, out_dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    W = torch.randn(oc, ic, generator=g) * 0.02
+    wq, _ = ops().spfp2_pack(W.cuda())
+    x = torch.randn(M, ic, generator=g).bfloat16()
+    b = (torch.randn(oc, generator=g) * 0.1) if bias else None
+    y = ops().linear("spfp2", wq, None, x.cuda(), oc, ic, bias=b.cuda() if b is not None else None,
+                     out_dtype=out_dtype, tcgen05=True)
+    torch.cuda.synchronize()
+    ops().check_device_errors()
+    return wq, x, b, y
+
+
+def check_oracle(oc, ic, M, **kw):
+    wq, x, b, y = run(oc, ic, M, **kw)
+    dec = O.unpack_blockwise_paired(wq.cpu().numpy(), oc * ic).reshape(oc, ic)
+    y64 = O.linear_f64(x.float().numpy(), dec, b.numpy() if b is not None else None)
+    err = np.abs(y.float().cpu().numpy().astype(np.float64) - y64)
+    if y.dtype == torch.float32:
+        assert err.max() <= TOL, (oc, ic, M, err.max())
+    else:
+        assert np.all(err <= TOL + 2.0 ** -8 * np.abs(y64)), (oc, ic, M, err.max())
+
+
+@pytest.mark.parametrize("oc,ic", [(9728, 2560), (2560, 9728), (256, 256), (1000, 512), (130, 768)])
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_tc_decode_shapes(oc, ic, M):
+    check_oracle(oc, ic, M)
+
+
+@pytest.mark.parametrize("M", [17, 64, 100, 128, 200, 256, 300, 520])
+def test_tc_token_tiles(M):
+    check_oracle(1000, 1024, M, seed=M)
+
+
+def test_tc_bias_bf16_out():
+    check_oracle(2560, 2560, 3, bias=True, out_dtype=torch.bfloat16)
+    check_oracle(2560, 2560, 3, bias=True)
+    check_oracle(640, 512, 300, bias=True, out_dtype=torch.bfloat16)
+
+
+def test_tc_repeat_calls_bit_identical():
+    """Stream-K partial sums are added in CTA order: repeated calls agree bit for bit."""
+    g = torch.Generator().manual_seed(5)
+    W = (torch.randn(9728, 2560, generator=g) * 0.02).cuda()
+    wq, _ = ops().spfp2_pack(W)
+    x = torch.randn(4, 2560, generator=g).bfloat16().cuda()
+    ys = [ops().linear("spfp2", wq, None, x, 9728, 2560, out_dtype=torch.float32, tcgen05=True) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(ys[0], t) for t in ys[1:])
+
+
+@pytest.mark.parametrize("oc,ic", [(9728, 2560), (2560, 9728)])
+def test_tc_prefill_full_size(oc, ic):
+    """Config-3 shapes (M = 2048) against an fp64 GEMM of the GPU-decoded weights
+    (decode is bit-exact against the oracle, tests/test_gpu_formats.py)."""
+    M = 2048
+    g = torch.Generator(device="cuda").manual_seed(11)
+    W = torch.randn(oc, ic, device="cuda", generator=g) * 0.02
+    wq, _ = ops().spfp2_pack(W)
+    x = torch.randn(M, ic, device="cuda", generator=g).bfloat16()
+    y = ops().linear("spfp2", wq, None, x, oc, ic, out_dtype=torch.float32, tcgen05=True)
+    Wd = ops().spfp2_unpack(wq, oc * ic).view(oc, ic).double()
+    y64 = x.double() @ Wd.T
+    err = (y.double() - y64).abs().max().item()
+    assert err <= TOL, err
+    ops().check_device_errors()
+
+
+def test_tc_rejects_unsupported():
+    from spark_b200 import _lib
+    wq, _ = ops().spfp2_pack(torch.randn(256, 200, device="cuda"))   # ic % 256 != 0
+    with pytest.raises(_lib.SparkError) as e:
+        ops().linear("spfp2", wq, None, torch.randn(1, 200, device="cuda").bfloat16(), 256, 200, tcgen05=True)
+    assert e.value.code == _lib.ERR_UNSUPPORTED
