@@ -1186,10 +1186,11 @@ bool fast_path_ok(int fmt, const uint8_t* wq, const uint8_t* scales, int64_t oc,
 
 namespace spark {
 size_t tc_partials_bytes(int dev, int64_t M);
-bool tc_spfp2_ok(const void* wq, const void* x, int x_dtype, int64_t ic, int64_t ldx);
-int tc_spfp2_linear(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int64_t ic, int64_t ldx,
-                    const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err, int* counters,
-                    int64_t max_counters, float* partials, cudaStream_t s);
+bool tc_linear_ok(int fmt, const void* wq, const void* scales, const void* x, int x_dtype, int64_t ic,
+                  int64_t ldx);
+int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int64_t M, int64_t oc, int64_t ic,
+              int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err,
+              int* counters, int64_t max_counters, float* partials, cudaStream_t s);
 }  // namespace spark
 
 // ====================================================================== C ABI
@@ -1225,9 +1226,9 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
     if (M == 0 || oc == 0) return SPARK_OK;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (tcgen05) {
-        SPARK_REQUIRE(fmt == SPARK_FMT_SPFP2 && !tiled && tc_spfp2_ok(wq, x, x_dtype, ic, ldx), SPARK_ERR_UNSUPPORTED,
-                      "spark_linear: the tcgen05 path takes SPFP2 (reference layout), bf16 x, ic %% 256 == 0, "
-                      "16-byte aligned weights and x, ldx %% 8 == 0");
+        SPARK_REQUIRE(!tiled && tc_linear_ok(fmt, wq, scales, x, x_dtype, ic, ldx), SPARK_ERR_UNSUPPORTED,
+                      "spark_linear: the tcgen05 path takes SPFP2, FP3 or NVFP4 in the reference layout, bf16 x, "
+                      "ic %% 256 == 0, 16-byte aligned weights, scales and x, ldx %% 8 == 0");
         int dev = 0;
         cudaGetDevice(&dev);
         const WsLayout L = ws_layout(ic, max_warps(dev));
@@ -1236,7 +1237,7 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
                       "spark_linear: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
         SPARK_REQUIRE(aligned(workspace, 256), SPARK_ERR_ALIGNMENT, "spark_linear: workspace must be 256-byte aligned");
         uint8_t* ws = static_cast<uint8_t*>(workspace);
-        return tc_spfp2_linear(wq, x, M, oc, ic, ldx, bias, bias_dtype, y, y_dtype, ldy,
+        return tc_linear(fmt, wq, scales, x, M, oc, ic, ldx, bias, bias_dtype, y, y_dtype, ldy,
                                reinterpret_cast<int*>(ws + L.err), reinterpret_cast<int*>(ws + L.counters),
                                kMaxRowGroups, reinterpret_cast<float*>(ws + L.partials), s);
     }

@@ -1,10 +1,19 @@
-// tc_linear.cu -- SPFP2 online-dequant linear on the 5th-generation tensor cores.
+// tc_linear.cu -- online-dequant linear on the 5th-generation tensor cores.
 //
-// y[M, oc] = x[M, ic] . decode(W)^T, W in the reference's paired SPFP2 layout
-// (block_fp2_emu.py:231-267: per 16 weights, mantissa words m0, m1 as u16 LE
-// then one byte e0 | e1 << 4), read in place: no load-time re-layout.
+// y[M, oc] = x[M, ic] . decode(W)^T with W in one of the reference's packed
+// layouts, read in place (no load-time re-layout):
+//   SPFP2  block_fp2_emu.py:231-267: per 16 weights, mantissa words m0, m1
+//          (u16 LE, code i at bits 2i) then one byte e0 | e1 << 4;
+//   FP3    fp3_emu.py:107-139: 8 codes of 3 bits in 3 bytes (code i at bit
+//          3i), plus one e4m3 scale per 16 weights;
+//   NVFP4  nvfp4_emu.py:81-107: two e2m1 codes per byte (even element in the
+//          low nibble), plus one e4m3 scale per 16 weights.
+// Every decoded weight is exact in bf16 (SPFP2: +-2^(e-10); FP3 / NVFP4: a
+// code value with at most 2 significant bits times an e4m3 scale with 4), so
+// the tensor core multiplies the caller's bf16 x by the exact weights.
 //
-// Work unit: 128 weight rows x 256 columns (one TMA box of 128 x 80 bytes),
+// Work unit: 128 weight rows x 256 columns (TMA boxes of 128 rows of codes,
+// and of scales),
 // for one tile of N tokens; a job is all units of one (token tile, row
 // block).  One CTA per SM.  Decode (M <= 16, N = 16) splits the units of all
 // jobs evenly over the CTAs (stream-K): a CTA whose unit range starts or ends
@@ -15,10 +24,10 @@
 // Roles inside a CTA (320 threads):
 //   warps 0-7  decode: warps w and w + 4 share TMEM lane quadrant w; thread r
 //              (mod 128) owns weight row r of the row block = TMEM lane r.
-//              Per 64 columns a thread turns 20 packed bytes into 32 bf16x2
-//              registers (prmt table lookups; the weights are +-2^(e-10),
-//              exact in bf16) and stores them to a TMEM A stage with one
-//              tcgen05.st; warps 0-3 take column steps 0 and 2 of each unit,
+//              Per 64 columns a thread turns its packed bytes into 32 bf16x2
+//              registers (SPFP2: prmt table lookups; FP3 / NVFP4: a table of
+//              code pairs times the block scale, one bf16x2 multiply per two
+//              weights) and stores them to a TMEM A stage with one tcgen05.st; warps 0-3 take column steps 0 and 2 of each unit,
 //              warps 4-7 steps 1 and 3.  After a job's last unit warps 0-3 read
 //              the fp32 accumulators back with tcgen05.ld and write y.
 //   warp 8     allocates TMEM; lane 0 issues tcgen05.mma (kind::f16, A from
@@ -44,18 +53,27 @@ namespace tc {
 
 constexpr int kRows = 128;            // weight rows per unit = MMA M = TMEM lanes
 constexpr int kUnitCols = 256;        // columns per unit
-constexpr int kRowBytes = 80;         // SPFP2 bytes of one row in one unit (16 pairs x 5 B)
-constexpr int kUnitBytes = kRows * kRowBytes;
 constexpr int kSub = 4;               // 64-column sub-steps per unit (one A stage each)
-constexpr int kWStages = 6;
+
+// Packed bytes of one row in one unit: codes (SPFP2 16 pairs x 5 B, FP3
+// 32 x 3 B, NVFP4 128 x 1 B) and e4m3 scales (16 per unit).
+template <int FMT>
+struct Wfmt {
+    static constexpr int kCodeBytes = FMT == SPARK_FMT_SPFP2 ? 80 : (FMT == SPARK_FMT_FP3 ? 96 : 128);
+    static constexpr int kScaleBytes = FMT == SPARK_FMT_SPFP2 ? 0 : 16;
+    static constexpr int kStageBytes = kRows * (kCodeBytes + kScaleBytes);   // multiple of 1024
+    static constexpr bool kSwizzle = FMT == SPARK_FMT_NVFP4;                 // 128-byte rows: swizzle them
+};
 constexpr int kDecThreads = 256;      // 8 decode warps: two per TMEM lane quadrant
 constexpr int kMmaWarp = 8;
 constexpr int kProducerWarp = 9;
 constexpr int kThreads = 320;
 constexpr uint64_t kWaitNs = 2000000000ull;
 
-template <int N>
+template <int FMT, int N>
 struct Cfg {
+    using W = Wfmt<FMT>;
+    static constexpr int kWStages = (FMT == SPARK_FMT_NVFP4 && N == 256) ? 4 : 6;
     // A stages (64 columns each) and the D buffers share the CTA's TMEM.
     static constexpr int kAStages = N == 16 ? 6 : 8;
     static constexpr int kDBuf = N <= 128 ? 2 : 1;
@@ -66,11 +84,13 @@ struct Cfg {
     // dynamic shared memory (offsets from a 1024-aligned base)
     static constexpr int kX = 0;
     static constexpr int kW = kX + kXStages * kXBytes;
-    static constexpr int kLut = kW + kWStages * kUnitBytes;
+    static constexpr int kLut = kW + kWStages * W::kStageBytes;
     static constexpr int kBar = kLut + 256 * 16;
     static constexpr int kNumBars = 2 * kWStages + 2 * kXStages + 2 * kAStages + 2 * kDBuf;
     static constexpr int kBytes = kBar + kNumBars * 8 + 16;
     static constexpr int kAlloc = kBytes + 1024;             // slack for aligning the base
+    static_assert(kAlloc <= 232448, "shared memory above the 227 KB a CTA may use");
+    static_assert(W::kStageBytes % 1024 == 0 && (kXStages * kXBytes) % 1024 == 0, "stages must stay 1024-aligned");
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -227,6 +247,28 @@ __device__ __forceinline__ void decode_pair(uint32_t mw, uint4 t, uint32_t* A) {
     decode8(se >> 16, so >> 16, t.z, t.w, A + 4);
 }
 
+// ------------------------------------------------------------------ FP3 / NVFP4 decode
+// Tables in shared memory: scale2[b] = the e4m3 byte b as bf16, in both halves
+// (fp8 to bf16 is exact: at most 4 significant bits; NaN stays NaN);
+// pairv[v] = the two code values of a code pair v as bf16x2 (low half = the
+// even column).  FP3 codes: sign bit 2, magnitudes {0, .5, 1, 1.5}
+// (fp3_emu.py:14); NVFP4 codes: sign bit 3, magnitudes {0, .5, 1, 1.5, 2, 3,
+// 4, 6} (nvfp4_emu.py:17).
+__device__ __forceinline__ uint32_t bf16_bits(float f) { return __float_as_uint(f) >> 16; }
+
+__device__ __forceinline__ uint32_t code_value_bf16(int fmt, uint32_t c) {
+    if (fmt == SPARK_FMT_FP3) return bf16_bits(0.5f * (float)(c & 3u)) | ((c & 4u) << 13);
+    const uint32_t m = c & 7u;
+    const float v = m < 4u ? 0.5f * (float)m : (float)(1u << ((m - 2u) >> 1)) * (m & 1u ? 1.5f : 1.0f);
+    return bf16_bits(v) | ((c & 8u) << 12);
+}
+
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 // ------------------------------------------------------------------ kernel
 struct Params {
     const void* bias;
@@ -293,14 +335,19 @@ struct UnitIter {
     }
 };
 
-template <int N>
+template <int FMT, int N>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_tc_spfp2(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const Params p) {
-    using C = Cfg<N>;
+    k_tc_linear(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                const __grid_constant__ CUtensorMap xmap, const Params p) {
+    using C = Cfg<FMT, N>;
+    using WF = Wfmt<FMT>;
+    constexpr int kWStages = C::kWStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint32_t tmem_base_s;
-    uint4* lut = reinterpret_cast<uint4*>(smem + C::kLut);
+    uint4* lut = reinterpret_cast<uint4*>(smem + C::kLut);                        // SPFP2
+    uint32_t* scale2 = reinterpret_cast<uint32_t*>(smem + C::kLut);                // FP3 / NVFP4
+    uint32_t* pairv = reinterpret_cast<uint32_t*>(smem + C::kLut + 1024);
     const uint32_t bar0 = smem_u32(smem + C::kBar);
     auto w_full = [&](int s) { return bar0 + 8u * s; };
     auto w_empty = [&](int s) { return bar0 + 8u * (kWStages + s); };
@@ -323,10 +370,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < C::kDBuf; ++s) { mbar_init(d_full(s), 1); mbar_init(d_empty(s), kRows); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == kProducerWarp && lane == 0) { prefetch_map(&wmap); prefetch_map(&xmap); }
+    if (warp == kProducerWarp && lane == 0) {
+        prefetch_map(&wmap);
+        if constexpr (WF::kScaleBytes > 0) prefetch_map(&smap);
+        prefetch_map(&xmap);
+    }
     for (int i = threadIdx.x; i < 256; i += kThreads) {
-        const uint2 a = exp_tables(i & 15), b = exp_tables(i >> 4);
-        lut[i] = make_uint4(a.x, a.y, b.x, b.y);
+        if constexpr (FMT == SPARK_FMT_SPFP2) {
+            const uint2 a = exp_tables(i & 15), b = exp_tables(i >> 4);
+            lut[i] = make_uint4(a.x, a.y, b.x, b.y);
+        } else {
+            const uint32_t sb = bf16_bits(e4m3_to_f32((uint32_t)i));
+            scale2[i] = sb | (sb << 16);
+            const int bits = FMT == SPARK_FMT_FP3 ? 3 : 4;
+            if (i < (1 << (2 * bits))) {
+                const uint32_t lo = code_value_bf16(FMT, (uint32_t)i & ((1u << bits) - 1u));
+                const uint32_t hi = code_value_bf16(FMT, (uint32_t)i >> bits);
+                pairv[i] = lo | (hi << 16);
+            }
+        }
     }
     if (warp == kMmaWarp) tmem_alloc(smem_u32(&tmem_base_s), C::kTmemCols);
     tc_fence_before();
@@ -346,9 +408,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             auto issue_w = [&](int i, int jb, int k) -> bool {
                 const int s = i % kWStages;
                 if (!mbar_wait(w_empty(s), ((i / kWStages) & 1) ^ 1)) return false;
-                mbar_expect_tx(w_full(s), kUnitBytes);
-                tma_load_2d(smem_u32(smem + C::kW + s * kUnitBytes), &wmap, k * kRowBytes, (jb % p.n_rb) * kRows,
-                            w_full(s));
+                const uint32_t dst = smem_u32(smem + C::kW + s * WF::kStageBytes);
+                mbar_expect_tx(w_full(s), WF::kStageBytes);
+                tma_load_2d(dst, &wmap, k * WF::kCodeBytes, (jb % p.n_rb) * kRows, w_full(s));
+                if constexpr (WF::kScaleBytes > 0)
+                    tma_load_2d(dst + kRows * WF::kCodeBytes, &smap, k * WF::kScaleBytes, (jb % p.n_rb) * kRows,
+                                w_full(s));
                 return true;
             };
             while (ok && iw < kWStages && wi.next(p, job, kc)) ok = issue_w(iw++, job, kc);
@@ -413,16 +478,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int sw = i % kWStages;
                 ok = __all_sync(0xffffffffu, mbar_wait(w_full(sw), (i / kWStages) & 1));
                 if (!ok) break;
-                // this half's two 64-column sub-steps: words 5j .. 5j+4 for j = half, half + 2
-                uint32_t q[10];
-                {
-                    const uint32_t* src =
-                        reinterpret_cast<const uint32_t*>(smem + C::kW + sw * kUnitBytes + r * kRowBytes);
+                // this half's two 64-column sub-steps j = half, half + 2
+                const uint8_t* stage = smem + C::kW + sw * WF::kStageBytes;
+                uint32_t q[FMT == SPARK_FMT_SPFP2 ? 10 : (FMT == SPARK_FMT_FP3 ? 12 : 16)];
+                uint32_t sc[2] = {0u, 0u};
+                if constexpr (FMT == SPARK_FMT_SPFP2) {
+                    const uint32_t* src = reinterpret_cast<const uint32_t*>(stage + r * WF::kCodeBytes);
 #pragma unroll
                     for (int k = 0; k < 5; ++k) {
                         q[k] = src[5 * half + k];
                         q[5 + k] = src[5 * (half + 2) + k];
                     }
+                } else if constexpr (FMT == SPARK_FMT_FP3) {
+#pragma unroll
+                    for (int jj = 0; jj < 2; ++jj) {
+                        const uint2* src = reinterpret_cast<const uint2*>(stage + r * 96 + 24 * (half + 2 * jj));
+#pragma unroll
+                        for (int k = 0; k < 3; ++k) {
+                            const uint2 v = src[k];
+                            q[6 * jj + 2 * k] = v.x;
+                            q[6 * jj + 2 * k + 1] = v.y;
+                        }
+                    }
+                } else {
+                    // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
+#pragma unroll
+                    for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int c = 2 * (half + 2 * jj) + h;
+                            const uint4 v =
+                                *reinterpret_cast<const uint4*>(stage + r * 128 + 16 * (c ^ (r & 7)));
+                            q[8 * jj + 4 * h] = v.x;
+                            q[8 * jj + 4 * h + 1] = v.y;
+                            q[8 * jj + 4 * h + 2] = v.z;
+                            q[8 * jj + 4 * h + 3] = v.w;
+                        }
+                }
+                if constexpr (WF::kScaleBytes > 0) {
+                    const uint32_t* srow = reinterpret_cast<const uint32_t*>(stage + kRows * WF::kCodeBytes + r * 16);
+                    sc[0] = srow[half];
+                    sc[1] = srow[half + 2];
                 }
                 mbar_arrive(w_empty(sw));
                 uint32_t A[2][32];
@@ -434,15 +530,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t* w = q + 5 * jj;
+                    if constexpr (FMT == SPARK_FMT_SPFP2) {
+                        const uint32_t* w = q + 5 * jj;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        uint32_t mw, eb;
-                        if (k == 0) { mw = w[0]; eb = w[1] & 0xffu; }
-                        else if (k == 1) { mw = __funnelshift_r(w[1], w[2], 8); eb = (w[2] >> 8) & 0xffu; }
-                        else if (k == 2) { mw = __funnelshift_r(w[2], w[3], 16); eb = (w[3] >> 16) & 0xffu; }
-                        else { mw = __funnelshift_r(w[3], w[4], 24); eb = w[4] >> 24; }
-                        decode_pair(mw, lut[eb], A[jj] + 8 * k);
+                        for (int k = 0; k < 4; ++k) {
+                            uint32_t mw, eb;
+                            if (k == 0) { mw = w[0]; eb = w[1] & 0xffu; }
+                            else if (k == 1) { mw = __funnelshift_r(w[1], w[2], 8); eb = (w[2] >> 8) & 0xffu; }
+                            else if (k == 2) { mw = __funnelshift_r(w[2], w[3], 16); eb = (w[3] >> 16) & 0xffu; }
+                            else { mw = __funnelshift_r(w[3], w[4], 24); eb = w[4] >> 24; }
+                            decode_pair(mw, lut[eb], A[jj] + 8 * k);
+                        }
+                    } else if constexpr (FMT == SPARK_FMT_FP3) {
+                        // 64 codes = 192 bits; code pair k (columns 2k, 2k+1) at bit 6k
+                        const uint32_t* w = q + 6 * jj;
+#pragma unroll
+                        for (int k = 0; k < 32; ++k) {
+                            const int bit = 6 * k, wi = bit >> 5, off = bit & 31;
+                            const uint32_t v = (off <= 26 ? (w[wi] >> off) : __funnelshift_r(w[wi], w[wi + 1], off)) & 63u;
+                            A[jj][k] = mul_bf16x2(pairv[v], scale2[(sc[jj] >> (8 * (k >> 3))) & 0xffu]);
+                        }
+                    } else {
+                        // 64 codes = 32 bytes; byte k holds columns 2k, 2k+1
+                        const uint32_t* w = q + 8 * jj;
+#pragma unroll
+                        for (int k = 0; k < 32; ++k)
+                            A[jj][k] = mul_bf16x2(pairv[(w[k >> 2] >> (8 * (k & 3))) & 0xffu],
+                                                  scale2[(sc[jj] >> (8 * (k >> 3))) & 0xffu]);
                     }
                     if (jj == 1) {
                         // the first store finished while the second half-chunk decoded
@@ -573,17 +687,18 @@ int sm_count_cached(int dev) {
     return cnt[dev] > 0 ? cnt[dev] : 148;
 }
 
-template <int N>
-int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, Params p, cudaStream_t s) {
-    using Cf = Cfg<N>;
+template <int FMT, int N>
+int launch(const CUtensorMap& wmap, const CUtensorMap& smap, const CUtensorMap& xmap, Params p, cudaStream_t s) {
+    using Cf = Cfg<FMT, N>;
     int dev = 0;
     cudaGetDevice(&dev);
     {
         static bool done[64] = {};
         std::lock_guard<std::mutex> lk(g_mu);
         if (!done[dev]) {
-            cudaError_t e = cudaFuncSetAttribute(k_tc_spfp2<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kAlloc);
-            if (e != cudaSuccess) return set_error((int)e, "k_tc_spfp2 attribute: %s", cudaGetErrorString(e));
+            cudaError_t e =
+                cudaFuncSetAttribute(k_tc_linear<FMT, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kAlloc);
+            if (e != cudaSuccess) return set_error((int)e, "k_tc_linear attribute: %s", cudaGetErrorString(e));
             done[dev] = true;
         }
     }
@@ -597,9 +712,20 @@ int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, Params p, cudaStrea
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, k_tc_spfp2<N>, wmap, xmap, p);
-    if (e != cudaSuccess) return set_error((int)e, "k_tc_spfp2 launch: %s", cudaGetErrorString(e));
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_tc_linear<FMT, N>, wmap, smap, xmap, p);
+    if (e != cudaSuccess) return set_error((int)e, "k_tc_linear launch: %s", cudaGetErrorString(e));
     return SPARK_OK;
+}
+
+template <int FMT>
+int launch_n(int N, const CUtensorMap& wmap, const CUtensorMap& smap, const CUtensorMap& xmap, const Params& p,
+             cudaStream_t s) {
+    switch (N) {
+        case 16: return launch<FMT, 16>(wmap, smap, xmap, p, s);
+        case 64: return launch<FMT, 64>(wmap, smap, xmap, p, s);
+        case 128: return launch<FMT, 128>(wmap, smap, xmap, p, s);
+        default: return launch<FMT, 256>(wmap, smap, xmap, p, s);
+    }
 }
 
 int token_tile(int64_t M) { return M <= 16 ? 16 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)); }
@@ -613,34 +739,48 @@ size_t tc_partials_bytes(int dev, int64_t M) {
     return (size_t)2 * tc::sm_count_cached(dev) * 16 * tc::kRows * sizeof(float);
 }
 
-bool tc_spfp2_ok(const void* wq, const void* x, int x_dtype, int64_t ic, int64_t ldx) {
+bool tc_linear_ok(int fmt, const void* wq, const void* scales, const void* x, int x_dtype, int64_t ic,
+                  int64_t ldx) {
+    if (fmt != SPARK_FMT_SPFP2 && fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4) return false;
+    if (fmt != SPARK_FMT_SPFP2 && !aligned(scales, 16)) return false;
     return x_dtype == SPARK_DTYPE_BF16 && ic % tc::kUnitCols == 0 && aligned(wq, 16) && aligned(x, 16) &&
            (ldx % 8) == 0;
 }
 
-// SPFP2 linear through k_tc_spfp2.  `counters` must hold max_counters zero
-// ints (4 per job are used); `partials` tc_partials_bytes(dev, M) bytes.
-int tc_spfp2_linear(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int64_t ic, int64_t ldx,
-                    const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err, int* counters,
-                    int64_t max_counters, float* partials, cudaStream_t s) {
-    SPARK_REQUIRE(tc_spfp2_ok(wq, x, SPARK_DTYPE_BF16, ic, ldx), SPARK_ERR_ALIGNMENT,
-                  "tcgen05 SPFP2 path: ic %% 256, 16-byte aligned weights and x, ldx %% 8 required");
+// Linear through k_tc_linear (SPFP2, FP3 or NVFP4, reference layouts).
+// `counters` must hold max_counters zero ints (4 per job are used);
+// `partials` tc_partials_bytes(dev, M) bytes.
+int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int64_t M, int64_t oc, int64_t ic,
+              int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err,
+              int* counters, int64_t max_counters, float* partials, cudaStream_t s) {
+    SPARK_REQUIRE(tc_linear_ok(fmt, wq, scales, x, SPARK_DTYPE_BF16, ic, ldx), SPARK_ERR_ALIGNMENT,
+                  "tcgen05 path: SPFP2/FP3/NVFP4, ic %% 256, 16-byte aligned weights, scales and x, ldx %% 8");
     int rc = tc::get_encoder();
     if (rc) return rc;
     const int N = tc::token_tile(M);
     const int64_t n_rb = (oc + tc::kRows - 1) / tc::kRows, n_kc = ic / tc::kUnitCols, n_tb = (M + N - 1) / N;
     const int64_t jobs = n_rb * n_tb;
-    SPARK_REQUIRE(4 * jobs <= max_counters, SPARK_ERR_UNSUPPORTED, "tcgen05 SPFP2 path: %lld jobs above %lld",
+    SPARK_REQUIRE(4 * jobs <= max_counters, SPARK_ERR_UNSUPPORTED, "tcgen05 path: %lld jobs above %lld",
                   (long long)jobs, (long long)(max_counters / 4));
     const int64_t units = jobs * n_kc;
-    SPARK_REQUIRE(units < (1ll << 31) / 1024, SPARK_ERR_UNSUPPORTED, "tcgen05 SPFP2 path: problem too large");
+    SPARK_REQUIRE(units < (1ll << 31) / 1024, SPARK_ERR_UNSUPPORTED, "tcgen05 path: problem too large");
     int dev = 0;
     cudaGetDevice(&dev);
     const int ctas = tc::sm_count_cached(dev);
-    alignas(64) CUtensorMap wmap, xmap;
-    rc = tc::encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)(ic / 16 * 5), (uint64_t)oc,
-                       (uint64_t)(ic / 16 * 5), tc::kRowBytes, tc::kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const int code_bytes = fmt == SPARK_FMT_SPFP2 ? 80 : (fmt == SPARK_FMT_FP3 ? 96 : 128);
+    const uint64_t row_code_bytes = (uint64_t)(ic / tc::kUnitCols * code_bytes);
+    alignas(64) CUtensorMap wmap, smap, xmap;
+    rc = tc::encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, row_code_bytes, (uint64_t)oc, row_code_bytes,
+                       (uint32_t)code_bytes, tc::kRows,
+                       fmt == SPARK_FMT_NVFP4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
+    if (fmt == SPARK_FMT_SPFP2) {
+        smap = wmap;                      // unused
+    } else {
+        rc = tc::encode_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT8, scales, (uint64_t)(ic / 16), (uint64_t)oc,
+                           (uint64_t)(ic / 16), 16, tc::kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    }
     rc = tc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)ic, (uint64_t)M, (uint64_t)ldx * 2, 64,
                        (uint32_t)N, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -663,11 +803,10 @@ int tc_spfp2_linear(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int
     p.grid = (int)(p.stream_k ? std::min<int64_t>(units, ctas) : std::min<int64_t>(jobs, ctas));
     p.bias_dtype = bias_dtype;
     p.y_dtype = y_dtype;
-    switch (N) {
-        case 16: return tc::launch<16>(wmap, xmap, p, s);
-        case 64: return tc::launch<64>(wmap, xmap, p, s);
-        case 128: return tc::launch<128>(wmap, xmap, p, s);
-        default: return tc::launch<256>(wmap, xmap, p, s);
+    switch (fmt) {
+        case SPARK_FMT_SPFP2: return tc::launch_n<SPARK_FMT_SPFP2>(N, wmap, smap, xmap, p, s);
+        case SPARK_FMT_FP3: return tc::launch_n<SPARK_FMT_FP3>(N, wmap, smap, xmap, p, s);
+        default: return tc::launch_n<SPARK_FMT_NVFP4>(N, wmap, smap, xmap, p, s);
     }
 }
 

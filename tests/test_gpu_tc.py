@@ -1,4 +1,4 @@
-"""The tcgen05 SPFP2 linear (A = decoded weights in tensor memory, B = x in
+"""The tcgen05 linear (A = decoded weights in tensor memory, B = x in
 shared memory, fp32 accumulation in tensor memory) against an fp64
 accumulation of the oracle-decoded weights: max |y - y_ref| <= 5e-4 for fp32
 output (bf16 output within its own rounding).  Covers the decode shape
@@ -22,22 +22,39 @@ def ops():
     return _ops
 
 
-def run(oc, ic, M, seed=0, bias=False, out_dtype=torch.float32):
+def pack(fmt, W):
+    if fmt == "spfp2":
+        return ops().spfp2_pack(W)[0], None
+    if fmt == "fp3":
+        return ops().fp3_pack(W)
+    return ops().nvfp4_pack(W)
+
+
+def oracle_decode(fmt, wq, s, oc, ic):
+    if fmt == "spfp2":
+        return O.unpack_blockwise_paired(wq.cpu().numpy(), oc * ic).reshape(oc, ic)
+    sb = s.cpu().view(torch.uint8).numpy()
+    if fmt == "fp3":
+        return O.fp3_unpack_3bit(wq.cpu().numpy(), sb, oc, ic)
+    return O.nvfp4_unpack(wq.cpu().numpy(), sb, oc, ic)
+
+
+def run(oc, ic, M, seed=0, bias=False, out_dtype=torch.float32, fmt="spfp2"):
     g = torch.Generator().manual_seed(seed)
     W = torch.randn(oc, ic, generator=g) * 0.02
-    wq, _ = ops().spfp2_pack(W.cuda())
+    wq, s = pack(fmt, W.cuda())
     x = torch.randn(M, ic, generator=g).bfloat16()
     b = (torch.randn(oc, generator=g) * 0.1) if bias else None
-    y = ops().linear("spfp2", wq, None, x.cuda(), oc, ic, bias=b.cuda() if b is not None else None,
+    y = ops().linear(fmt, wq, s, x.cuda(), oc, ic, bias=b.cuda() if b is not None else None,
                      out_dtype=out_dtype, tcgen05=True)
     torch.cuda.synchronize()
     ops().check_device_errors()
-    return wq, x, b, y
+    return wq, s, x, b, y
 
 
-def check_oracle(oc, ic, M, **kw):
-    wq, x, b, y = run(oc, ic, M, **kw)
-    dec = O.unpack_blockwise_paired(wq.cpu().numpy(), oc * ic).reshape(oc, ic)
+def check_oracle(oc, ic, M, fmt="spfp2", **kw):
+    wq, s, x, b, y = run(oc, ic, M, fmt=fmt, **kw)
+    dec = oracle_decode(fmt, wq, s, oc, ic)
     y64 = O.linear_f64(x.float().numpy(), dec, b.numpy() if b is not None else None)
     err = np.abs(y.float().cpu().numpy().astype(np.float64) - y64)
     if y.dtype == torch.float32:
@@ -57,6 +74,18 @@ def test_tc_token_tiles(M):
     check_oracle(1000, 1024, M, seed=M)
 
 
+@pytest.mark.parametrize("fmt", ["fp3", "nvfp4"])
+@pytest.mark.parametrize("oc,ic,M", [(4096, 2560, 1), (2560, 4096, 16), (1000, 512, 3), (640, 768, 64),
+                                     (1000, 1024, 300), (130, 256, 200)])
+def test_tc_scaled_formats(fmt, oc, ic, M):
+    check_oracle(oc, ic, M, fmt=fmt, seed=oc + M)
+
+
+@pytest.mark.parametrize("fmt", ["fp3", "nvfp4"])
+def test_tc_scaled_formats_bias_bf16(fmt):
+    check_oracle(512, 512, 40, fmt=fmt, bias=True, out_dtype=torch.bfloat16)
+
+
 def test_tc_bias_bf16_out():
     check_oracle(2560, 2560, 3, bias=True, out_dtype=torch.bfloat16)
     check_oracle(2560, 2560, 3, bias=True)
@@ -74,17 +103,23 @@ def test_tc_repeat_calls_bit_identical():
     assert all(torch.equal(ys[0], t) for t in ys[1:])
 
 
-@pytest.mark.parametrize("oc,ic", [(9728, 2560), (2560, 9728)])
-def test_tc_prefill_full_size(oc, ic):
+@pytest.mark.parametrize("fmt,oc,ic", [("spfp2", 9728, 2560), ("spfp2", 2560, 9728), ("fp3", 4096, 2560),
+                                       ("nvfp4", 2560, 4096)])
+def test_tc_prefill_full_size(fmt, oc, ic):
     """Config-3 shapes (M = 2048) against an fp64 GEMM of the GPU-decoded weights
     (decode is bit-exact against the oracle, tests/test_gpu_formats.py)."""
     M = 2048
     g = torch.Generator(device="cuda").manual_seed(11)
     W = torch.randn(oc, ic, device="cuda", generator=g) * 0.02
-    wq, _ = ops().spfp2_pack(W)
+    wq, s = pack(fmt, W)
     x = torch.randn(M, ic, device="cuda", generator=g).bfloat16()
-    y = ops().linear("spfp2", wq, None, x, oc, ic, out_dtype=torch.float32, tcgen05=True)
-    Wd = ops().spfp2_unpack(wq, oc * ic).view(oc, ic).double()
+    y = ops().linear(fmt, wq, s, x, oc, ic, out_dtype=torch.float32, tcgen05=True)
+    if fmt == "spfp2":
+        Wd = ops().spfp2_unpack(wq, oc * ic).view(oc, ic).double()
+    elif fmt == "fp3":
+        Wd = ops().fp3_unpack(wq, s, oc, ic).view(oc, ic).double()
+    else:
+        Wd = ops().nvfp4_unpack(wq, s, oc, ic).view(oc, ic).double()
     y64 = x.double() @ Wd.T
     err = (y.double() - y64).abs().max().item()
     assert err <= TOL, err
