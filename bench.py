@@ -57,6 +57,7 @@ CONFIG = {
     "graph": "each step replayed as one CUDA graph",
 }
 METRIC = "dequant-GEMV HBM GB/s (% of 8 TB/s) at M=1; prefill dequant-GEMM TFLOP/s"
+PREFILL_M = 2048               # prefill tokens through one layer's 7 linears
 
 
 def weight_bytes(fmt, oc, ic):
@@ -84,6 +85,16 @@ def peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 TFLOP/s: the measured cuBLAS burst figure (the prefill loop is
+    timed for a few ms), else the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured MEASURED_PEAKS.json bf16_tflops (burst)"
+    except Exception:
+        return 1590.0, "fallback 1590 TFLOP/s"
 
 
 # ------------------------------------------------------------------ clocks
@@ -281,11 +292,35 @@ def run_gpu(args, rank, world, local):
     ms_e2e = max_over_ranks(e0.elapsed_time(e1), world)
     barrier(world)
 
+    # ---------------- prefill: PREFILL_M bf16 tokens through the
+    # 7 linears of one layer, reference-layout weights -> the tcgen05 GEMM
+    xs = {ic: torch.randn(PREFILL_M, ic, device=device, generator=g).bfloat16() for ic in (2560, 4096, 9728)}
+    ys = {name: torch.empty(PREFILL_M, oc, device=device, dtype=torch.bfloat16) for name, _, oc, _ in SHAPES}
+
+    def prefill_step():
+        for name, (fmt, wq, s, oc, ic, _) in layers[0].items():
+            ops.linear(fmt, wq, s, xs[ic], oc, ic, out=ys[name])
+
+    with torch.cuda.stream(stream):
+        prefill_step()
+        prefill_step()
+    torch.cuda.synchronize()
+    graph_pre = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_pre, stream=stream):
+        prefill_step()
+    pre_steps = max(5, args.steps // 20)
+    ms_pre = timed(graph_pre, pre_steps)
+    ops.check_device_errors()
+    pre_flops = sum(2.0 * PREFILL_M * oc * ic for _, _, oc, ic in SHAPES)
+    pre_tflops = world * pre_flops * pre_steps / (ms_pre * 1e-3) / 1e12
+    tpeak, tpeak_kind = tensor_peak()
+
     peak, peak_kind = peaks()
     value = world * STEP_BYTES * args.steps / (ms_total * 1e-3) / 1e9
     spfp2_gbs = SPFP2_BYTES * args.steps / (ms_spfp2 * 1e-3) / 1e9
     e2e_gbs = world * STEP_BYTES * args.steps / (ms_e2e * 1e-3) / 1e9
-    launches = args.steps * LAYERS * len(SHAPES) * 2    # prepare + GEMV per linear
+    # SPFP2 with bf16 x: one GEMV launch; FP3 / NVFP4: activation prepare + GEMV
+    launches = args.steps * LAYERS * sum(1 if f == "spfp2" else 2 for _, f, _, _ in SHAPES)
     traffic = load_traffic()
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -303,6 +338,16 @@ def run_gpu(args, rank, world, local):
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "spark_b200.inference_v3.V3PackedLinear, eager, pinned host I/O"},
         "clocks": clk.summary(),
+        "prefill": {
+            "workload": f"BASELINE config 3: M={PREFILL_M} bf16 tokens through the 7 linears of one layer "
+                        "(SPFP2 gate/up/down, FP3 q/k/v, NVFP4 out_proj), reference-layout weights, "
+                        "one CUDA graph per step",
+            "value": round(pre_tflops, 1), "unit": "TFLOP/s", "steps": pre_steps,
+            "ms_per_step": round(ms_pre / pre_steps, 4), "flops_per_step": pre_flops,
+            "kernel": "k_tc_linear<FMT, 128 or 256 tokens> (tcgen05.mma kind::f16, A = decoded weights in TMEM)",
+            "roofline": {"bound": "tensor", "achieved": round(pre_tflops / world, 1), "peak": tpeak,
+                         "unit": "TFLOP/s", "frac": round(pre_tflops / world / tpeak, 4), "peak_source": tpeak_kind},
+        },
     }
     if rank == 0:
         if not args.no_cpu_baseline and world == 1:

@@ -1225,8 +1225,10 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
                   SPARK_ERR_INVALID, "spark_linear: bad dtype");
     if (M == 0 || oc == 0) return SPARK_OK;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (tcgen05) {
-        SPARK_REQUIRE(!tiled && tc_linear_ok(fmt, wq, scales, x, x_dtype, ic, ldx), SPARK_ERR_UNSUPPORTED,
+    // More than 16 tokens on a reference layout with bf16 x: the tcgen05 GEMM.
+    const bool tc_ok = !tiled && tc_linear_ok(fmt, wq, scales, x, x_dtype, ic, ldx);
+    if (tcgen05 || (tc_ok && M > kMaxTokens)) {
+        SPARK_REQUIRE(tc_ok, SPARK_ERR_UNSUPPORTED,
                       "spark_linear: the tcgen05 path takes SPFP2, FP3 or NVFP4 in the reference layout, bf16 x, "
                       "ic %% 256 == 0, 16-byte aligned weights, scales and x, ldx %% 8 == 0");
         int dev = 0;

@@ -728,7 +728,16 @@ int launch_n(int N, const CUtensorMap& wmap, const CUtensorMap& smap, const CUte
     }
 }
 
-int token_tile(int64_t M) { return M <= 16 ? 16 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)); }
+// Tokens per tile.  Above 128 tokens: 256 unless 128-token tiles need
+// noticeably fewer token-rows per CTA once whole jobs are dealt out in rounds
+// (a 128-wide MMA runs ~15% below the 256-wide one per flop).
+int token_tile(int64_t M, int64_t n_rb, int ctas) {
+    if (M <= 16) return 16;
+    if (M <= 64) return 64;
+    if (M <= 128) return 128;
+    auto rounds = [&](int64_t n) { return (n_rb * ((M + n - 1) / n) + ctas - 1) / ctas; };
+    return (double)rounds(128) * 128 * 1.15 < (double)rounds(256) * 256 ? 128 : 256;
+}
 
 }  // namespace tc
 
@@ -757,16 +766,17 @@ int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, 
                   "tcgen05 path: SPFP2/FP3/NVFP4, ic %% 256, 16-byte aligned weights, scales and x, ldx %% 8");
     int rc = tc::get_encoder();
     if (rc) return rc;
-    const int N = tc::token_tile(M);
-    const int64_t n_rb = (oc + tc::kRows - 1) / tc::kRows, n_kc = ic / tc::kUnitCols, n_tb = (M + N - 1) / N;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int ctas = tc::sm_count_cached(dev);
+    const int64_t n_rb = (oc + tc::kRows - 1) / tc::kRows, n_kc = ic / tc::kUnitCols;
+    const int N = tc::token_tile(M, n_rb, ctas);
+    const int64_t n_tb = (M + N - 1) / N;
     const int64_t jobs = n_rb * n_tb;
     SPARK_REQUIRE(4 * jobs <= max_counters, SPARK_ERR_UNSUPPORTED, "tcgen05 path: %lld jobs above %lld",
                   (long long)jobs, (long long)(max_counters / 4));
     const int64_t units = jobs * n_kc;
     SPARK_REQUIRE(units < (1ll << 31) / 1024, SPARK_ERR_UNSUPPORTED, "tcgen05 path: problem too large");
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int ctas = tc::sm_count_cached(dev);
     const int code_bytes = fmt == SPARK_FMT_SPFP2 ? 80 : (fmt == SPARK_FMT_FP3 ? 96 : 128);
     const uint64_t row_code_bytes = (uint64_t)(ic / tc::kUnitCols * code_bytes);
     alignas(64) CUtensorMap wmap, smap, xmap;

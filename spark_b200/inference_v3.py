@@ -68,7 +68,9 @@ class V3PackedLinear(nn.Module):
             pad = (ic + 7) // 8 * 8
             x = torch.nn.functional.pad(x, (0, pad - ic))
             ic = pad
-        if self.w_tiled is not None and ic == self.in_features:
+        # up to 16 tokens: the decode GEMV on the tiled copy; more: the tcgen05
+        # GEMM, which reads the reference-layout bytes
+        if self.w_tiled is not None and ic == self.in_features and x.numel() <= 16 * ic:
             return ops.linear(self.fmt, self.w_tiled, None, x, self.out_features, ic, bias=self.bias,
                               out_dtype=x.dtype, tiled=True)
         return ops.linear(self.fmt, self.w_packed, self.w_scales, x, self.out_features, ic,

@@ -132,3 +132,18 @@ def test_tc_rejects_unsupported():
     with pytest.raises(_lib.SparkError) as e:
         ops().linear("spfp2", wq, None, torch.randn(1, 200, device="cuda").bfloat16(), 256, 200, tcgen05=True)
     assert e.value.code == _lib.ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("fmt", ["spfp2", "fp3", "nvfp4"])
+def test_tc_activation_range(fmt):
+    """bf16 x enters the tensor core unscaled: products are exact at any magnitude."""
+    oc, ic, M = 256, 1024, 40
+    g = torch.Generator().manual_seed(21)
+    wq, s = pack(fmt, (torch.randn(oc, ic, generator=g) * 0.02).cuda())
+    dec = oracle_decode(fmt, wq, s, oc, ic)
+    for scale in (1e-6, 1.0, 3e4, 1e8):
+        x = (torch.randn(M, ic, generator=g) * scale).bfloat16()
+        y = ops().linear(fmt, wq, s, x.cuda(), oc, ic, out_dtype=torch.float32).cpu().numpy()
+        y64 = O.linear_f64(x.float().numpy(), dec)
+        rel = np.abs(y - y64).max() / max(np.abs(y64).max(), 1e-30)
+        assert rel < 1e-5, (fmt, scale, rel)
