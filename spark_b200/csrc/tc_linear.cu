@@ -21,19 +21,21 @@
 // contributor adds them in CTA order, so the result does not depend on
 // timing.  Prefill (N = 64, 128 or 256) hands whole jobs to the CTAs in turn.
 //
-// Roles inside a CTA (320 threads):
-//   warps 0-7  decode: warps w and w + 4 share TMEM lane quadrant w; thread r
-//              (mod 128) owns weight row r of the row block = TMEM lane r.
-//              Per 64 columns a thread turns its packed bytes into 32 bf16x2
-//              registers (SPFP2: prmt table lookups; FP3 / NVFP4: a table of
-//              code pairs times the block scale, one bf16x2 multiply per two
-//              weights) and stores them to a TMEM A stage with one tcgen05.st; warps 0-3 take column steps 0 and 2 of each unit,
-//              warps 4-7 steps 1 and 3.  After a job's last unit warps 0-3 read
-//              the fp32 accumulators back with tcgen05.ld and write y.
-//   warp 8     allocates TMEM; lane 0 issues tcgen05.mma (kind::f16, A from
+// Roles inside a CTA (576 threads):
+//   warps 0-15 decode: warp w works on TMEM lane quadrant w % 4 and on column
+//              step w / 4 (64 columns) of every unit; thread r (mod 128) owns
+//              weight row r of the row block = TMEM lane r.  Per step a thread
+//              turns its packed bytes into 32 bf16x2 registers (SPFP2: prmt
+//              table lookups; FP3 / NVFP4: a table of code pairs times the
+//              block scale, one bf16x2 multiply per two weights) and stores
+//              them to a TMEM A stage with one tcgen05.st.  After a job's last
+//              unit the groups read the fp32 accumulators back with tcgen05.ld
+//              (each a quarter of the tokens; warps 0-3 alone for 16-token
+//              tiles), release them to the next job and write y.
+//   warp 16    allocates TMEM; lane 0 issues tcgen05.mma (kind::f16, A from
 //              TMEM, B = x from shared memory, D fp32 in TMEM) and commits
 //              each stage back to its producer.
-//   warp 9     lane 0 issues the TMA loads: weight tiles (before the
+//   warp 17    lane 0 issues the TMA loads: weight tiles (before the
 //              programmatic-launch wait, since weights never depend on the
 //              previous kernel) and x tiles (128-byte swizzled, K-major).
 //
@@ -64,22 +66,26 @@ struct Wfmt {
     static constexpr int kStageBytes = kRows * (kCodeBytes + kScaleBytes);   // multiple of 1024
     static constexpr bool kSwizzle = FMT == SPARK_FMT_NVFP4;                 // 128-byte rows: swizzle them
 };
-constexpr int kDecThreads = 256;      // 8 decode warps: two per TMEM lane quadrant
-constexpr int kMmaWarp = 8;
-constexpr int kProducerWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kDecThreads = 512;      // 16 decode warps: four per TMEM lane quadrant
+constexpr int kMmaWarp = 16;
+constexpr int kProducerWarp = 17;
+constexpr int kThreads = 576;
 constexpr uint64_t kWaitNs = 2000000000ull;
 
 template <int FMT, int N>
 struct Cfg {
     using W = Wfmt<FMT>;
-    static constexpr int kWStages = (FMT == SPARK_FMT_NVFP4 && N == 256) ? 4 : 6;
+    // Weight tiles decode fast: a few stages ahead suffice.  x tiles come from
+    // L2 and feed the tensor core directly, so big token tiles get the room.
+    static constexpr int kWStages = N >= 128 ? 3 : 6;
     // A stages (64 columns each) and the D buffers share the CTA's TMEM.
     static constexpr int kAStages = N == 16 ? 6 : 8;
     static constexpr int kDBuf = N <= 128 ? 2 : 1;
+    // decode groups that drain D after a job (each a slice of the N columns)
+    static constexpr int kEpiGroups = N >= 64 ? 4 : 1;
     static constexpr int kDCols = kDBuf * N;
     static constexpr uint32_t kTmemCols = kDCols + kAStages * 32 <= 256 ? 256u : 512u;
-    static constexpr int kXStages = N <= 64 ? 8 : (N == 128 ? 6 : 4);
+    static constexpr int kXStages = N <= 64 ? 8 : (N == 128 ? 10 : 5);
     static constexpr int kXBytes = N * 128;                  // N rows x 64 bf16
     // dynamic shared memory (offsets from a 1024-aligned base)
     static constexpr int kX = 0;
@@ -367,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < kWStages; ++s) { mbar_init(w_full(s), 1); mbar_init(w_empty(s), kDecThreads); }
         for (int s = 0; s < C::kXStages; ++s) { mbar_init(x_full(s), 1); mbar_init(x_empty(s), 1); }
         for (int s = 0; s < C::kAStages; ++s) { mbar_init(a_full(s), kRows); mbar_init(a_empty(s), 1); }
-        for (int s = 0; s < C::kDBuf; ++s) { mbar_init(d_full(s), 1); mbar_init(d_empty(s), kRows); }
+        for (int s = 0; s < C::kDBuf; ++s) { mbar_init(d_full(s), 1); mbar_init(d_empty(s), kRows * C::kEpiGroups); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == kProducerWarp && lane == 0) {
@@ -466,8 +472,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ------------------------------------------------------------ decode (+ epilogue in half 0)
-        const int half = warp >> 2, quad = warp & 3;
+        // ------------------------------------------------------------ decode (+ epilogue in group 0)
+        const int group = warp >> 2, quad = warp & 3;    // group = the 64-column step of each unit
         const int r = threadIdx.x & (kRows - 1);          // row in the block = TMEM lane
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         SegIter it(cta, p);
@@ -478,102 +484,79 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int sw = i % kWStages;
                 ok = __all_sync(0xffffffffu, mbar_wait(w_full(sw), (i / kWStages) & 1));
                 if (!ok) break;
-                // this half's two 64-column sub-steps j = half, half + 2
+                // this thread's 64 columns (step j = group) of row r
                 const uint8_t* stage = smem + C::kW + sw * WF::kStageBytes;
-                uint32_t q[FMT == SPARK_FMT_SPFP2 ? 10 : (FMT == SPARK_FMT_FP3 ? 12 : 16)];
-                uint32_t sc[2] = {0u, 0u};
+                uint32_t q[FMT == SPARK_FMT_SPFP2 ? 5 : (FMT == SPARK_FMT_FP3 ? 6 : 8)];
+                uint32_t sc = 0u;
                 if constexpr (FMT == SPARK_FMT_SPFP2) {
-                    const uint32_t* src = reinterpret_cast<const uint32_t*>(stage + r * WF::kCodeBytes);
+                    const uint32_t* src = reinterpret_cast<const uint32_t*>(stage + r * WF::kCodeBytes) + 5 * group;
 #pragma unroll
-                    for (int k = 0; k < 5; ++k) {
-                        q[k] = src[5 * half + k];
-                        q[5 + k] = src[5 * (half + 2) + k];
-                    }
+                    for (int k = 0; k < 5; ++k) q[k] = src[k];
                 } else if constexpr (FMT == SPARK_FMT_FP3) {
+                    const uint2* src = reinterpret_cast<const uint2*>(stage + r * 96 + 24 * group);
 #pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) {
-                        const uint2* src = reinterpret_cast<const uint2*>(stage + r * 96 + 24 * (half + 2 * jj));
-#pragma unroll
-                        for (int k = 0; k < 3; ++k) {
-                            const uint2 v = src[k];
-                            q[6 * jj + 2 * k] = v.x;
-                            q[6 * jj + 2 * k + 1] = v.y;
-                        }
+                    for (int k = 0; k < 3; ++k) {
+                        const uint2 v = src[k];
+                        q[2 * k] = v.x;
+                        q[2 * k + 1] = v.y;
                     }
                 } else {
                     // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
 #pragma unroll
-                    for (int jj = 0; jj < 2; ++jj)
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int c = 2 * (half + 2 * jj) + h;
-                            const uint4 v =
-                                *reinterpret_cast<const uint4*>(stage + r * 128 + 16 * (c ^ (r & 7)));
-                            q[8 * jj + 4 * h] = v.x;
-                            q[8 * jj + 4 * h + 1] = v.y;
-                            q[8 * jj + 4 * h + 2] = v.z;
-                            q[8 * jj + 4 * h + 3] = v.w;
-                        }
+                    for (int h = 0; h < 2; ++h) {
+                        const uint4 v =
+                            *reinterpret_cast<const uint4*>(stage + r * 128 + 16 * ((2 * group + h) ^ (r & 7)));
+                        q[4 * h] = v.x;
+                        q[4 * h + 1] = v.y;
+                        q[4 * h + 2] = v.z;
+                        q[4 * h + 3] = v.w;
+                    }
                 }
-                if constexpr (WF::kScaleBytes > 0) {
-                    const uint32_t* srow = reinterpret_cast<const uint32_t*>(stage + kRows * WF::kCodeBytes + r * 16);
-                    sc[0] = srow[half];
-                    sc[1] = srow[half + 2];
-                }
+                if constexpr (WF::kScaleBytes > 0)
+                    sc = reinterpret_cast<const uint32_t*>(stage + kRows * WF::kCodeBytes + r * 16)[group];
                 mbar_arrive(w_empty(sw));
-                uint32_t A[2][32];
-#pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
-                    const int j = half + 2 * jj, ia = i * kSub + j, sa = ia % C::kAStages;
-                    if (!__all_sync(0xffffffffu, mbar_wait(a_empty(sa), ((ia / C::kAStages) & 1) ^ 1))) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    if constexpr (FMT == SPARK_FMT_SPFP2) {
-                        const uint32_t* w = q + 5 * jj;
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            uint32_t mw, eb;
-                            if (k == 0) { mw = w[0]; eb = w[1] & 0xffu; }
-                            else if (k == 1) { mw = __funnelshift_r(w[1], w[2], 8); eb = (w[2] >> 8) & 0xffu; }
-                            else if (k == 2) { mw = __funnelshift_r(w[2], w[3], 16); eb = (w[3] >> 16) & 0xffu; }
-                            else { mw = __funnelshift_r(w[3], w[4], 24); eb = w[4] >> 24; }
-                            decode_pair(mw, lut[eb], A[jj] + 8 * k);
-                        }
-                    } else if constexpr (FMT == SPARK_FMT_FP3) {
-                        // 64 codes = 192 bits; code pair k (columns 2k, 2k+1) at bit 6k
-                        const uint32_t* w = q + 6 * jj;
-#pragma unroll
-                        for (int k = 0; k < 32; ++k) {
-                            const int bit = 6 * k, wi = bit >> 5, off = bit & 31;
-                            const uint32_t v = (off <= 26 ? (w[wi] >> off) : __funnelshift_r(w[wi], w[wi + 1], off)) & 63u;
-                            A[jj][k] = mul_bf16x2(pairv[v], scale2[(sc[jj] >> (8 * (k >> 3))) & 0xffu]);
-                        }
-                    } else {
-                        // 64 codes = 32 bytes; byte k holds columns 2k, 2k+1
-                        const uint32_t* w = q + 8 * jj;
-#pragma unroll
-                        for (int k = 0; k < 32; ++k)
-                            A[jj][k] = mul_bf16x2(pairv[(w[k >> 2] >> (8 * (k & 3))) & 0xffu],
-                                                  scale2[(sc[jj] >> (8 * (k >> 3))) & 0xffu]);
-                    }
-                    if (jj == 1) {
-                        // the first store finished while the second half-chunk decoded
-                        tmem_st_wait();
-                        tc_fence_before();
-                        mbar_arrive(a_full((ia - 2) % C::kAStages));
-                    }
-                    tmem_st32(tbase + lane_addr + a_col0 + (uint32_t)(sa * 32), A[jj]);
+
+                const int ia = i * kSub + group, sa = ia % C::kAStages;
+                if (!__all_sync(0xffffffffu, mbar_wait(a_empty(sa), ((ia / C::kAStages) & 1) ^ 1))) {
+                    ok = false;
+                    break;
                 }
-                if (!ok) break;
+                tc_fence_after();
+                uint32_t A[32];
+                if constexpr (FMT == SPARK_FMT_SPFP2) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        uint32_t mw, eb;
+                        if (k == 0) { mw = q[0]; eb = q[1] & 0xffu; }
+                        else if (k == 1) { mw = __funnelshift_r(q[1], q[2], 8); eb = (q[2] >> 8) & 0xffu; }
+                        else if (k == 2) { mw = __funnelshift_r(q[2], q[3], 16); eb = (q[3] >> 16) & 0xffu; }
+                        else { mw = __funnelshift_r(q[3], q[4], 24); eb = q[4] >> 24; }
+                        decode_pair(mw, lut[eb], A + 8 * k);
+                    }
+                } else if constexpr (FMT == SPARK_FMT_FP3) {
+                    // 64 codes = 192 bits; code pair k (columns 2k, 2k+1) at bit 6k
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) {
+                        const int bit = 6 * k, wi = bit >> 5, off = bit & 31;
+                        const uint32_t v = (off <= 26 ? (q[wi] >> off) : __funnelshift_r(q[wi], q[wi + 1], off)) & 63u;
+                        A[k] = mul_bf16x2(pairv[v], scale2[(sc >> (8 * (k >> 3))) & 0xffu]);
+                    }
+                } else {
+                    // 64 codes = 32 bytes; byte k holds columns 2k, 2k+1
+#pragma unroll
+                    for (int k = 0; k < 32; ++k)
+                        A[k] = mul_bf16x2(pairv[(q[k >> 2] >> (8 * (k & 3))) & 0xffu],
+                                          scale2[(sc >> (8 * (k >> 3))) & 0xffu]);
+                }
+                tmem_st32(tbase + lane_addr + a_col0 + (uint32_t)(sa * 32), A);
                 tmem_st_wait();
                 tc_fence_before();
-                mbar_arrive(a_full((i * kSub + half + 2) % C::kAStages));
+                mbar_arrive(a_full(sa));
             }
-            if (!ok || half != 0) continue;
+            if (!ok || group >= C::kEpiGroups) continue;
 
-            // ---------------- epilogue (half 0: warps 0-3, thread r = row r)
+            // ---------------- epilogue: group g reads D columns [g*N/G, (g+1)*N/G)
+            // (thread r = row r), frees D, then writes y
             const int buf = seg % C::kDBuf;
             ok = __all_sync(0xffffffffu, mbar_wait(d_full(buf), (seg / C::kDBuf) & 1));
             if (!ok) break;
@@ -586,17 +569,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t d_addr = tbase + lane_addr + (uint32_t)(buf * N);
             const float bias = (p.bias && row < p.oc) ? load_as_float(p.bias, p.bias_dtype, row) : 0.0f;
             if (sg.ka == 0 && sg.kb == p.n_kc) {
-                for (int c = 0; c < N; c += 16) {
-                    float v[16];
-                    tmem_ld16(d_addr + c, v);
-                    if (row < p.oc)
+                constexpr int kCols = N / C::kEpiGroups;
+                const int c0 = group * kCols;
+                float v[kCols];
 #pragma unroll
-                        for (int t = 0; t < 16; ++t)
-                            if (c + t < mcount)
-                                store_from_float(p.y, p.y_dtype, (int64_t)(m0 + c + t) * p.ldy + row, v[t] + bias);
-                }
+                for (int c = 0; c < kCols; c += 16) tmem_ld16(d_addr + c0 + c, v + c);
                 tc_fence_before();
                 mbar_arrive(d_empty(buf));
+                if (row < p.oc)
+#pragma unroll
+                    for (int t = 0; t < kCols; ++t)
+                        if (c0 + t < mcount)
+                            store_from_float(p.y, p.y_dtype, (int64_t)(m0 + c0 + t) * p.ldy + row, v[t] + bias);
             } else if constexpr (N == 16) {
                 // Partial sum (stream-K, N = 16): publish it; per 32-row slice,
                 // the warp that arrives last over all contributors adds every
@@ -728,15 +712,15 @@ int launch_n(int N, const CUtensorMap& wmap, const CUtensorMap& smap, const CUte
     }
 }
 
-// Tokens per tile.  Above 128 tokens: 256 unless 128-token tiles need
-// noticeably fewer token-rows per CTA once whole jobs are dealt out in rounds
-// (a 128-wide MMA runs ~15% below the 256-wide one per flop).
+// Tokens per tile.  Above 128 tokens: 256 unless 128-token tiles need far
+// fewer token-rows per CTA once whole jobs are dealt out in rounds (per flop
+// a 128-token tile runs ~35% slower: the same decode feeds half the MMA work).
 int token_tile(int64_t M, int64_t n_rb, int ctas) {
     if (M <= 16) return 16;
     if (M <= 64) return 64;
     if (M <= 128) return 128;
     auto rounds = [&](int64_t n) { return (n_rb * ((M + n - 1) / n) + ctas - 1) / ctas; };
-    return (double)rounds(128) * 128 * 1.15 < (double)rounds(256) * 256 ? 128 : 256;
+    return (double)rounds(128) * 128 * 1.4 < (double)rounds(256) * 256 ? 128 : 256;
 }
 
 }  // namespace tc
