@@ -115,6 +115,18 @@ SPARK_API int spark_twofour_unpack(const uint8_t* packed, int64_t n_elements, vo
 /* two_four_fake_quant -- 01_core/two_four.py:70 (TwoFourSTE backward is the identity, :65-67). */
 SPARK_API int spark_twofour_fake_quant(const void* w, int w_dtype, int64_t n, void* out, int out_dtype, void* stream);
 
+/* ---------------------------------------------------------------- INT8 (lm_head tier) */
+/* int8_fake_quant -- 01_core/int8_emu.py:12 (INT8STE backward is the identity, :26-27):
+ * per-row symmetric, scale = max(amax/127, 1e-12), q = clamp(round(w/scale), +-127). */
+SPARK_API int spark_int8_fake_quant(const void* w, int w_dtype, int64_t oc, int64_t ic, void* out, int out_dtype,
+                                    void* stream);
+/* ptq_int8_pack -- 01_core/int8_emu.py:37: q int8 [oc, ic], scale fp32 [oc]. */
+SPARK_API int spark_int8_pack(const void* w, int w_dtype, int64_t oc, int64_t ic, int8_t* q, float* scale,
+                              void* stream);
+/* ptq_int8_unpack -- 01_core/int8_emu.py:49: out = q * scale[row]. */
+SPARK_API int spark_int8_unpack(const int8_t* q, const float* scale, int64_t oc, int64_t ic, void* out, int out_dtype,
+                                void* stream);
+
 /* ---------------------------------------------------------------- linear */
 /* y[M, oc] = x[M, ic] . decode(W)^T (+ bias), fp32 accumulation.
  * Replaces spark_v3_spfp2_linear_forward / spark_v3_spfp2_forward

@@ -68,6 +68,8 @@ def lib():
             "spo_cpu_fp3_linear": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i64, _f32p]),
             "spo_cpu_nvfp4_linear": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i64, _f32p]),
             "spo_center_thresholds": (ctypes.POINTER(ctypes.c_uint32), []),
+            "spo_int8_fake_quant": (None, [_f32p, _i64, _i64, _f32p]),
+            "spo_int8_pack": (None, [_f32p, _i64, _i64, ctypes.POINTER(ctypes.c_int8), _f32p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -224,6 +226,26 @@ def nvfp4_fake_quant(w) -> np.ndarray:
     out = np.zeros((oc, ic), np.float32)
     lib().spo_nvfp4_fake_quant(_p(w, _f32p), oc, ic, _p(out, _f32p))
     return out
+
+
+# ---------------------------------------------------------------- INT8
+def int8_fake_quant(w) -> np.ndarray:
+    """int8_emu.py:12-18 (per-row symmetric INT8 round trip)."""
+    w = _f32(w)
+    oc, ic = w.shape
+    out = np.zeros((oc, ic), np.float32)
+    lib().spo_int8_fake_quant(_p(w, _f32p), oc, ic, _p(out, _f32p))
+    return out
+
+
+def ptq_int8_pack(w) -> tuple[np.ndarray, np.ndarray]:
+    """int8_emu.py:37-46: (q int8 [oc, ic], scale fp32 [oc])."""
+    w = _f32(w)
+    oc, ic = w.shape
+    q = np.zeros((oc, ic), np.int8)
+    scale = np.zeros(oc, np.float32)
+    lib().spo_int8_pack(_p(w, _f32p), oc, ic, _p(q, ctypes.POINTER(ctypes.c_int8)), _p(scale, _f32p))
+    return q, scale
 
 
 # ---------------------------------------------------------------- 2:4

@@ -728,3 +728,44 @@ SPO_API void spo_cpu_nvfp4_linear(const uint8_t* codes, const uint8_t* scales, c
         for (int64_t m = 0; m < mm; ++m) y[m * oc + r] = acc[m];
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* per-channel symmetric INT8 -- int8_emu.py                                 */
+/* ------------------------------------------------------------------------ */
+/* int8_emu.py:15 / :43: scale = (|w|.amax(dim=1) / 127).clamp_min(1e-12); a NaN
+ * in the row makes amax (and the scale) NaN, as torch.amax propagates NaN. */
+static float int8_scale(const float* row, int64_t ic) {
+    float amax = 0.0f;
+    int nan = 0;
+    for (int64_t c = 0; c < ic; ++c) {
+        float a = fabsf(row[c]);
+        if (a != a) nan = 1;
+        else if (a > amax) amax = a;
+    }
+    if (nan) return NAN;
+    float s = amax / 127.0f;
+    return s < 1e-12f ? 1e-12f : s;
+}
+
+/* :16 / :44: torch.round (half to even) of w / scale, clamp to +-127 (NaN stays) */
+static float int8_q(float v, float s) {
+    float q = nearbyintf(v / s);
+    return q < -127.0f ? -127.0f : (q > 127.0f ? 127.0f : q);
+}
+
+/* int8_fake_quant -- int8_emu.py:12-18 */
+SPO_API void spo_int8_fake_quant(const float* w, int64_t oc, int64_t ic, float* out) {
+    for (int64_t r = 0; r < oc; ++r) {
+        float s = int8_scale(w + r * ic, ic);
+        for (int64_t c = 0; c < ic; ++c) out[r * ic + c] = int8_q(w[r * ic + c], s) * s;
+    }
+}
+
+/* ptq_int8_pack -- int8_emu.py:37-46 (rows without NaN) */
+SPO_API void spo_int8_pack(const float* w, int64_t oc, int64_t ic, int8_t* q, float* scale) {
+    for (int64_t r = 0; r < oc; ++r) {
+        float s = int8_scale(w + r * ic, ic);
+        scale[r] = s;
+        for (int64_t c = 0; c < ic; ++c) q[r * ic + c] = (int8_t)(int)int8_q(w[r * ic + c], s);
+    }
+}

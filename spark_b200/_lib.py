@@ -59,6 +59,9 @@ _SIGNATURES = {
     "spark_twofour_pack": (_i, [_p, _i, _i64, _i64, _p, _p]),
     "spark_twofour_unpack": (_i, [_p, _i64, _p, _i, _p]),
     "spark_twofour_fake_quant": (_i, [_p, _i, _i64, _p, _i, _p]),
+    "spark_int8_fake_quant": (_i, [_p, _i, _i64, _i64, _p, _i, _p]),
+    "spark_int8_pack": (_i, [_p, _i, _i64, _i64, _p, _p, _p]),
+    "spark_int8_unpack": (_i, [_p, _p, _i64, _i64, _p, _i, _p]),
     "spark_linear_workspace_size": (_sz, [_i, _i64, _i64, _i64]),
     "spark_linear": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p]),
     "spark_linear_noalloc": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p]),

@@ -23,6 +23,19 @@ _FMT_KEYS = {
 }
 
 
+def fp3_nibbles_to_3bit(codes: torch.Tensor, n: int) -> torch.Tensor:
+    """FP3 nibble codes (fp3_emu.fp3_pack, element 2j in the low nibble) to the
+    3-bit layout (fp3_emu.fp3_pack_3bit: 8 codes in 3 bytes, code i at bit 3i),
+    once at load time."""
+    c = codes.view(torch.uint8).to(torch.int32)
+    flat = torch.stack([c & 7, (c >> 4) & 7], dim=1).reshape(-1)[:n]
+    if n % 8:
+        flat = torch.nn.functional.pad(flat, (0, 8 - n % 8))
+    g = flat.view(-1, 8)
+    word = (g << torch.arange(0, 24, 3, device=g.device, dtype=torch.int32)).sum(dim=1)
+    return torch.stack([word & 0xFF, (word >> 8) & 0xFF, (word >> 16) & 0xFF], dim=1).reshape(-1).to(torch.uint8)
+
+
 class V3PackedLinear(nn.Module):
     """y = x . decode(W)^T + bias with W kept packed in HBM.
 
@@ -58,6 +71,9 @@ class V3PackedLinear(nn.Module):
         oc, ic = (int(v) for v in state[name + "_meta"][:2])
         packed = state[name + codes_key].to(device)
         scales = state[name + scales_key].to(device) if scales_key else None
+        n = oc * ((ic + 15) // 16) * 16
+        if fmt == "fp3" and packed.numel() == (n + 1) // 2:
+            packed = fp3_nibbles_to_3bit(packed, n)
         b = state.get(f"param::{name}.bias")
         return cls(fmt, packed, oc, ic, scales=scales, bias=b.to(device) if b is not None else None)
 

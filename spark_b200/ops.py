@@ -189,6 +189,35 @@ def twofour_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
     return _home(out, w)
 
 
+# ------------------------------------------------------------------ INT8
+def int8_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    """int8_fake_quant: per-row symmetric INT8 round trip (fp32 out by default)."""
+    x = _cuda(w.detach())
+    oc, ic = x.shape
+    out = torch.empty(oc, ic, dtype=out_dtype or torch.float32, device=x.device)
+    call("spark_int8_fake_quant", _p(x), _dt(x), oc, ic, _p(out), _dt(out), _stream(x))
+    return _home(out, w)
+
+
+def int8_pack(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """ptq_int8_pack: (q int8 [oc, ic], scale fp32 [oc])."""
+    x = _cuda(w.detach())
+    oc, ic = x.shape
+    q = torch.empty(oc, ic, dtype=torch.int8, device=x.device)
+    scale = torch.empty(oc, dtype=torch.float32, device=x.device)
+    call("spark_int8_pack", _p(x), _dt(x), oc, ic, _p(q), _p(scale), _stream(x))
+    return _home(q, w), _home(scale, w)
+
+
+def int8_unpack(q: torch.Tensor, scale: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
+    """ptq_int8_unpack: q * scale[row]."""
+    qq, s = _cuda(q), _cuda(scale.float())
+    oc, ic = qq.shape
+    out = torch.empty(oc, ic, dtype=dtype, device=qq.device)
+    call("spark_int8_unpack", _p(qq), _p(s), oc, ic, _p(out), _DT[dtype], _stream(qq))
+    return _home(out, q)
+
+
 # ------------------------------------------------------------------ linear
 _ws_lock = threading.Lock()
 _ws: dict[tuple[int, int], torch.Tensor] = {}

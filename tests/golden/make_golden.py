@@ -28,6 +28,7 @@ import block_fp2_emu as fp2  # noqa: E402
 import fp3_emu  # noqa: E402
 import nvfp4_emu  # noqa: E402
 import two_four  # noqa: E402
+import int8_emu  # noqa: E402
 
 OUT = os.path.dirname(os.path.abspath(__file__))
 META = dict(torch_version=torch.__version__,
@@ -244,6 +245,27 @@ def gen_two_four():
     save("two_four.npz", **out)
 
 
+def gen_int8():
+    """int8_emu: per-row symmetric INT8 (lm_head tier).  Rows: Gaussian, huge,
+    tiny (scale clamps at 1e-12), all-zero, exact .5 ties of w/scale, a NaN row."""
+    gen = torch.Generator().manual_seed(8)
+    w = torch.randn(24, 200, generator=gen) * 0.02
+    w[1] *= 1e4
+    w[2] *= 1e-12
+    w[3] = 0.0
+    w[4] = torch.arange(200, dtype=torch.float32) * 0.5 - 50.0       # scale 0.3937..: many near-ties
+    w[5, :] = torch.tensor([(k + 0.5) for k in range(-100, 100)], dtype=torch.float32) * (1.0 / 127.0) * 99.5 / 99.5
+    w[6, 7] = float("nan")
+    out = {"w": npy(w), "fq": npy(int8_emu.int8_fake_quant(w))}
+    wp = w[torch.arange(24) != 6]
+    q, scale = int8_emu.ptq_int8_pack(wp)
+    out.update(w_pack=npy(wp), q=npy(q), scale=npy(scale), unpack=npy(int8_emu.ptq_int8_unpack(q, scale)))
+    g2 = torch.Generator().manual_seed(9)
+    wb = (torch.randn(16, 96, generator=g2) * 0.05).bfloat16()
+    out.update(w_bf16_bits=npy(wb.view(torch.int16)), fq_bf16_in=npy(int8_emu.int8_fake_quant(wb)))
+    save("int8.npz", **out)
+
+
 def gen_thresholds():
     save("thresholds.npz", center_t=np.array(CENTER_T, np.uint32))
 
@@ -253,3 +275,4 @@ if __name__ == "__main__":
     gen_spfp2()
     gen_fp3_nvfp4()
     gen_two_four()
+    gen_int8()

@@ -173,3 +173,23 @@ def test_two_four_full_down_proj_vs_oracle():
     p = ops().twofour_pack(W.cuda())
     assert np.array_equal(host(p), O.two_four_pack(W.numpy()))
     assert same_bits(host(ops().twofour_fake_quant(W.cuda())), O.two_four_fake_quant(W.numpy()))
+
+
+# ----------------------------------------------------------------- INT8
+def test_int8_golden_gpu():
+    g = load("int8.npz")
+    fq = host(ops().int8_fake_quant(cuda(g["w"])))
+    assert same_values(fq, g["fq"])
+    assert same_bits(fq[np.arange(24) != 6], g["fq"][np.arange(24) != 6])
+    q, scale = ops().int8_pack(cuda(g["w_pack"]))
+    assert np.array_equal(host(q), g["q"]) and same_bits(host(scale), g["scale"])
+    assert same_bits(host(ops().int8_unpack(q, scale)), g["unpack"])
+    wb = cuda(g["w_bf16_bits"]).view(torch.bfloat16)
+    assert same_bits(host(ops().int8_fake_quant(wb)), g["fq_bf16_in"])
+
+
+def test_int8_full_size_vs_oracle():
+    gen = torch.Generator().manual_seed(12)
+    w = torch.randn(2560, 4096, generator=gen) * 0.02
+    fq = host(ops().int8_fake_quant(w.cuda()))
+    assert same_bits(fq, O.int8_fake_quant(w.numpy()))

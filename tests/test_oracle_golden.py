@@ -191,3 +191,16 @@ def test_two_four_pack_unpack(name):
 def test_two_four_random_bytes():
     g = load("two_four.npz")
     assert same_bits(O.two_four_unpack(g["rnd_bytes"], 33 * 32), g["rnd_bytes_dec"])
+
+
+# ----------------------------------------------------------------- INT8
+def test_int8_golden():
+    """int8_emu (lm_head tier): fake-quant incl. a NaN row, PTQ pack / unpack."""
+    g = load("int8.npz")
+    assert same_values(O.int8_fake_quant(g["w"]), g["fq"])
+    assert same_bits(O.int8_fake_quant(g["w"])[np.arange(24) != 6], g["fq"][np.arange(24) != 6])
+    q, scale = O.ptq_int8_pack(g["w_pack"])
+    assert np.array_equal(q, g["q"]) and same_bits(scale, g["scale"])
+    assert same_bits(q.astype(np.float32) * scale[:, None], g["unpack"])
+    wb = torch.from_numpy(g["w_bf16_bits"]).view(torch.bfloat16).float().numpy()
+    assert same_bits(O.int8_fake_quant(wb), g["fq_bf16_in"])
