@@ -444,6 +444,85 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+TP_LAYERS, TP_H, TP_I, TP_M = 32, 4096, 12288, 64
+
+
+def run_tp_mlp(args, rank, world, local):
+    """a 32-layer SPFP2 MLP stack (hidden 4096, intermediate
+    12288, N(0, 0.015) weights, SiLU(gate) * up), 64 bf16 tokens, tensor-
+    parallel over the `world` ranks (gate/up column-parallel, down row-parallel
+    + one NCCL all-reduce per layer).  Prints its own JSON line."""
+    from spark_b200 import ops
+    from spark_b200.tp import TPMLP
+    device = torch.device("cuda", local)
+    g = torch.Generator(device=device)
+    layers = []
+    for li in range(TP_LAYERS):
+        g.manual_seed(4000 + li)
+        gate = torch.randn(TP_I, TP_H, device=device, generator=g) * 0.015
+        up = torch.randn(TP_I, TP_H, device=device, generator=g) * 0.015
+        down = torch.randn(TP_H, TP_I, device=device, generator=g) * 0.015
+        layers.append(TPMLP(gate, up, down, rank, world))
+        del gate, up, down
+    g.manual_seed(4)
+    x0 = torch.randn(TP_M, TP_H, device=device, generator=g).bfloat16()
+    stream = torch.cuda.Stream(device)
+    out = {}
+
+    def step():
+        x = x0
+        for layer in layers:
+            x = layer(x)
+        out["y"] = x
+
+    with torch.cuda.stream(stream):
+        step()
+        step()
+    torch.cuda.synchronize()
+    graph = None
+    if args.tp_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
+    k = max(5, args.steps // 10)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            run()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(k):
+            run()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    finite = bool(torch.isfinite(out["y"].float()).all().item())
+    ops.check_device_errors()
+    barrier(world)
+    del graph
+    packed_total = TP_LAYERS * 3 * (TP_I * TP_H // 16 * 5)
+    peak, peak_kind = peaks()
+    sec = ms * 1e-3 / k
+    line = {"metric": "config-4 tensor-parallel SPFP2 MLP stack", "n_gpus": world, "steps": k,
+            "ms_per_step": round(ms / k, 4), "tokens_per_s": round(TP_M / sec, 1),
+            "weight_GBps_total": round(packed_total / sec / 1e9, 1),
+            "roofline": {"bound": "hbm", "achieved": round(packed_total / world / sec / 1e9, 1), "peak": peak,
+                         "unit": "GB/s per GPU", "frac": round(packed_total / world / sec / 1e9 / peak, 4),
+                         "peak_source": peak_kind},
+            "config": {"workload": "BASELINE config 4: 32 x (gate/up [12288,4096], down [4096,12288]) SPFP2, "
+                                   "N(0,0.015), M=64 bf16, SiLU(gate)*up", "tp": world,
+                       "parallelism": f"tp{world}: gate/up column-parallel, down row-parallel + NCCL all-reduce",
+                       "graph": bool(args.tp_graph)},
+            "finite": finite}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_profile(args):
     """Timing of one linear shape on its own (also the target of ncu captures).
 
@@ -526,6 +605,8 @@ def main():
     ap.add_argument("--path", default="tiled", choices=["tiled", "tc", "plain"],
                     help="profile mode: tiled-layout GEMV, tcgen05 kernel, or reference-layout GEMV")
     ap.add_argument("--copies", type=int, default=0, help="profile mode: weight copies to rotate over")
+    ap.add_argument("--tp-mlp", action="store_true", help="run the config-4 tensor-parallel MLP stack instead")
+    ap.add_argument("--tp-graph", type=int, default=1, help="tp-mlp: replay each step as a CUDA graph")
     ap.add_argument("--oc", type=int, default=0, help="profile mode: output features")
     ap.add_argument("--ic", type=int, default=0, help="profile mode: input features")
     args = ap.parse_args()
@@ -540,7 +621,10 @@ def main():
         return
     rank, world, local = dist_setup(args.gpus)
     try:
-        run_gpu(args, rank, world, local)
+        if args.tp_mlp:
+            run_tp_mlp(args, rank, world, local)
+        else:
+            run_gpu(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist

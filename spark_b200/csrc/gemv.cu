@@ -1200,10 +1200,11 @@ extern "C" {
 
 size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int64_t ic) {
     (void)fmt;
-    (void)M;
+    (void)oc;
     int dev = 0;
     cudaGetDevice(&dev);
-    return ws_layout(ic, max_warps(dev)).total;
+    const WsLayout L = ws_layout(ic, max_warps(dev));
+    return std::max(L.total, L.partials + tc_partials_bytes(dev, M));
 }
 
 int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,

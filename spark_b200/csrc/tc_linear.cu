@@ -79,13 +79,20 @@ struct Cfg {
     // L2 and feed the tensor core directly, so big token tiles get the room.
     static constexpr int kWStages = N >= 128 ? 3 : 6;
     // A stages (64 columns each) and the D buffers share the CTA's TMEM.
-    static constexpr int kAStages = N == 16 ? 6 : 8;
+    static constexpr int kAStages = N == 16 ? 12 : 8;
     static constexpr int kDBuf = N <= 128 ? 2 : 1;
+    // Independent accumulators per D buffer: MMA kk of every 64-column step
+    // adds into chain kk % kChains, so small-N MMAs do not wait on one
+    // another's accumulator; the epilogue sums the chains (fixed order).
+    static constexpr int kChains = N == 16 ? 4 : (N == 64 ? 2 : 1);
+    static constexpr int kDStride = kChains * N;         // columns of one D buffer
     // decode groups that drain D after a job (each a slice of the N columns)
     static constexpr int kEpiGroups = N >= 64 ? 4 : 1;
-    static constexpr int kDCols = kDBuf * N;
+    static constexpr int kDCols = kDBuf * kDStride;
     static constexpr uint32_t kTmemCols = kDCols + kAStages * 32 <= 256 ? 256u : 512u;
-    static constexpr int kXStages = N <= 64 ? 8 : (N == 128 ? 10 : 5);
+    // x tiles are small for decode-sized token tiles and latency-bound from
+    // L2: keep many in flight
+    static constexpr int kXStages = N == 16 ? 32 : (N == 64 ? 12 : (N == 128 ? 10 : 5));
     static constexpr int kXBytes = N * 128;                  // N rows x 64 bf16
     // dynamic shared memory (offsets from a 1024-aligned base)
     static constexpr int kX = 0;
@@ -451,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = mbar_wait(d_empty(buf), ((seg / C::kDBuf) & 1) ^ 1);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tbase + (uint32_t)(buf * N);
+                const uint32_t d_tmem = tbase + (uint32_t)(buf * C::kDStride);
                 for (int kc = sg.ka; kc < sg.kb && ok; ++kc, ++i) {
                     for (int j = 0; j < kSub; ++j) {
                         const int ia = i * kSub + j, sa = ia % C::kAStages, sx = ia % C::kXStages;
@@ -462,8 +469,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t xb = smem_u32(smem + C::kX + sx * C::kXBytes);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            mma_ts(d_tmem, tbase + a_col0 + (uint32_t)(sa * 32 + kk * 8), sdesc_sw128(xb + kk * 32),
-                                   idesc, (kc == sg.ka && j == 0 && kk == 0) ? 0u : 1u);
+                            mma_ts(d_tmem + (uint32_t)((kk % C::kChains) * N), tbase + a_col0 + (uint32_t)(sa * 32 + kk * 8),
+                                   sdesc_sw128(xb + kk * 32), idesc,
+                                   (kc == sg.ka && j == 0 && kk < C::kChains) ? 0u : 1u);
                         mma_commit(a_empty(sa));
                         mma_commit(x_empty(sx));
                     }
@@ -566,14 +574,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t row = (int64_t)rb * kRows + r;
             const int m0 = tb * N;
             const int mcount = min(N, p.M - m0);
-            const uint32_t d_addr = tbase + lane_addr + (uint32_t)(buf * N);
+            const uint32_t d_addr = tbase + lane_addr + (uint32_t)(buf * C::kDStride);
+            // 16 accumulator columns, summed over the chains
+            auto ld_sum16 = [&](uint32_t addr, float* v) {
+                tmem_ld16(addr, v);
+#pragma unroll
+                for (int ch = 1; ch < C::kChains; ++ch) {
+                    float w[16];
+                    tmem_ld16(addr + (uint32_t)(ch * N), w);
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) v[t] += w[t];
+                }
+            };
             const float bias = (p.bias && row < p.oc) ? load_as_float(p.bias, p.bias_dtype, row) : 0.0f;
             if (sg.ka == 0 && sg.kb == p.n_kc) {
                 constexpr int kCols = N / C::kEpiGroups;
                 const int c0 = group * kCols;
                 float v[kCols];
 #pragma unroll
-                for (int c = 0; c < kCols; c += 16) tmem_ld16(d_addr + c0 + c, v + c);
+                for (int c = 0; c < kCols; c += 16) ld_sum16(d_addr + c0 + c, v + c);
                 tc_fence_before();
                 mbar_arrive(d_empty(buf));
                 if (row < p.oc)
@@ -581,48 +600,53 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int t = 0; t < kCols; ++t)
                         if (c0 + t < mcount)
                             store_from_float(p.y, p.y_dtype, (int64_t)(m0 + c0 + t) * p.ldy + row, v[t] + bias);
-            } else if constexpr (N == 16) {
-                // Partial sum (stream-K, N = 16): publish it; per 32-row slice,
-                // the warp that arrives last over all contributors adds every
-                // contributor's partial in CTA order (same order on every call).
+            } else if constexpr (N <= 64) {
+                // Partial sum (stream-K): each group publishes its 16-token slice;
+                // per (slice, 32-row quadrant), the warp that arrives last over
+                // all contributors adds every contributor's partial in CTA order
+                // (the same order on every call).
+                constexpr int kCols = N / C::kEpiGroups;
+                static_assert(kCols == 16, "one 16-token slice per epilogue group");
+                const int c0 = group * kCols;
                 const int slot = 2 * cta + (seg == 0 ? 0 : 1);
-                float* mine = p.partials + (int64_t)slot * N * kRows + r;
-                for (int c = 0; c < N; c += 16) {
+                float* mine = p.partials + ((int64_t)slot * N + c0) * kRows + r;
+                {
                     float v[16];
-                    tmem_ld16(d_addr + c, v);
+                    ld_sum16(d_addr + c0, v);
+                    tc_fence_before();
+                    mbar_arrive(d_empty(buf));
 #pragma unroll
-                    for (int t = 0; t < 16; ++t) __stcg(mine + (c + t) * kRows, v[t]);
+                    for (int t = 0; t < 16; ++t) __stcg(mine + t * kRows, v[t]);
                 }
-                tc_fence_before();
-                mbar_arrive(d_empty(buf));
                 __threadfence();
                 __syncwarp();
                 const int job_u0 = job * p.n_kc;
                 const int cA = unit_owner(job_u0, p), cB = unit_owner(job_u0 + p.n_kc - 1, p);
+                int* counter = p.counters + ((int64_t)job * C::kEpiGroups + group) * 4 + quad;
                 int last = 0;
-                if (lane == 0) last = atomic_add_acq_rel(p.counters + 4 * job + quad, 1) == cB - cA;
+                if (lane == 0) last = atomic_add_acq_rel(counter, 1) == cB - cA;
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     __threadfence();
                     if (row < p.oc) {
-                        float acc[N];
+                        float acc[16];
 #pragma unroll
-                        for (int t = 0; t < N; ++t) acc[t] = 0.0f;
+                        for (int t = 0; t < 16; ++t) acc[t] = 0.0f;
                         for (int cc = cA; cc <= cB; ++cc) {
                             const int sl = 2 * cc + (unit_begin(cc, p) >= job_u0 ? 0 : 1);
-                            const float* src = p.partials + (int64_t)sl * N * kRows + r;
-                            float v[N];
+                            const float* src = p.partials + ((int64_t)sl * N + c0) * kRows + r;
+                            float v[16];
 #pragma unroll
-                            for (int t = 0; t < N; ++t) v[t] = t < mcount ? __ldcg(src + t * kRows) : 0.0f;
+                            for (int t = 0; t < 16; ++t) v[t] = c0 + t < mcount ? __ldcg(src + t * kRows) : 0.0f;
 #pragma unroll
-                            for (int t = 0; t < N; ++t) acc[t] += v[t];
+                            for (int t = 0; t < 16; ++t) acc[t] += v[t];
                         }
 #pragma unroll
-                        for (int t = 0; t < N; ++t)
-                            if (t < mcount)
-                                store_from_float(p.y, p.y_dtype, (int64_t)(m0 + t) * p.ldy + row, acc[t] + bias);
+                        for (int t = 0; t < 16; ++t)
+                            if (c0 + t < mcount)
+                                store_from_float(p.y, p.y_dtype, (int64_t)(m0 + c0 + t) * p.ldy + row, acc[t] + bias);
                     }
-                    if (lane == 0) p.counters[4 * job + quad] = 0;
+                    if (lane == 0) *counter = 0;
                 }
             }
         }
@@ -726,10 +750,11 @@ int token_tile(int64_t M, int64_t n_rb, int ctas) {
 }  // namespace tc
 
 // Workspace bytes of the tcgen05 path beyond the error word and counters:
-// two partial slots of 16 x 128 fp32 per CTA (stream-K runs only for M <= 16).
+// two partial slots of N x 128 fp32 per CTA (stream-K runs for 16- and
+// 64-token tiles).
 size_t tc_partials_bytes(int dev, int64_t M) {
-    (void)M;
-    return (size_t)2 * tc::sm_count_cached(dev) * 16 * tc::kRows * sizeof(float);
+    const int64_t n = M <= 16 ? 16 : 64;
+    return (size_t)2 * tc::sm_count_cached(dev) * n * tc::kRows * sizeof(float);
 }
 
 bool tc_linear_ok(int fmt, const void* wq, const void* scales, const void* x, int x_dtype, int64_t ic,
@@ -741,7 +766,7 @@ bool tc_linear_ok(int fmt, const void* wq, const void* scales, const void* x, in
 }
 
 // Linear through k_tc_linear (SPFP2, FP3 or NVFP4, reference layouts).
-// `counters` must hold max_counters zero ints (4 per job are used);
+// `counters` must hold max_counters zero ints (up to 16 per job are used);
 // `partials` tc_partials_bytes(dev, M) bytes.
 int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int64_t M, int64_t oc, int64_t ic,
               int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err,
@@ -757,8 +782,8 @@ int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, 
     const int N = tc::token_tile(M, n_rb, ctas);
     const int64_t n_tb = (M + N - 1) / N;
     const int64_t jobs = n_rb * n_tb;
-    SPARK_REQUIRE(4 * jobs <= max_counters, SPARK_ERR_UNSUPPORTED, "tcgen05 path: %lld jobs above %lld",
-                  (long long)jobs, (long long)(max_counters / 4));
+    SPARK_REQUIRE(16 * jobs <= max_counters, SPARK_ERR_UNSUPPORTED, "tcgen05 path: %lld jobs above %lld",
+                  (long long)jobs, (long long)(max_counters / 16));
     const int64_t units = jobs * n_kc;
     SPARK_REQUIRE(units < (1ll << 31) / 1024, SPARK_ERR_UNSUPPORTED, "tcgen05 path: problem too large");
     const int code_bytes = fmt == SPARK_FMT_SPFP2 ? 80 : (fmt == SPARK_FMT_FP3 ? 96 : 128);
@@ -793,7 +818,7 @@ int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, 
     p.units = (int)units;
     // Decode: units split evenly over the CTAs (stream-K, 16-token partials).
     // Larger token tiles: whole jobs in turn, no partial sums.
-    p.stream_k = N == 16 ? 1 : 0;
+    p.stream_k = (N == 16 || (N == 64 && jobs < ctas)) ? 1 : 0;
     p.grid = (int)(p.stream_k ? std::min<int64_t>(units, ctas) : std::min<int64_t>(jobs, ctas));
     p.bias_dtype = bias_dtype;
     p.y_dtype = y_dtype;

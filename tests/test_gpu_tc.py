@@ -147,3 +147,9 @@ def test_tc_activation_range(fmt):
         y64 = O.linear_f64(x.float().numpy(), dec)
         rel = np.abs(y - y64).max() / max(np.abs(y64).max(), 1e-30)
         assert rel < 1e-5, (fmt, scale, rel)
+
+
+@pytest.mark.parametrize("oc,ic", [(1536, 4096), (4096, 1536), (12288, 4096)])
+def test_tc_config4_shapes_m64(oc, ic):
+    """Config-4 shards at M = 64: 64-token stream-K with partial sums."""
+    check_oracle(oc, ic, 64, seed=oc)
