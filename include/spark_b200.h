@@ -168,6 +168,40 @@ SPARK_API int spark_linear_noalloc(int fmt, const uint8_t* wq, const uint8_t* sc
                                    int64_t M, int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype,
                                    void* y, int y_dtype, int64_t ldy, void* stream);
 
+/* A chain of dependent decode-step ops in ONE persistent launch: dequant
+ * linears (SPFP2 / FP3 / NVFP4 reference layouts, bf16 x, M <= 16 tokens) and
+ * SiLU(gate) * up.  It replaces a sequence of spark_linear / spark_silu_mul
+ * calls (a layer's q/k/v -> o -> gate/up -> SiLU -> down, as the reference
+ * model runs them one by one); no counterpart in the reference.  dep[] names
+ * the earlier ops whose output the op reads (-1: none): the op's input is
+ * loaded only after they complete, while its weights stream and decode
+ * earlier.  Up to 16 ops; the launch is cooperative (one CTA per SM).
+ *   linear:   fmt, wq, scales, x [M, ic] (row stride ldx), oc, bias, y [M, oc]
+ *             (row stride ldy, y_dtype; bf16 when a later op reads it)
+ *   silu_mul: x = gate, x2 = up, y = out, all bf16 [M, ic] contiguous
+ * workspace: spark_linear_chain_workspace_size(n_ops) bytes, 256-byte aligned,
+ * zero before its first use; launches that share it must not overlap. */
+#define SPARK_CHAIN_LINEAR 0
+#define SPARK_CHAIN_SILU_MUL 1
+typedef struct {
+    int kind;
+    int fmt;
+    const uint8_t* wq;
+    const uint8_t* scales;
+    const void* x;
+    const void* x2;
+    int64_t ic, ldx, oc;
+    const void* bias;
+    int bias_dtype;
+    void* y;
+    int y_dtype;
+    int64_t ldy;
+    int dep[2];
+} SparkChainOp;
+SPARK_API size_t spark_linear_chain_workspace_size(int n_ops);
+SPARK_API int spark_linear_chain(const SparkChainOp* ops, int n_ops, int64_t M, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* Fragment-major copy of a packed weight for spark_linear(fmt | SPARK_LAYOUT_TILED):
  * the same bytes (codes and, for FP3/NVFP4, scales) permuted so every thread of the
  * decode GEMV reads its MMA fragments with coalesced 16-byte loads.  No counterpart

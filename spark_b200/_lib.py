@@ -27,6 +27,17 @@ LAYOUT_TILED = 0x100
 PATH_TCGEN05 = 0x200
 
 
+CHAIN_LINEAR, CHAIN_SILU_MUL = 0, 1
+
+
+class SparkChainOp(ctypes.Structure):
+    """struct SparkChainOp of include/spark_b200.h."""
+    _fields_ = [("kind", ctypes.c_int), ("fmt", ctypes.c_int), ("wq", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+                ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p), ("ic", ctypes.c_int64), ("ldx", ctypes.c_int64),
+                ("oc", ctypes.c_int64), ("bias", ctypes.c_void_p), ("bias_dtype", ctypes.c_int),
+                ("y", ctypes.c_void_p), ("y_dtype", ctypes.c_int), ("ldy", ctypes.c_int64), ("dep", ctypes.c_int * 2)]
+
+
 class SparkError(RuntimeError):
     """A C-ABI call returned a non-zero status."""
 
@@ -64,6 +75,8 @@ _SIGNATURES = {
     "spark_int8_unpack": (_i, [_p, _p, _i64, _i64, _p, _i, _p]),
     "spark_linear_workspace_size": (_sz, [_i, _i64, _i64, _i64]),
     "spark_linear": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p]),
+    "spark_linear_chain_workspace_size": (_sz, [_i]),
+    "spark_linear_chain": (_i, [_p, _i, _i64, _p, _sz, _p]),
     "spark_linear_noalloc": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p]),
     "spark_workspace_check": (_i, [_p, _p]),
     "spark_tiled_bytes": (_sz, [_i, _i64, _i64]),

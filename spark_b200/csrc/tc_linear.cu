@@ -282,6 +282,68 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
     return d;
 }
 
+// One 64-column step (j) of row r of a weight stage: the packed bytes
+// (q, 5 / 6 / 8 words) and the step's four e4m3 scales (sc).
+template <int FMT>
+__device__ __forceinline__ void load_step(const uint8_t* stage, int r, int j, uint32_t* q, uint32_t& sc) {
+    using WF = Wfmt<FMT>;
+    if constexpr (FMT == SPARK_FMT_SPFP2) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(stage + r * WF::kCodeBytes) + 5 * j;
+#pragma unroll
+        for (int k = 0; k < 5; ++k) q[k] = src[k];
+    } else if constexpr (FMT == SPARK_FMT_FP3) {
+        const uint2* src = reinterpret_cast<const uint2*>(stage + r * 96 + 24 * j);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const uint2 v = src[k];
+            q[2 * k] = v.x;
+            q[2 * k + 1] = v.y;
+        }
+    } else {
+        // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 128 + 16 * ((2 * j + h) ^ (r & 7)));
+            q[4 * h] = v.x;
+            q[4 * h + 1] = v.y;
+            q[4 * h + 2] = v.z;
+            q[4 * h + 3] = v.w;
+        }
+    }
+    if constexpr (WF::kScaleBytes > 0)
+        sc = reinterpret_cast<const uint32_t*>(stage + kRows * WF::kCodeBytes + r * 16)[j];
+}
+
+// 64 weights of one row -> 32 bf16x2 registers in natural column order.
+template <int FMT>
+__device__ __forceinline__ void decode_step(const uint32_t* q, uint32_t sc, const uint4* lut, const uint32_t* scale2,
+                                            const uint32_t* pairv, uint32_t* A) {
+    if constexpr (FMT == SPARK_FMT_SPFP2) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t mw, eb;
+            if (k == 0) { mw = q[0]; eb = q[1] & 0xffu; }
+            else if (k == 1) { mw = __funnelshift_r(q[1], q[2], 8); eb = (q[2] >> 8) & 0xffu; }
+            else if (k == 2) { mw = __funnelshift_r(q[2], q[3], 16); eb = (q[3] >> 16) & 0xffu; }
+            else { mw = __funnelshift_r(q[3], q[4], 24); eb = q[4] >> 24; }
+            decode_pair(mw, lut[eb], A + 8 * k);
+        }
+    } else if constexpr (FMT == SPARK_FMT_FP3) {
+        // 64 codes = 192 bits; code pair k (columns 2k, 2k+1) at bit 6k
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+            const int bit = 6 * k, wi = bit >> 5, off = bit & 31;
+            const uint32_t v = (off <= 26 ? (q[wi] >> off) : __funnelshift_r(q[wi], q[wi + 1], off)) & 63u;
+            A[k] = mul_bf16x2(pairv[v], scale2[(sc >> (8 * (k >> 3))) & 0xffu]);
+        }
+    } else {
+        // 64 codes = 32 bytes; byte k holds columns 2k, 2k+1
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+            A[k] = mul_bf16x2(pairv[(q[k >> 2] >> (8 * (k & 3))) & 0xffu], scale2[(sc >> (8 * (k >> 3))) & 0xffu]);
+    }
+}
+
 // ------------------------------------------------------------------ kernel
 struct Params {
     const void* bias;
@@ -496,32 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint8_t* stage = smem + C::kW + sw * WF::kStageBytes;
                 uint32_t q[FMT == SPARK_FMT_SPFP2 ? 5 : (FMT == SPARK_FMT_FP3 ? 6 : 8)];
                 uint32_t sc = 0u;
-                if constexpr (FMT == SPARK_FMT_SPFP2) {
-                    const uint32_t* src = reinterpret_cast<const uint32_t*>(stage + r * WF::kCodeBytes) + 5 * group;
-#pragma unroll
-                    for (int k = 0; k < 5; ++k) q[k] = src[k];
-                } else if constexpr (FMT == SPARK_FMT_FP3) {
-                    const uint2* src = reinterpret_cast<const uint2*>(stage + r * 96 + 24 * group);
-#pragma unroll
-                    for (int k = 0; k < 3; ++k) {
-                        const uint2 v = src[k];
-                        q[2 * k] = v.x;
-                        q[2 * k + 1] = v.y;
-                    }
-                } else {
-                    // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint4 v =
-                            *reinterpret_cast<const uint4*>(stage + r * 128 + 16 * ((2 * group + h) ^ (r & 7)));
-                        q[4 * h] = v.x;
-                        q[4 * h + 1] = v.y;
-                        q[4 * h + 2] = v.z;
-                        q[4 * h + 3] = v.w;
-                    }
-                }
-                if constexpr (WF::kScaleBytes > 0)
-                    sc = reinterpret_cast<const uint32_t*>(stage + kRows * WF::kCodeBytes + r * 16)[group];
+                load_step<FMT>(stage, r, group, q, sc);
                 mbar_arrive(w_empty(sw));
 
                 const int ia = i * kSub + group, sa = ia % C::kAStages;
@@ -531,31 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 uint32_t A[32];
-                if constexpr (FMT == SPARK_FMT_SPFP2) {
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        uint32_t mw, eb;
-                        if (k == 0) { mw = q[0]; eb = q[1] & 0xffu; }
-                        else if (k == 1) { mw = __funnelshift_r(q[1], q[2], 8); eb = (q[2] >> 8) & 0xffu; }
-                        else if (k == 2) { mw = __funnelshift_r(q[2], q[3], 16); eb = (q[3] >> 16) & 0xffu; }
-                        else { mw = __funnelshift_r(q[3], q[4], 24); eb = q[4] >> 24; }
-                        decode_pair(mw, lut[eb], A + 8 * k);
-                    }
-                } else if constexpr (FMT == SPARK_FMT_FP3) {
-                    // 64 codes = 192 bits; code pair k (columns 2k, 2k+1) at bit 6k
-#pragma unroll
-                    for (int k = 0; k < 32; ++k) {
-                        const int bit = 6 * k, wi = bit >> 5, off = bit & 31;
-                        const uint32_t v = (off <= 26 ? (q[wi] >> off) : __funnelshift_r(q[wi], q[wi + 1], off)) & 63u;
-                        A[k] = mul_bf16x2(pairv[v], scale2[(sc >> (8 * (k >> 3))) & 0xffu]);
-                    }
-                } else {
-                    // 64 codes = 32 bytes; byte k holds columns 2k, 2k+1
-#pragma unroll
-                    for (int k = 0; k < 32; ++k)
-                        A[k] = mul_bf16x2(pairv[(q[k >> 2] >> (8 * (k & 3))) & 0xffu],
-                                          scale2[(sc >> (8 * (k >> 3))) & 0xffu]);
-                }
+                decode_step<FMT>(q, sc, lut, scale2, pairv, A);
                 tmem_st32(tbase + lane_addr + a_col0 + (uint32_t)(sa * 32), A);
                 tmem_st_wait();
                 tc_fence_before();
@@ -830,3 +843,513 @@ int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, 
 }
 
 }  // namespace spark
+
+// ====================================================================== chains
+// One persistent launch over a list of dependent ops (a decode step of a
+// layer stack): dequant linears with up to 16 tokens, and SiLU(gate) * up.
+// Every CTA takes part in every op (stream-K over the op's units, as the
+// single-op kernel does for 16-token tiles) and the stage rings run straight
+// across op boundaries, so the weights of the next op stream and decode
+// while the previous one finishes.  Op k is complete when its done counter
+// reaches its target (each CTA's epilogue warps add one after writing their
+// rows); an op that reads an earlier op's output waits, bounded, for that
+// count before its x tiles are loaded.  The launch is cooperative: every CTA
+// is resident, so the waits between CTAs always end.
+namespace spark {
+namespace tc {
+
+constexpr int kMaxOps = 16;
+constexpr int kCN = 16;                  // tokens per tile
+constexpr int kCWStage = 18432;          // largest weight stage (NVFP4: 128 x (128 + 16) B)
+constexpr int kCWStages = 6;
+constexpr int kCXStages = 32;
+constexpr int kCAStages = 12;
+constexpr int kCChains = 4;
+constexpr int kCDStride = kCChains * kCN;
+constexpr int kCDCols = 2 * kCDStride;
+constexpr uint32_t kCTmemCols = 512;
+static_assert(kCDCols + kCAStages * 32 <= 512, "TMEM budget");
+// dynamic shared memory
+constexpr int kCX = 0;
+constexpr int kCW = kCX + kCXStages * kCN * 128;
+constexpr int kCLut = kCW + kCWStages * kCWStage;       // SPFP2 table (4 KB)
+constexpr int kCScale = kCLut + 4096;                   // e4m3 -> bf16x2 (1 KB)
+constexpr int kCPair3 = kCScale + 1024;                 // FP3 code pairs (256 B)
+constexpr int kCPair4 = kCPair3 + 256;                  // NVFP4 code pairs (1 KB)
+constexpr int kCBar = kCPair4 + 1024;
+constexpr int kCNumBars = 2 * kCWStages + 2 * kCXStages + 2 * kCAStages + 4;
+constexpr int kCAlloc = kCBar + kCNumBars * 8 + 16 + 1024;
+static_assert(kCAlloc <= 232448, "chain kernel shared memory");
+
+struct ChainOp {
+    int kind;                // 0 linear, 1 silu_mul
+    int fmt, dep0, dep1, target;
+    int n_rb, n_kc, units, bias_dtype, y_dtype, stage_bytes;
+    int64_t oc, ldy, n;      // n: silu element count
+    const void* bias;
+    void* y;
+    const void* g;
+    const void* u;
+    float* partials;         // linear: [2 * grid][16][128]
+    int* counters;           // linear: [n_rb][4]
+};
+
+struct ChainProgram {
+    CUtensorMap wmap[kMaxOps], smap[kMaxOps], xmap[kMaxOps];
+    ChainOp op[kMaxOps];
+    int n_ops, grid, M;
+    int* done;               // [kMaxOps], zero at launch
+    int* err;
+};
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait for an op's completion count; false after kWaitNs.
+__device__ bool wait_done(const int* done, int k, int target) {
+    if (k < 0 || ld_acquire(done + k) >= target) return true;
+    const uint64_t deadline = globaltimer_ns() + kWaitNs;
+    while (ld_acquire(done + k) < target) {
+        if (globaltimer_ns() > deadline) return false;
+        __nanosleep(64);
+    }
+    return true;
+}
+
+__device__ __forceinline__ int op_unit_begin(int c, int units, int grid) {
+    return (int)(((int64_t)c * units) / grid);
+}
+__device__ __forceinline__ int op_unit_owner(int u, int units, int grid) {
+    return (int)((((int64_t)u + 1) * grid - 1) / units);
+}
+
+// Units of the linear ops of a chain, for this CTA, in program order.
+struct ChainUnits {
+    const ChainProgram* pr;
+    int cta, k, u, u1;
+    __device__ ChainUnits(const ChainProgram& p, int c) : pr(&p), cta(c), k(-1), u(0), u1(0) {}
+    // next (op, job, column block); false at the end
+    __device__ bool next(int& op, int& job, int& kc) {
+        while (u >= u1) {
+            if (++k >= pr->n_ops) return false;
+            const ChainOp& o = pr->op[k];
+            if (o.kind != 0) { u = u1 = 0; continue; }
+            u = op_unit_begin(cta, o.units, pr->grid);
+            u1 = op_unit_begin(cta + 1, o.units, pr->grid);
+        }
+        op = k;
+        job = u / pr->op[k].n_kc;
+        kc = u - job * pr->op[k].n_kc;
+        ++u;
+        return true;
+    }
+};
+
+template <int FMT>
+__device__ __forceinline__ void decode_op_step(const uint8_t* stage, int r, int j, const uint4* lut,
+                                               const uint32_t* scale2, const uint32_t* pair3, const uint32_t* pair4,
+                                               uint32_t* A) {
+    uint32_t q[FMT == SPARK_FMT_SPFP2 ? 5 : (FMT == SPARK_FMT_FP3 ? 6 : 8)];
+    uint32_t sc = 0u;
+    load_step<FMT>(stage, r, j, q, sc);
+    decode_step<FMT>(q, sc, lut, scale2, FMT == SPARK_FMT_FP3 ? pair3 : pair4, A);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_tc_chain(const __grid_constant__ ChainProgram pr) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint32_t tmem_base_s;
+    uint4* lut = reinterpret_cast<uint4*>(smem + kCLut);
+    uint32_t* scale2 = reinterpret_cast<uint32_t*>(smem + kCScale);
+    uint32_t* pair3 = reinterpret_cast<uint32_t*>(smem + kCPair3);
+    uint32_t* pair4 = reinterpret_cast<uint32_t*>(smem + kCPair4);
+    const uint32_t bar0 = smem_u32(smem + kCBar);
+    auto w_full = [&](int s) { return bar0 + 8u * s; };
+    auto w_empty = [&](int s) { return bar0 + 8u * (kCWStages + s); };
+    auto x_full = [&](int s) { return bar0 + 8u * (2 * kCWStages + s); };
+    auto x_empty = [&](int s) { return bar0 + 8u * (2 * kCWStages + kCXStages + s); };
+    auto a_full = [&](int s) { return bar0 + 8u * (2 * kCWStages + 2 * kCXStages + s); };
+    auto a_empty = [&](int s) { return bar0 + 8u * (2 * kCWStages + 2 * kCXStages + kCAStages + s); };
+    auto d_full = [&](int s) { return bar0 + 8u * (2 * kCWStages + 2 * kCXStages + 2 * kCAStages + s); };
+    auto d_empty = [&](int s) { return bar0 + 8u * (2 * kCWStages + 2 * kCXStages + 2 * kCAStages + 2 + s); };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kCWStages; ++s) { mbar_init(w_full(s), 1); mbar_init(w_empty(s), kDecThreads); }
+        for (int s = 0; s < kCXStages; ++s) { mbar_init(x_full(s), 1); mbar_init(x_empty(s), 1); }
+        for (int s = 0; s < kCAStages; ++s) { mbar_init(a_full(s), kRows); mbar_init(a_empty(s), 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(d_full(s), 1); mbar_init(d_empty(s), kRows); }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i < 256; i += kThreads) {
+        const uint2 a = exp_tables(i & 15), b = exp_tables(i >> 4);
+        lut[i] = make_uint4(a.x, a.y, b.x, b.y);
+        const uint32_t sb = bf16_bits(e4m3_to_f32((uint32_t)i));
+        scale2[i] = sb | (sb << 16);
+        pair4[i] = code_value_bf16(SPARK_FMT_NVFP4, i & 15u) | (code_value_bf16(SPARK_FMT_NVFP4, i >> 4) << 16);
+        if (i < 64) pair3[i] = code_value_bf16(SPARK_FMT_FP3, i & 7u) | (code_value_bf16(SPARK_FMT_FP3, i >> 3) << 16);
+    }
+    if (warp == kMmaWarp) tmem_alloc(smem_u32(&tmem_base_s), kCTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = tmem_base_s;
+    const uint32_t a_col0 = kCDCols;
+    bool ok = true;
+
+    if (warp == kProducerWarp) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            ChainUnits wi(pr, cta), xi(pr, cta);
+            int iw = 0, op, job, kc;
+            auto issue_w = [&](int i, int o, int jb, int k) -> bool {
+                const int s = i % kCWStages;
+                if (!mbar_wait(w_empty(s), ((i / kCWStages) & 1) ^ 1)) return false;
+                const ChainOp& c = pr.op[o];
+                const uint32_t dst = smem_u32(smem + kCW + s * kCWStage);
+                const int code_bytes = c.fmt == SPARK_FMT_SPFP2 ? 80 : (c.fmt == SPARK_FMT_FP3 ? 96 : 128);
+                const int row = (jb % c.n_rb) * kRows;
+                mbar_expect_tx(w_full(s), c.stage_bytes);
+                tma_load_2d(dst, &pr.wmap[o], k * code_bytes, row, w_full(s));
+                if (c.fmt != SPARK_FMT_SPFP2) tma_load_2d(dst + kRows * code_bytes, &pr.smap[o], k * 16, row, w_full(s));
+                return true;
+            };
+            while (ok && iw < kCWStages && wi.next(op, job, kc)) ok = issue_w(iw++, op, job, kc);
+            int cur = -1;
+            for (int i = 0; ok && xi.next(op, job, kc); ++i) {
+                const ChainOp& c = pr.op[op];
+                if (op != cur) {
+                    // the op's input comes from earlier ops: wait until they are complete
+                    cur = op;
+                    ok = wait_done(pr.done, c.dep0, c.dep0 >= 0 ? pr.op[c.dep0].target : 0) &&
+                         wait_done(pr.done, c.dep1, c.dep1 >= 0 ? pr.op[c.dep1].target : 0);
+                    if (!ok) break;
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                }
+                const int tb = job / c.n_rb;
+                for (int j = 0; j < kSub && ok; ++j) {
+                    const int ix = i * kSub + j, s = ix % kCXStages;
+                    ok = mbar_wait(x_empty(s), ((ix / kCXStages) & 1) ^ 1);
+                    if (!ok) break;
+                    mbar_expect_tx(x_full(s), kCN * 128);
+                    tma_load_2d(smem_u32(smem + kCX + s * kCN * 128), &pr.xmap[op], kc * kUnitCols + j * 64,
+                                tb * kCN, x_full(s));
+                }
+                int o2, jb, k;
+                if (ok && wi.next(o2, jb, k)) ok = issue_w(iw++, o2, jb, k);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(kCN);
+            int i = 0, seg = 0;
+            for (int op = 0; ok && op < pr.n_ops; ++op) {
+                const ChainOp& c = pr.op[op];
+                if (c.kind != 0) continue;
+                int u = op_unit_begin(cta, c.units, pr.grid);
+                const int u1 = op_unit_begin(cta + 1, c.units, pr.grid);
+                while (ok && u < u1) {
+                    const int job = u / c.n_kc, ka = u - job * c.n_kc;
+                    const int kb = min(c.n_kc, ka + (u1 - u));
+                    const int buf = seg & 1;
+                    ok = mbar_wait(d_empty(buf), ((seg >> 1) & 1) ^ 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t d_tmem = tbase + (uint32_t)(buf * kCDStride);
+                    for (int kc = ka; kc < kb && ok; ++kc, ++i) {
+                        for (int j = 0; j < kSub; ++j) {
+                            const int ia = i * kSub + j, sa = ia % kCAStages, sx = ia % kCXStages;
+                            ok = mbar_wait(a_full(sa), (ia / kCAStages) & 1) &&
+                                 mbar_wait(x_full(sx), (ia / kCXStages) & 1);
+                            if (!ok) break;
+                            tc_fence_after();
+                            const uint32_t xb = smem_u32(smem + kCX + sx * kCN * 128);
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)
+                                mma_ts(d_tmem + (uint32_t)((kk % kCChains) * kCN),
+                                       tbase + a_col0 + (uint32_t)(sa * 32 + kk * 8), sdesc_sw128(xb + kk * 32), idesc,
+                                       (kc == ka && j == 0 && kk < kCChains) ? 0u : 1u);
+                            mma_commit(a_empty(sa));
+                            mma_commit(x_empty(sx));
+                        }
+                    }
+                    if (ok) mma_commit(d_full(buf));
+                    u += kb - ka;
+                    ++seg;
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ decode, epilogue, SiLU ops
+        const int group = warp >> 2, quad = warp & 3;
+        const int r = threadIdx.x & (kRows - 1);
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        int i = 0, seg = 0;
+        for (int op = 0; ok && op < pr.n_ops; ++op) {
+            const ChainOp& c = pr.op[op];
+            if (c.kind == 1) {
+                // SiLU(gate) * up over this CTA's slice, once gate and up are complete
+                if (lane == 0)
+                    ok = wait_done(pr.done, c.dep0, pr.op[c.dep0].target) &&
+                         wait_done(pr.done, c.dep1, pr.op[c.dep1].target);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                const int64_t e0 = (int64_t)cta * c.n / pr.grid, e1 = (int64_t)(cta + 1) * c.n / pr.grid;
+                const __nv_bfloat16* g = static_cast<const __nv_bfloat16*>(c.g);
+                const __nv_bfloat16* uu = static_cast<const __nv_bfloat16*>(c.u);
+                __nv_bfloat16* o = static_cast<__nv_bfloat16*>(c.y);
+                for (int64_t e = e0 + threadIdx.x; e < e1; e += kDecThreads) {
+                    const float a = __bfloat162float(__ldcg(g + e)), b = __bfloat162float(__ldcg(uu + e));
+                    o[e] = __float2bfloat16_rn(a / (1.0f + __expf(-a)) * b);
+                }
+                __syncwarp();
+                if (lane == 0) red_release_add(pr.done + op, 1);
+                continue;
+            }
+            int u = op_unit_begin(cta, c.units, pr.grid);
+            const int u1 = op_unit_begin(cta + 1, c.units, pr.grid), cu0 = u;
+            while (ok && u < u1) {
+                const int job = u / c.n_kc, ka = u - job * c.n_kc;
+                const int kb = min(c.n_kc, ka + (u1 - u));
+                for (int kc = ka; kc < kb && ok; ++kc, ++i) {
+                    const int sw = i % kCWStages;
+                    ok = __all_sync(0xffffffffu, mbar_wait(w_full(sw), (i / kCWStages) & 1));
+                    if (!ok) break;
+                    const int ia = i * kSub + group, sa = ia % kCAStages;
+                    const uint8_t* stage = smem + kCW + sw * kCWStage;
+                    uint32_t A[32];
+                    // read the stage before releasing it; decode after the A stage is free
+                    uint32_t q[8];
+                    uint32_t sc = 0u;
+                    if (c.fmt == SPARK_FMT_SPFP2) load_step<SPARK_FMT_SPFP2>(stage, r, group, q, sc);
+                    else if (c.fmt == SPARK_FMT_FP3) load_step<SPARK_FMT_FP3>(stage, r, group, q, sc);
+                    else load_step<SPARK_FMT_NVFP4>(stage, r, group, q, sc);
+                    mbar_arrive(w_empty(sw));
+                    if (!__all_sync(0xffffffffu, mbar_wait(a_empty(sa), ((ia / kCAStages) & 1) ^ 1))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (c.fmt == SPARK_FMT_SPFP2) decode_step<SPARK_FMT_SPFP2>(q, sc, lut, scale2, pair3, A);
+                    else if (c.fmt == SPARK_FMT_FP3) decode_step<SPARK_FMT_FP3>(q, sc, lut, scale2, pair3, A);
+                    else decode_step<SPARK_FMT_NVFP4>(q, sc, lut, scale2, pair4, A);
+                    tmem_st32(tbase + lane_addr + a_col0 + (uint32_t)(sa * 32), A);
+                    tmem_st_wait();
+                    tc_fence_before();
+                    mbar_arrive(a_full(sa));
+                }
+                if (!ok) break;
+                const int seg_first = u == cu0;
+                u += kb - ka;
+                const int buf = seg & 1;
+                ++seg;
+                if (group != 0) continue;
+
+                // ---------------- epilogue of this segment (group 0, thread r = row r)
+                ok = __all_sync(0xffffffffu, mbar_wait(d_full(buf), ((seg - 1) >> 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                const int rb = job % c.n_rb, tb = job / c.n_rb;
+                const int64_t row = (int64_t)rb * kRows + r;
+                const int m0 = tb * kCN, mcount = min(kCN, pr.M - m0);
+                const uint32_t d_addr = tbase + lane_addr + (uint32_t)(buf * kCDStride);
+                float v[16];
+                tmem_ld16(d_addr, v);
+#pragma unroll
+                for (int ch = 1; ch < kCChains; ++ch) {
+                    float w[16];
+                    tmem_ld16(d_addr + (uint32_t)(ch * kCN), w);
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) v[t] += w[t];
+                }
+                tc_fence_before();
+                mbar_arrive(d_empty(buf));
+                const float bias = (c.bias && row < c.oc) ? load_as_float(c.bias, c.bias_dtype, row) : 0.0f;
+                if (ka == 0 && kb == c.n_kc) {
+                    if (row < c.oc)
+#pragma unroll
+                        for (int t = 0; t < 16; ++t)
+                            if (t < mcount) store_from_float(c.y, c.y_dtype, (int64_t)(m0 + t) * c.ldy + row, v[t] + bias);
+                    continue;
+                }
+                // partial sum: publish; the last contributor per 32-row quadrant adds them in CTA order
+                const int slot = 2 * cta + (seg_first ? 0 : 1);
+                float* mine = c.partials + (int64_t)slot * kCN * kRows + r;
+#pragma unroll
+                for (int t = 0; t < 16; ++t) __stcg(mine + t * kRows, v[t]);
+                __syncwarp();
+                const int job_u0 = job * c.n_kc;
+                const int cA = op_unit_owner(job_u0, c.units, pr.grid);
+                const int cB = op_unit_owner(job_u0 + c.n_kc - 1, c.units, pr.grid);
+                int* counter = c.counters + job * 4 + quad;
+                int last = 0;
+                if (lane == 0) last = atomic_add_acq_rel(counter, 1) == cB - cA;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (!last) continue;
+                if (row < c.oc) {
+                    float acc[16];
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) acc[t] = 0.0f;
+                    for (int cc = cA; cc <= cB; ++cc) {
+                        const int sl = 2 * cc + (op_unit_begin(cc, c.units, pr.grid) >= job_u0 ? 0 : 1);
+                        const float* src = c.partials + (int64_t)sl * kCN * kRows + r;
+                        float w[16];
+#pragma unroll
+                        for (int t = 0; t < 16; ++t) w[t] = t < mcount ? __ldcg(src + t * kRows) : 0.0f;
+#pragma unroll
+                        for (int t = 0; t < 16; ++t) acc[t] += w[t];
+                    }
+#pragma unroll
+                    for (int t = 0; t < 16; ++t)
+                        if (t < mcount) store_from_float(c.y, c.y_dtype, (int64_t)(m0 + t) * c.ldy + row, acc[t] + bias);
+                }
+                if (lane == 0) *counter = 0;
+            }
+            if (!ok) break;
+            // this CTA's rows of op are written (group 0 warps, one count each)
+            if (group == 0) {
+                __syncwarp();
+                if (lane == 0) red_release_add(pr.done + op, 1);
+            }
+        }
+    }
+    if (!ok) report_device_error(pr.err, 4);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tbase, kCTmemCols);
+    }
+}
+
+}  // namespace tc
+}  // namespace spark
+
+// ---------------------------------------------------------------------- C ABI
+using namespace spark;
+
+extern "C" {
+
+size_t spark_linear_chain_workspace_size(int n_ops) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t grid = (size_t)tc::sm_count_cached(dev);
+    // error word, done counters, fixup counters (64 Ki), per-op partials
+    return 512 + (size_t)65536 * 4 + (size_t)std::max(n_ops, 0) * 2 * grid * tc::kCN * tc::kRows * 4;
+}
+
+int spark_linear_chain(const SparkChainOp* ops, int n_ops, int64_t M, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+    SPARK_REQUIRE(ops && n_ops >= 1 && n_ops <= tc::kMaxOps, SPARK_ERR_INVALID,
+                  "spark_linear_chain: 1..%d ops", tc::kMaxOps);
+    SPARK_REQUIRE(M >= 1 && M <= 16, SPARK_ERR_UNSUPPORTED, "spark_linear_chain: M must be 1..16");
+    SPARK_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= spark_linear_chain_workspace_size(n_ops),
+                  SPARK_ERR_WORKSPACE, "spark_linear_chain: workspace of %zu bytes (256-aligned) needed",
+                  spark_linear_chain_workspace_size(n_ops));
+    int rc = tc::get_encoder();
+    if (rc) return rc;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int grid = tc::sm_count_cached(dev);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    static tc::ChainProgram pr;                 // built on the host, copied into the launch
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    memset(&pr, 0, sizeof(pr));
+    pr.n_ops = n_ops;
+    pr.grid = grid;
+    pr.M = (int)M;
+    pr.err = reinterpret_cast<int*>(ws);
+    pr.done = reinterpret_cast<int*>(ws + 256);
+    int* counters = reinterpret_cast<int*>(ws + 512);
+    int64_t counter_next = 0;
+    float* partials = reinterpret_cast<float*>(ws + 512 + 65536 * 4);
+    for (int k = 0; k < n_ops; ++k) {
+        const SparkChainOp& o = ops[k];
+        tc::ChainOp& c = pr.op[k];
+        SPARK_REQUIRE(o.dep[0] < k && o.dep[1] < k, SPARK_ERR_INVALID, "spark_linear_chain: op %d depends on a later op", k);
+        c.kind = o.kind;
+        c.dep0 = o.dep[0];
+        c.dep1 = o.dep[1];
+        c.y = o.y;
+        if (o.kind == SPARK_CHAIN_SILU_MUL) {
+            SPARK_REQUIRE(o.x && o.x2 && o.y && o.ic > 0 && o.dep[0] >= 0 && o.dep[1] >= 0, SPARK_ERR_INVALID,
+                          "spark_linear_chain: op %d: SiLU needs gate, up, out, width and both producing ops", k);
+            c.g = o.x;
+            c.u = o.x2;
+            c.n = M * o.ic;
+            c.target = grid * (tc::kDecThreads / 32);
+            continue;
+        }
+        SPARK_REQUIRE(o.kind == SPARK_CHAIN_LINEAR, SPARK_ERR_INVALID, "spark_linear_chain: op %d: bad kind", k);
+        SPARK_REQUIRE(tc_linear_ok(o.fmt, o.wq, o.scales, o.x, SPARK_DTYPE_BF16, o.ic, o.ldx) && o.y && o.oc > 0,
+                      SPARK_ERR_UNSUPPORTED,
+                      "spark_linear_chain: op %d: SPFP2/FP3/NVFP4 reference layout, bf16 x, ic %% 256, "
+                      "16-byte aligned buffers, ldx %% 8", k);
+        const int code_bytes = o.fmt == SPARK_FMT_SPFP2 ? 80 : (o.fmt == SPARK_FMT_FP3 ? 96 : 128);
+        const uint64_t row_code = (uint64_t)(o.ic / tc::kUnitCols * code_bytes);
+        rc = tc::encode_2d(&pr.wmap[k], CU_TENSOR_MAP_DATA_TYPE_UINT8, o.wq, row_code, (uint64_t)o.oc, row_code,
+                           (uint32_t)code_bytes, tc::kRows,
+                           o.fmt == SPARK_FMT_NVFP4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+        if (o.fmt == SPARK_FMT_SPFP2) {
+            pr.smap[k] = pr.wmap[k];
+        } else {
+            rc = tc::encode_2d(&pr.smap[k], CU_TENSOR_MAP_DATA_TYPE_UINT8, o.scales, (uint64_t)(o.ic / 16),
+                               (uint64_t)o.oc, (uint64_t)(o.ic / 16), 16, tc::kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (rc) return rc;
+        }
+        rc = tc::encode_2d(&pr.xmap[k], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, o.x, (uint64_t)o.ic, (uint64_t)M,
+                           (uint64_t)o.ldx * 2, 64, tc::kCN, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+        c.fmt = o.fmt;
+        c.n_rb = (int)((o.oc + tc::kRows - 1) / tc::kRows);
+        c.n_kc = (int)(o.ic / tc::kUnitCols);
+        c.units = c.n_rb * c.n_kc;
+        c.stage_bytes = tc::kRows * (code_bytes + (o.fmt == SPARK_FMT_SPFP2 ? 0 : 16));
+        c.oc = o.oc;
+        c.ldy = o.ldy;
+        c.bias = o.bias;
+        c.bias_dtype = o.bias_dtype;
+        c.y_dtype = o.y_dtype;
+        c.target = grid * 4;
+        SPARK_REQUIRE(counter_next + 4 * c.n_rb <= 65536, SPARK_ERR_UNSUPPORTED, "spark_linear_chain: too many rows");
+        c.counters = counters + counter_next;
+        counter_next += 4 * c.n_rb;
+        c.partials = partials + (int64_t)k * 2 * grid * tc::kCN * tc::kRows;
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    {
+        static bool done[64] = {};
+        if (dev >= 0 && dev < 64 && !done[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(tc::k_tc_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kCAlloc);
+            if (e != cudaSuccess) return set_error((int)e, "k_tc_chain attribute: %s", cudaGetErrorString(e));
+            done[dev] = true;
+        }
+    }
+    // done counters start at zero for every launch
+    cudaError_t e = cudaMemsetAsync(pr.done, 0, tc::kMaxOps * sizeof(int), s);
+    if (e != cudaSuccess) return set_error((int)e, "spark_linear_chain: %s", cudaGetErrorString(e));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::kCAlloc;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, tc::k_tc_chain, pr);
+    if (e != cudaSuccess) return set_error((int)e, "k_tc_chain launch: %s", cudaGetErrorString(e));
+    return SPARK_OK;
+}
+
+}  // extern "C"

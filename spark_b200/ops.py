@@ -289,9 +289,61 @@ def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bia
     return y.reshape(*lead, oc)
 
 
+class ChainOp:
+    """One op of linear_chain: a dequant linear or SiLU(gate) * up.
+
+    Linear: ChainOp("linear", fmt=, wq=, scales=, x=, y=, bias=, deps=[...]).
+    SiLU:   ChainOp("silu_mul", x=gate, x2=up, y=out, deps=[gate op, up op]).
+    deps: indices of earlier ops whose output this op reads."""
+
+    def __init__(self, kind, x, y, fmt="spfp2", wq=None, scales=None, x2=None, bias=None, deps=()):
+        self.kind, self.fmt, self.wq, self.scales, self.x, self.x2, self.y = kind, fmt, wq, scales, x, x2, y
+        self.bias, self.deps = bias, list(deps)
+
+
+_chain_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def linear_chain(chain: list[ChainOp], stream=None) -> None:
+    """Run the ops in one persistent launch (spark_linear_chain).  Outputs are
+    the caller's preallocated y tensors; every activation is bf16 [M, n]."""
+    if not chain:
+        return
+    x0 = chain[0].x
+    M = x0.shape[0]
+    arr = (_lib.SparkChainOp * len(chain))()
+    keep = []
+    for k, op in enumerate(chain):
+        c = arr[k]
+        deps = op.deps + [-1] * (2 - len(op.deps))
+        c.dep[0], c.dep[1] = deps[0], deps[1]
+        c.x, c.y = op.x.data_ptr(), op.y.data_ptr()
+        if op.kind == "silu_mul":
+            c.kind, c.x2, c.ic = _lib.CHAIN_SILU_MUL, op.x2.data_ptr(), op.x.shape[1]
+            continue
+        f = FORMATS[op.fmt] if isinstance(op.fmt, str) else int(op.fmt)
+        w = _bytes(op.wq)
+        s = _bytes(op.scales) if op.scales is not None else None
+        keep += [w, s]
+        oc = op.y.shape[1]
+        c.kind, c.fmt, c.wq, c.scales = _lib.CHAIN_LINEAR, f, w.data_ptr(), (s.data_ptr() if s is not None else None)
+        c.ic, c.ldx, c.oc, c.ldy, c.y_dtype = op.x.shape[1], op.x.stride(0), oc, op.y.stride(0), _dt(op.y)
+        if op.bias is not None:
+            c.bias, c.bias_dtype = op.bias.data_ptr(), _dt(op.bias)
+    n = int(_lib.lib().spark_linear_chain_workspace_size(len(chain)))
+    st = stream if stream is not None else torch.cuda.current_stream(x0.device)
+    key = (x0.device.index, st.cuda_stream)
+    ws = _chain_ws.get(key)
+    if ws is None or ws.numel() < n:
+        ws = torch.zeros(n, dtype=torch.uint8, device=x0.device)
+        _chain_ws[key] = ws
+    call("spark_linear_chain", ctypes.cast(arr, ctypes.c_void_p), len(chain), M, _p(ws), ws.numel(),
+         ctypes.c_void_p(st.cuda_stream))
+
+
 def check_device_errors(device=None) -> None:
     """Raise if a kernel left an error in a workspace (synchronises)."""
-    for (dev, sh), buf in list(_ws.items()):
+    for (dev, sh), buf in list(_ws.items()) + list(_chain_ws.items()):
         if device is not None and dev != device:
             continue
         call("spark_workspace_check", _p(buf), ctypes.c_void_p(sh))
