@@ -1228,7 +1228,8 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     // More than 16 tokens on a reference layout with bf16 x: the tcgen05 GEMM.
     const bool tc_ok = !tiled && tc_linear_ok(fmt, wq, scales, x, x_dtype, ic, ldx);
-    if (tcgen05 || (tc_ok && M > kMaxTokens)) {
+    // 2:4 weights: the tcgen05 kernel at every token count (its decode GEMV is far slower)
+    if (tcgen05 || (tc_ok && (M > kMaxTokens || fmt == SPARK_FMT_TWOFOUR))) {
         SPARK_REQUIRE(tc_ok, SPARK_ERR_UNSUPPORTED,
                       "spark_linear: the tcgen05 path takes SPFP2, FP3 or NVFP4 in the reference layout, bf16 x, "
                       "ic %% 256 == 0, 16-byte aligned weights, scales and x, ldx %% 8 == 0");

@@ -61,8 +61,13 @@ constexpr int kSub = 4;               // 64-column sub-steps per unit (one A sta
 // 32 x 3 B, NVFP4 128 x 1 B) and e4m3 scales (16 per unit).
 template <int FMT>
 struct Wfmt {
-    static constexpr int kCodeBytes = FMT == SPARK_FMT_SPFP2 ? 80 : (FMT == SPARK_FMT_FP3 ? 96 : 128);
-    static constexpr int kScaleBytes = FMT == SPARK_FMT_SPFP2 ? 0 : 16;
+    // 2:4 rows take 7 bytes per 32 weights: a 512-column unit (112 bytes) is
+    // the smallest whole 16-byte TMA box; the other formats use 256 columns
+    static constexpr int kSub = FMT == SPARK_FMT_TWOFOUR ? 8 : 4;      // 64-column steps per unit
+    static constexpr int kCols = 64 * kSub;
+    static constexpr int kCodeBytes =
+        FMT == SPARK_FMT_SPFP2 ? 80 : (FMT == SPARK_FMT_FP3 ? 96 : (FMT == SPARK_FMT_NVFP4 ? 128 : 112));
+    static constexpr int kScaleBytes = (FMT == SPARK_FMT_FP3 || FMT == SPARK_FMT_NVFP4) ? 16 : 0;
     static constexpr int kStageBytes = kRows * (kCodeBytes + kScaleBytes);   // multiple of 1024
     static constexpr bool kSwizzle = FMT == SPARK_FMT_NVFP4;                 // 128-byte rows: swizzle them
 };
@@ -98,7 +103,8 @@ struct Cfg {
     static constexpr int kX = 0;
     static constexpr int kW = kX + kXStages * kXBytes;
     static constexpr int kLut = kW + kWStages * W::kStageBytes;
-    static constexpr int kBar = kLut + 256 * 16;
+    static constexpr int kTfCodes = kLut + 256 * 16;            // 2:4 code table (64 B)
+    static constexpr int kBar = kTfCodes + 128;
     static constexpr int kNumBars = 2 * kWStages + 2 * kXStages + 2 * kAStages + 2 * kDBuf;
     static constexpr int kBytes = kBar + kNumBars * 8 + 16;
     static constexpr int kAlloc = kBytes + 1024;             // slack for aligning the base
@@ -260,6 +266,39 @@ __device__ __forceinline__ void decode_pair(uint32_t mw, uint4 t, uint32_t* A) {
     decode8(se >> 16, so >> 16, t.z, t.w, A + 4);
 }
 
+// 2:4 (two_four.py:112-189): a 7-byte pair holds two 16-blocks; block slot s
+// is the 28-bit field at bit 28s: four 4-bit modes (group g at bit 4g), two
+// sign bits per group (bits 16 + 2g, 17 + 2g) and the exponent (bit 24).
+// tf_codes[mode | s0 << 4 | s1 << 5] = the group's four SPFP2 codes (code i at
+// bit 2i; 0 = +, 1 = -, 2 = zero), so a block becomes one 16-code mantissa
+// word for decode_pair, with the same exponent for both of its 8-halves.
+__device__ __forceinline__ uint32_t twofour_codes(uint32_t idx) {
+    const uint32_t mode = idx & 15u, s0 = (idx >> 4) & 1u, s1 = (idx >> 5) & 1u;
+    const int pa[6] = {0, 0, 0, 1, 1, 2}, pb[6] = {1, 2, 3, 2, 3, 3};
+    uint32_t c = 0xaau;                                          // four zero codes
+    auto put = [&](int pos, uint32_t neg) { c = (c & ~(3u << (2 * pos))) | (neg << (2 * pos)); };
+    if (mode < 6) {
+        put(pa[mode], s0);
+        put(pb[mode], s1);
+    } else if (mode >= 8 && mode <= 11) {
+        put((int)mode - 8, s0);
+    }
+    return c;
+}
+
+// One 16-block (28-bit field f) -> 8 bf16x2 registers.
+__device__ __forceinline__ void decode_twofour_block(uint32_t f, const uint4* lut, const uint8_t* tf_codes,
+                                                     uint32_t* A) {
+    uint32_t mw = 0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const uint32_t idx = ((f >> (4 * g)) & 15u) | (((f >> (16 + 2 * g)) & 3u) << 4);
+        mw |= (uint32_t)tf_codes[idx] << (8 * g);
+    }
+    const uint32_t e = (f >> 24) & 15u;
+    decode_pair(mw, lut[e | (e << 4)], A);
+}
+
 // ------------------------------------------------------------------ FP3 / NVFP4 decode
 // Tables in shared memory: scale2[b] = the e4m3 byte b as bf16, in both halves
 // (fp8 to bf16 is exact: at most 4 significant bits; NaN stays NaN);
@@ -291,6 +330,12 @@ __device__ __forceinline__ void load_step(const uint8_t* stage, int r, int j, ui
         const uint32_t* src = reinterpret_cast<const uint32_t*>(stage + r * WF::kCodeBytes) + 5 * j;
 #pragma unroll
         for (int k = 0; k < 5; ++k) q[k] = src[k];
+    } else if constexpr (FMT == SPARK_FMT_TWOFOUR) {
+        // step j = two pairs = bytes [14j, 14j + 14) of the 112-byte row: the
+        // five words from the word holding byte 14j
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(stage + r * 112) + (14 * j) / 4;
+#pragma unroll
+        for (int k = 0; k < 5; ++k) q[k] = src[k];
     } else if constexpr (FMT == SPARK_FMT_FP3) {
         const uint2* src = reinterpret_cast<const uint2*>(stage + r * 96 + 24 * j);
 #pragma unroll
@@ -317,8 +362,20 @@ __device__ __forceinline__ void load_step(const uint8_t* stage, int r, int j, ui
 // 64 weights of one row -> 32 bf16x2 registers in natural column order.
 template <int FMT>
 __device__ __forceinline__ void decode_step(const uint32_t* q, uint32_t sc, const uint4* lut, const uint32_t* scale2,
-                                            const uint32_t* pairv, uint32_t* A) {
-    if constexpr (FMT == SPARK_FMT_SPFP2) {
+                                            const uint32_t* pairv, uint32_t* A, int j = 0,
+                                            const uint8_t* tf_codes = nullptr) {
+    if constexpr (FMT == SPARK_FMT_TWOFOUR) {
+        // 56-bit pairs at byte offset (14j) % 4 and + 7 of the five words
+        const int b0 = (14 * j) % 4;                 // 0 or 2
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+            const int bit = 8 * (b0 + 7 * pp), wi = bit >> 5, off = bit & 31;
+            const uint32_t lo = off ? __funnelshift_r(q[wi], q[wi + 1], off) : q[wi];
+            const uint32_t hi = off ? __funnelshift_r(q[wi + 1], q[wi + 2], off) : q[wi + 1];
+            decode_twofour_block(lo & 0x0fffffffu, lut, tf_codes, A + 16 * pp);
+            decode_twofour_block(__funnelshift_r(lo, hi, 28) & 0x0fffffffu, lut, tf_codes, A + 16 * pp + 8);
+        }
+    } else if constexpr (FMT == SPARK_FMT_SPFP2) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             uint32_t mw, eb;
@@ -423,6 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint4* lut = reinterpret_cast<uint4*>(smem + C::kLut);                        // SPFP2
     uint32_t* scale2 = reinterpret_cast<uint32_t*>(smem + C::kLut);                // FP3 / NVFP4
     uint32_t* pairv = reinterpret_cast<uint32_t*>(smem + C::kLut + 1024);
+    uint8_t* tf_codes = smem + C::kTfCodes;                                        // 2:4
     const uint32_t bar0 = smem_u32(smem + C::kBar);
     auto w_full = [&](int s) { return bar0 + 8u * s; };
     auto w_empty = [&](int s) { return bar0 + 8u * (kWStages + s); };
@@ -451,9 +509,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_map(&xmap);
     }
     for (int i = threadIdx.x; i < 256; i += kThreads) {
-        if constexpr (FMT == SPARK_FMT_SPFP2) {
+        if constexpr (FMT == SPARK_FMT_SPFP2 || FMT == SPARK_FMT_TWOFOUR) {
             const uint2 a = exp_tables(i & 15), b = exp_tables(i >> 4);
             lut[i] = make_uint4(a.x, a.y, b.x, b.y);
+            if (FMT == SPARK_FMT_TWOFOUR && i < 64) tf_codes[i] = (uint8_t)twofour_codes((uint32_t)i);
         } else {
             const uint32_t sb = bf16_bits(e4m3_to_f32((uint32_t)i));
             scale2[i] = sb | (sb << 16);
@@ -496,12 +555,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int i = 0; ok && xi.next(p, job, kc); ++i) {
                 const int tb = job / p.n_rb;
-                for (int j = 0; j < kSub && ok; ++j) {
-                    const int ix = i * kSub + j, s = ix % C::kXStages;
+                for (int j = 0; j < WF::kSub && ok; ++j) {
+                    const int ix = i * WF::kSub + j, s = ix % C::kXStages;
                     ok = mbar_wait(x_empty(s), ((ix / C::kXStages) & 1) ^ 1);
                     if (!ok) break;
                     mbar_expect_tx(x_full(s), C::kXBytes);
-                    tma_load_2d(smem_u32(smem + C::kX + s * C::kXBytes), &xmap, kc * kUnitCols + j * 64, tb * N,
+                    tma_load_2d(smem_u32(smem + C::kX + s * C::kXBytes), &xmap, kc * WF::kCols + j * 64, tb * N,
                                 x_full(s));
                 }
                 int jb, k;
@@ -522,8 +581,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tbase + (uint32_t)(buf * C::kDStride);
                 for (int kc = sg.ka; kc < sg.kb && ok; ++kc, ++i) {
-                    for (int j = 0; j < kSub; ++j) {
-                        const int ia = i * kSub + j, sa = ia % C::kAStages, sx = ia % C::kXStages;
+                    for (int j = 0; j < WF::kSub; ++j) {
+                        const int ia = i * WF::kSub + j, sa = ia % C::kAStages, sx = ia % C::kXStages;
                         ok = mbar_wait(a_full(sa), (ia / C::kAStages) & 1) &&
                              mbar_wait(x_full(sx), (ia / C::kXStages) & 1);
                         if (!ok) break;
@@ -554,25 +613,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int sw = i % kWStages;
                 ok = __all_sync(0xffffffffu, mbar_wait(w_full(sw), (i / kWStages) & 1));
                 if (!ok) break;
-                // this thread's 64 columns (step j = group) of row r
+                // this thread's 64-column steps j = group + 4t of row r
                 const uint8_t* stage = smem + C::kW + sw * WF::kStageBytes;
-                uint32_t q[FMT == SPARK_FMT_SPFP2 ? 5 : (FMT == SPARK_FMT_FP3 ? 6 : 8)];
-                uint32_t sc = 0u;
-                load_step<FMT>(stage, r, group, q, sc);
-                mbar_arrive(w_empty(sw));
-
-                const int ia = i * kSub + group, sa = ia % C::kAStages;
-                if (!__all_sync(0xffffffffu, mbar_wait(a_empty(sa), ((ia / C::kAStages) & 1) ^ 1))) {
-                    ok = false;
-                    break;
+                constexpr int kT = WF::kSub / 4;
+                constexpr int kQ = FMT == SPARK_FMT_FP3 ? 6 : (FMT == SPARK_FMT_NVFP4 ? 8 : 5);
+                uint32_t q[kT][kQ];
+                uint32_t sc[kT];
+#pragma unroll
+                for (int t = 0; t < kT; ++t) {
+                    sc[t] = 0u;
+                    load_step<FMT>(stage, r, group + 4 * t, q[t], sc[t]);
                 }
-                tc_fence_after();
-                uint32_t A[32];
-                decode_step<FMT>(q, sc, lut, scale2, pairv, A);
-                tmem_st32(tbase + lane_addr + a_col0 + (uint32_t)(sa * 32), A);
-                tmem_st_wait();
-                tc_fence_before();
-                mbar_arrive(a_full(sa));
+                mbar_arrive(w_empty(sw));
+#pragma unroll
+                for (int t = 0; t < kT; ++t) {
+                    const int j = group + 4 * t;
+                    const int ia = i * WF::kSub + j, sa = ia % C::kAStages;
+                    if (!__all_sync(0xffffffffu, mbar_wait(a_empty(sa), ((ia / C::kAStages) & 1) ^ 1))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t A[32];
+                    decode_step<FMT>(q[t], sc[t], lut, scale2, pairv, A, j, tf_codes);
+                    tmem_st32(tbase + lane_addr + a_col0 + (uint32_t)(sa * 32), A);
+                    tmem_st_wait();
+                    tc_fence_before();
+                    mbar_arrive(a_full(sa));
+                }
             }
             if (!ok || group >= C::kEpiGroups) continue;
 
@@ -772,10 +840,11 @@ size_t tc_partials_bytes(int dev, int64_t M) {
 
 bool tc_linear_ok(int fmt, const void* wq, const void* scales, const void* x, int x_dtype, int64_t ic,
                   int64_t ldx) {
-    if (fmt != SPARK_FMT_SPFP2 && fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4) return false;
-    if (fmt != SPARK_FMT_SPFP2 && !aligned(scales, 16)) return false;
-    return x_dtype == SPARK_DTYPE_BF16 && ic % tc::kUnitCols == 0 && aligned(wq, 16) && aligned(x, 16) &&
-           (ldx % 8) == 0;
+    if (fmt != SPARK_FMT_SPFP2 && fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4 && fmt != SPARK_FMT_TWOFOUR)
+        return false;
+    if ((fmt == SPARK_FMT_FP3 || fmt == SPARK_FMT_NVFP4) && !aligned(scales, 16)) return false;
+    const int64_t unit = fmt == SPARK_FMT_TWOFOUR ? 512 : 256;
+    return x_dtype == SPARK_DTYPE_BF16 && ic % unit == 0 && aligned(wq, 16) && aligned(x, 16) && (ldx % 8) == 0;
 }
 
 // Linear through k_tc_linear (SPFP2, FP3 or NVFP4, reference layouts).
@@ -791,7 +860,8 @@ int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, 
     int dev = 0;
     cudaGetDevice(&dev);
     const int ctas = tc::sm_count_cached(dev);
-    const int64_t n_rb = (oc + tc::kRows - 1) / tc::kRows, n_kc = ic / tc::kUnitCols;
+    const int64_t unit_cols = fmt == SPARK_FMT_TWOFOUR ? 512 : 256;
+    const int64_t n_rb = (oc + tc::kRows - 1) / tc::kRows, n_kc = ic / unit_cols;
     const int N = tc::token_tile(M, n_rb, ctas);
     const int64_t n_tb = (M + N - 1) / N;
     const int64_t jobs = n_rb * n_tb;
@@ -799,14 +869,15 @@ int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, 
                   (long long)jobs, (long long)(max_counters / 16));
     const int64_t units = jobs * n_kc;
     SPARK_REQUIRE(units < (1ll << 31) / 1024, SPARK_ERR_UNSUPPORTED, "tcgen05 path: problem too large");
-    const int code_bytes = fmt == SPARK_FMT_SPFP2 ? 80 : (fmt == SPARK_FMT_FP3 ? 96 : 128);
-    const uint64_t row_code_bytes = (uint64_t)(ic / tc::kUnitCols * code_bytes);
+    const int code_bytes =
+        fmt == SPARK_FMT_SPFP2 ? 80 : (fmt == SPARK_FMT_FP3 ? 96 : (fmt == SPARK_FMT_NVFP4 ? 128 : 112));
+    const uint64_t row_code_bytes = (uint64_t)(ic / unit_cols * code_bytes);
     alignas(64) CUtensorMap wmap, smap, xmap;
     rc = tc::encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, row_code_bytes, (uint64_t)oc, row_code_bytes,
                        (uint32_t)code_bytes, tc::kRows,
                        fmt == SPARK_FMT_NVFP4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    if (fmt == SPARK_FMT_SPFP2) {
+    if (fmt == SPARK_FMT_SPFP2 || fmt == SPARK_FMT_TWOFOUR) {
         smap = wmap;                      // unused
     } else {
         rc = tc::encode_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT8, scales, (uint64_t)(ic / 16), (uint64_t)oc,
@@ -838,7 +909,8 @@ int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, 
     switch (fmt) {
         case SPARK_FMT_SPFP2: return tc::launch_n<SPARK_FMT_SPFP2>(N, wmap, smap, xmap, p, s);
         case SPARK_FMT_FP3: return tc::launch_n<SPARK_FMT_FP3>(N, wmap, smap, xmap, p, s);
-        default: return tc::launch_n<SPARK_FMT_NVFP4>(N, wmap, smap, xmap, p, s);
+        case SPARK_FMT_NVFP4: return tc::launch_n<SPARK_FMT_NVFP4>(N, wmap, smap, xmap, p, s);
+        default: return tc::launch_n<SPARK_FMT_TWOFOUR>(N, wmap, smap, xmap, p, s);
     }
 }
 
@@ -1289,7 +1361,8 @@ int spark_linear_chain(const SparkChainOp* ops, int n_ops, int64_t M, void* work
             continue;
         }
         SPARK_REQUIRE(o.kind == SPARK_CHAIN_LINEAR, SPARK_ERR_INVALID, "spark_linear_chain: op %d: bad kind", k);
-        SPARK_REQUIRE(tc_linear_ok(o.fmt, o.wq, o.scales, o.x, SPARK_DTYPE_BF16, o.ic, o.ldx) && o.y && o.oc > 0,
+        SPARK_REQUIRE(o.fmt != SPARK_FMT_TWOFOUR && tc_linear_ok(o.fmt, o.wq, o.scales, o.x, SPARK_DTYPE_BF16, o.ic, o.ldx) &&
+                          o.y && o.oc > 0,
                       SPARK_ERR_UNSUPPORTED,
                       "spark_linear_chain: op %d: SPFP2/FP3/NVFP4 reference layout, bf16 x, ic %% 256, "
                       "16-byte aligned buffers, ldx %% 8", k);

@@ -56,8 +56,9 @@ class V3PackedLinear(nn.Module):
         self.register_buffer("bias", bias)
         # fragment-major copy for the decode GEMV when the shape allows it; the
         # reference-layout bytes are kept for export and for the other paths
+        # (2:4 always runs the tcgen05 kernel on the reference layout)
         self.register_buffer("w_tiled", ops.tile_weights(fmt, packed, scales, out_features, in_features)
-                             if packed.is_cuda and fmt in ("spfp2", "fp3", "nvfp4", "twofour") else None,
+                             if packed.is_cuda and fmt in ("spfp2", "fp3", "nvfp4") else None,
                              persistent=False)
 
     @classmethod

@@ -25,6 +25,8 @@ def ops():
 def pack(fmt, W):
     if fmt == "spfp2":
         return ops().spfp2_pack(W)[0], None
+    if fmt == "twofour":
+        return ops().twofour_pack(W), None
     if fmt == "fp3":
         return ops().fp3_pack(W)
     return ops().nvfp4_pack(W)
@@ -33,6 +35,8 @@ def pack(fmt, W):
 def oracle_decode(fmt, wq, s, oc, ic):
     if fmt == "spfp2":
         return O.unpack_blockwise_paired(wq.cpu().numpy(), oc * ic).reshape(oc, ic)
+    if fmt == "twofour":
+        return O.two_four_unpack(wq.cpu().numpy(), oc * ic).reshape(oc, ic)
     sb = s.cpu().view(torch.uint8).numpy()
     if fmt == "fp3":
         return O.fp3_unpack_3bit(wq.cpu().numpy(), sb, oc, ic)
@@ -81,6 +85,12 @@ def test_tc_scaled_formats(fmt, oc, ic, M):
     check_oracle(oc, ic, M, fmt=fmt, seed=oc + M)
 
 
+@pytest.mark.parametrize("oc,ic,M", [(2560, 9728, 1), (2560, 9728, 16), (1000, 1024, 3), (640, 1536, 64),
+                                     (1000, 512, 300), (130, 512, 200)])
+def test_tc_twofour(oc, ic, M):
+    check_oracle(oc, ic, M, fmt="twofour", seed=oc + M)
+
+
 @pytest.mark.parametrize("fmt", ["fp3", "nvfp4"])
 def test_tc_scaled_formats_bias_bf16(fmt):
     check_oracle(512, 512, 40, fmt=fmt, bias=True, out_dtype=torch.bfloat16)
@@ -104,7 +114,7 @@ def test_tc_repeat_calls_bit_identical():
 
 
 @pytest.mark.parametrize("fmt,oc,ic", [("spfp2", 9728, 2560), ("spfp2", 2560, 9728), ("fp3", 4096, 2560),
-                                       ("nvfp4", 2560, 4096)])
+                                       ("nvfp4", 2560, 4096), ("twofour", 2560, 9728)])
 def test_tc_prefill_full_size(fmt, oc, ic):
     """Config-3 shapes (M = 2048) against an fp64 GEMM of the GPU-decoded weights
     (decode is bit-exact against the oracle, tests/test_gpu_formats.py)."""
@@ -116,6 +126,8 @@ def test_tc_prefill_full_size(fmt, oc, ic):
     y = ops().linear(fmt, wq, s, x, oc, ic, out_dtype=torch.float32, tcgen05=True)
     if fmt == "spfp2":
         Wd = ops().spfp2_unpack(wq, oc * ic).view(oc, ic).double()
+    elif fmt == "twofour":
+        Wd = ops().twofour_unpack(wq, oc * ic).view(oc, ic).double()
     elif fmt == "fp3":
         Wd = ops().fp3_unpack(wq, s, oc, ic).view(oc, ic).double()
     else:
@@ -134,11 +146,13 @@ def test_tc_rejects_unsupported():
     assert e.value.code == _lib.ERR_UNSUPPORTED
 
 
-@pytest.mark.parametrize("fmt", ["spfp2", "fp3", "nvfp4"])
+@pytest.mark.parametrize("fmt", ["spfp2", "fp3", "nvfp4", "twofour"])
 def test_tc_activation_range(fmt):
     """bf16 x enters the tensor core unscaled: products are exact at any magnitude."""
     oc, ic, M = 256, 1024, 40
     g = torch.Generator().manual_seed(21)
+    if fmt == "twofour":
+        ic = 1024
     wq, s = pack(fmt, (torch.randn(oc, ic, generator=g) * 0.02).cuda())
     dec = oracle_decode(fmt, wq, s, oc, ic)
     for scale in (1e-6, 1.0, 3e4, 1e8):
