@@ -321,6 +321,40 @@ __device__ __forceinline__ void decode_step(const uint32_t* c, uint32_t sw, int 
     else decode_twofour_t<false>(c, s, A);
 }
 
+// Sum, in warp order, of the partials that warps w_lo..w_hi published for
+// one row group.  Warps after w_lo start inside the row group, so they hold
+// it in slot 0; w_lo holds it in slot 1 when its range began in an earlier
+// row group.  A batch's loads are all issued before its first add: the
+// reduction costs one L2 round trip per batch instead of one per warp.
+template <int NT>
+__device__ __forceinline__ void sum_partials(const float* partials, int w_lo, int w_hi, bool lo_second, int lane,
+                                             float (&sum)[NT][4]) {
+    constexpr int B = 8 / NT;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sum[nt][i] = 0.0f;
+    for (int w0 = w_lo; w0 <= w_hi; w0 += B) {
+        float4 v[B][NT];
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const int w = w0 + k;
+            const int sl = (w == w_lo && lo_second) ? 1 : 0;
+            const float4* src = reinterpret_cast<const float4*>(partials + (((int64_t)w * 2 + sl) * NT * 32 + lane) * 4);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) v[k][nt] = w <= w_hi ? __ldcg(src + nt * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            if (w0 + k > w_hi) break;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                sum[nt][0] += v[k][nt].x; sum[nt][1] += v[k][nt].y; sum[nt][2] += v[k][nt].z; sum[nt][3] += v[k][nt].w;
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------- kernel args
 struct GemvArgs {
     const uint8_t* wq;
@@ -572,20 +606,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv(const GemvArgs a) {
         if (old != w_hi - w_lo) return;
         __threadfence();
         float sum[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sum[nt][i] = 0.0f;
-        for (int w = w_lo; w <= w_hi; ++w) {
-            const int ws = (int)((int64_t)U * w / T);
-            const int sl = (ws / nkc == rg) ? 0 : 1;
-            const float* src = a.partials + (((int64_t)w * 2 + sl) * NT * 32 + lane) * 4;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                float4 v = __ldcg(reinterpret_cast<const float4*>(src + nt * 128));
-                sum[nt][0] += v.x; sum[nt][1] += v.y; sum[nt][2] += v.z; sum[nt][3] += v.w;
-            }
-        }
+        const bool lo_second = (int)((int64_t)U * w_lo / T) / nkc != rg;
+        sum_partials<NT>(a.partials, w_lo, w_hi, lo_second, lane, sum);
         write_rows<NT>(a, rg, sum, lane, a.sigma);
         if (lane == 0) a.counters[rg] = 0;
     };
@@ -787,7 +809,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    float acc[NT][4];
+    // one token tile: the second MMA of each step accumulates separately, so
+    // consecutive MMAs do not wait on each other
+    float acc[NT][4], accb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float* acc2 = NT == 1 ? accb : acc[0];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -822,20 +847,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
         old = __shfl_sync(0xffffffffu, old, 0);
         if (old != w_hi - w_lo) return;
         float sum[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sum[nt][i] = 0.0f;
-        for (int w = w_lo; w <= w_hi; ++w) {
-            const int ws = (int)((int64_t)U * w / T);
-            const int sl = (ws / nkc == rg) ? 0 : 1;
-            const float* src = a.partials + (((int64_t)w * 2 + sl) * NT * 32 + lane) * 4;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                float4 v = __ldcg(reinterpret_cast<const float4*>(src + nt * 128));
-                sum[nt][0] += v.x; sum[nt][1] += v.y; sum[nt][2] += v.z; sum[nt][3] += v.w;
-            }
-        }
+        const bool lo_second = (int)((int64_t)U * w_lo / T) / nkc != rg;
+        sum_partials<NT>(a.partials, w_lo, w_hi, lo_second, lane, sum);
         write_rows<NT>(a, rg, sum, lane, sig);
         if (lane == 0) a.counters[rg] = 0;
     };
@@ -881,7 +894,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
                 if (tok0) x0 = ldg_nc_v4(xb0 + col0 + 8 * s);
                 if (NT > 1 && tok1) x1 = ldg_nc_v4(xb1 + col0 + 8 * s);
                 mma_16816_bf16(acc[0], A0[0], A1[0], A0[1], A1[1], x0.x, x0.y);
-                mma_16816_bf16(acc[0], A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
+                mma_16816_bf16(acc2, A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
                 if (NT > 1) {
                     mma_16816_bf16(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
                     mma_16816_bf16(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
@@ -896,7 +909,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
                     if (tok0) x0 = ldg_nc_v4(xrow0 + po);
                     if (NT > 1 && tok1) x1 = ldg_nc_v4(xrow1 + po);
                     mma_16816(acc[0], A0[0], A1[0], A0[1], A1[1], x0.x, x0.y);
-                    mma_16816(acc[0], A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
+                    mma_16816(acc2, A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
                     if (NT > 1) {
                         mma_16816(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
                         mma_16816(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
@@ -906,6 +919,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
         }
         const int u = u0 + i;
         if (++ckc == nkc || i + 1 == n) {
+            if constexpr (NT == 1) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) { acc[0][q] += accb[q]; accb[q] = 0.0f; }
+            }
             flush(crg, seg0, u + 1);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)

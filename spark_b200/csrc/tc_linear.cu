@@ -97,11 +97,16 @@ struct Cfg {
     static constexpr uint32_t kTmemCols = kDCols + kAStages * 32 <= 256 ? 256u : 512u;
     // x tiles are small for decode-sized token tiles and latency-bound from
     // L2: keep many in flight
-    static constexpr int kXStages = N == 16 ? 32 : (N == 64 ? 12 : (N == 128 ? 10 : 5));
-    static constexpr int kXBytes = N * 128;                  // N rows x 64 bf16
+    // Up to 64 tokens one TMA brings a whole unit of x (kSub sub-tiles of N
+    // rows x 64 columns, each 128-byte swizzled); larger tiles take one TMA per
+    // 64-column sub-tile.
+    static constexpr bool kXUnit = N <= 64;
+    static constexpr int kXBytes = N * 128;                  // one sub-tile: N rows x 64 bf16
+    static constexpr int kXStageBytes = kXUnit ? W::kSub * kXBytes : kXBytes;
+    static constexpr int kXStages = kXUnit ? (N == 16 ? 8 : (W::kSub == 8 ? 2 : 3)) : (N == 128 ? 10 : 5);
     // dynamic shared memory (offsets from a 1024-aligned base)
     static constexpr int kX = 0;
-    static constexpr int kW = kX + kXStages * kXBytes;
+    static constexpr int kW = kX + kXStages * kXStageBytes;
     static constexpr int kLut = kW + kWStages * W::kStageBytes;
     static constexpr int kTfCodes = kLut + 256 * 16;            // 2:4 code table (64 B)
     static constexpr int kBar = kTfCodes + 128;
@@ -109,7 +114,7 @@ struct Cfg {
     static constexpr int kBytes = kBar + kNumBars * 8 + 16;
     static constexpr int kAlloc = kBytes + 1024;             // slack for aligning the base
     static_assert(kAlloc <= 232448, "shared memory above the 227 KB a CTA may use");
-    static_assert(W::kStageBytes % 1024 == 0 && (kXStages * kXBytes) % 1024 == 0, "stages must stay 1024-aligned");
+    static_assert(W::kStageBytes % 1024 == 0 && kXBytes % 1024 == 0, "stages must stay 1024-aligned");
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -154,6 +159,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             dst),
         "l"(map), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
         : "memory");
 }
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
@@ -555,13 +567,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int i = 0; ok && xi.next(p, job, kc); ++i) {
                 const int tb = job / p.n_rb;
-                for (int j = 0; j < WF::kSub && ok; ++j) {
-                    const int ix = i * WF::kSub + j, s = ix % C::kXStages;
-                    ok = mbar_wait(x_empty(s), ((ix / C::kXStages) & 1) ^ 1);
+                if constexpr (C::kXUnit) {
+                    // the unit's kSub sub-tiles in one box of the [chunk][row][64] view of x
+                    const int s = i % C::kXStages;
+                    ok = mbar_wait(x_empty(s), ((i / C::kXStages) & 1) ^ 1);
                     if (!ok) break;
-                    mbar_expect_tx(x_full(s), C::kXBytes);
-                    tma_load_2d(smem_u32(smem + C::kX + s * C::kXBytes), &xmap, kc * WF::kCols + j * 64, tb * N,
+                    mbar_expect_tx(x_full(s), C::kXStageBytes);
+                    tma_load_3d(smem_u32(smem + C::kX + s * C::kXStageBytes), &xmap, 0, tb * N, kc * WF::kSub,
                                 x_full(s));
+                } else {
+                    for (int j = 0; j < WF::kSub && ok; ++j) {
+                        const int ix = i * WF::kSub + j, s = ix % C::kXStages;
+                        ok = mbar_wait(x_empty(s), ((ix / C::kXStages) & 1) ^ 1);
+                        if (!ok) break;
+                        mbar_expect_tx(x_full(s), C::kXBytes);
+                        tma_load_2d(smem_u32(smem + C::kX + s * C::kXBytes), &xmap, kc * WF::kCols + j * 64, tb * N,
+                                    x_full(s));
+                    }
                 }
                 int jb, k;
                 if (ok && wi.next(p, jb, k)) ok = issue_w(iw++, jb, k);
@@ -581,21 +603,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tbase + (uint32_t)(buf * C::kDStride);
                 for (int kc = sg.ka; kc < sg.kb && ok; ++kc, ++i) {
+                    const int su = i % C::kXStages;
+                    if constexpr (C::kXUnit) {
+                        ok = mbar_wait(x_full(su), (i / C::kXStages) & 1);
+                        if (!ok) break;
+                    }
                     for (int j = 0; j < WF::kSub; ++j) {
-                        const int ia = i * WF::kSub + j, sa = ia % C::kAStages, sx = ia % C::kXStages;
+                        const int ia = i * WF::kSub + j, sa = ia % C::kAStages;
+                        const int sx = C::kXUnit ? su : ia % C::kXStages;
                         ok = mbar_wait(a_full(sa), (ia / C::kAStages) & 1) &&
-                             mbar_wait(x_full(sx), (ia / C::kXStages) & 1);
+                             (C::kXUnit || mbar_wait(x_full(sx), (ia / C::kXStages) & 1));
                         if (!ok) break;
                         tc_fence_after();
-                        const uint32_t xb = smem_u32(smem + C::kX + sx * C::kXBytes);
+                        const uint32_t xb = C::kXUnit ? smem_u32(smem + C::kX + su * C::kXStageBytes + j * C::kXBytes)
+                                                      : smem_u32(smem + C::kX + sx * C::kXBytes);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
                             mma_ts(d_tmem + (uint32_t)((kk % C::kChains) * N), tbase + a_col0 + (uint32_t)(sa * 32 + kk * 8),
                                    sdesc_sw128(xb + kk * 32), idesc,
                                    (kc == sg.ka && j == 0 && kk < C::kChains) ? 0u : 1u);
                         mma_commit(a_empty(sa));
-                        mma_commit(x_empty(sx));
+                        if (!C::kXUnit) mma_commit(x_empty(sx));
                     }
+                    if (C::kXUnit && ok) mma_commit(x_empty(su));
                 }
                 if (ok) mma_commit(d_full(buf));
             }
@@ -884,9 +914,21 @@ int tc_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, 
                            (uint64_t)(ic / 16), 16, tc::kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
-    rc = tc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)ic, (uint64_t)M, (uint64_t)ldx * 2, 64,
-                       (uint32_t)N, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
+    if (N <= 64) {
+        // [ic/64 chunks][M rows][64 columns] view of x: one box = a unit's sub-tiles
+        const cuuint64_t dims[3] = {64, (cuuint64_t)M, (cuuint64_t)(ic / 64)};
+        const cuuint64_t strides[2] = {(cuuint64_t)ldx * 2, 128};
+        const cuuint32_t box[3] = {64, (cuuint32_t)N, (cuuint32_t)(unit_cols / 64)};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        CUresult r = tc::g_encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(x), dims, strides, box,
+                                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return set_error(SPARK_ERR_INVALID, "cuTensorMapEncodeTiled (x, 3-d) failed (%d)", (int)r);
+    } else {
+        rc = tc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)ic, (uint64_t)M, (uint64_t)ldx * 2, 64,
+                           (uint32_t)N, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
     tc::Params p = {};
     p.bias = bias;
     p.y = y;
