@@ -48,6 +48,15 @@ SHAPES = [                     # (name, fmt, oc, ic)
     ("v_proj", "fp3", 4096, 2560),
     ("out_proj", "nvfp4", 2560, 4096),
 ]
+# Projections that read the same activations run as one row-merged launch
+# (spark_b200.inference_v3.V3MergedLinear), as inference engines fuse q/k/v
+# and gate/up: the same weights, bytes and outputs in 4 launches per layer.
+GROUPS = [                     # (launch name, fmt, projections in row order)
+    ("qkv_proj", "fp3", ("q_proj", "k_proj", "v_proj")),
+    ("out_proj", "nvfp4", ("out_proj",)),
+    ("gate_up_proj", "spfp2", ("gate_proj", "up_proj")),
+    ("down_proj", "spfp2", ("down_proj",)),
+]
 CONFIG = {
     "workload": "BASELINE config 2: tiered decode linears of one 4B-like hybrid-attention layer "
                 "(SPFP2 gate/up/down, FP3 q/k/v, NVFP4 out_proj), M=1, one token through 8 layer copies per step",
@@ -55,6 +64,8 @@ CONFIG = {
     "layers_per_step": LAYERS,
     "l2": "weights rotate over 8 distinct layer copies (344 MB) > 126 MB L2",
     "graph": "each step replayed as one CUDA graph",
+    "projections": "q|k|v and gate|up row-merged into one packed weight each (V3MergedLinear): 4 GEMV "
+                   "launches per layer; per_projection repeats the step with one launch per linear",
 }
 METRIC = "dequant-GEMV HBM GB/s (% of 8 TB/s) at M=1; prefill dequant-GEMM TFLOP/s"
 PREFILL_M = 2048               # prefill tokens through one layer's 7 linears
@@ -204,10 +215,23 @@ def build_layers(device):
     return layers
 
 
+def merge_layer(L):
+    """Row-merged launches of one layer: packed bytes (and scales) concatenated."""
+    from spark_b200 import ops
+    out = {}
+    for gname, fmt, parts in GROUPS:
+        wq = torch.cat([L[p][1] for p in parts])
+        s = torch.cat([L[p][2] for p in parts]) if L[parts[0]][2] is not None else None
+        oc, ic = sum(L[p][3] for p in parts), L[parts[0]][4]
+        out[gname] = (fmt, wq, s, oc, ic, ops.tile_weights(fmt, wq, s, oc, ic))
+    return out
+
+
 def run_gpu(args, rank, world, local):
     from spark_b200 import ops
     device = torch.device("cuda", local)
     layers = build_layers(device)
+    merged = [merge_layer(L) for L in layers]
     g = torch.Generator(device=device).manual_seed(7)
     x = {ic: torch.randn(1, ic, device=device, generator=g).bfloat16() for ic in (2560, 4096, 9728)}
     outs = {}
@@ -215,8 +239,8 @@ def run_gpu(args, rank, world, local):
     max_ws = max(ops.workspace_size(ops.FORMATS[f], 1, oc, ic) for _, f, oc, ic in SHAPES)
     ops.workspace(device, max_ws, stream=stream)
 
-    def step(only=None):
-        for L in layers:
+    def step(only=None, which=None):
+        for L in (which or merged):
             for name, (fmt, wq, s, oc, ic, wt) in L.items():
                 if only and fmt != only:
                     continue
@@ -228,12 +252,15 @@ def run_gpu(args, rank, world, local):
         for _ in range(2):
             step()
             step("spfp2")
+            step(which=layers)
     torch.cuda.synchronize()
-    graph, graph_spfp2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    graph, graph_spfp2, graph_pp = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
     with torch.cuda.graph(graph_spfp2, stream=stream):
         step("spfp2")
+    with torch.cuda.graph(graph_pp, stream=stream):
+        step(which=layers)
     torch.cuda.synchronize()
 
     def timed(gr, k):
@@ -257,25 +284,34 @@ def run_gpu(args, rank, world, local):
     with Clocks(local) as clk:
         ms_total = timed(graph, args.steps)
     ms_spfp2 = timed(graph_spfp2, args.steps)
+    ms_pp = timed(graph_pp, args.steps)
     ops.check_device_errors()
 
     # ---------------- e2e through the public layer API with host buffers
-    from spark_b200.inference_v3 import V3PackedLinear
-    mods = [{name: V3PackedLinear.from_packed(fmt, wq, s, oc, ic) for name, (fmt, wq, s, oc, ic, _) in L.items()}
-            for L in layers]
+    from spark_b200.inference_v3 import V3MergedLinear, V3PackedLinear
+    mods = []
+    for L in layers:
+        lin = {name: V3PackedLinear.from_packed(fmt, wq, s, oc, ic) for name, (fmt, wq, s, oc, ic, _) in L.items()}
+        mods.append({gname: V3MergedLinear([lin[p] for p in parts]) if len(parts) > 1 else lin[parts[0]]
+                     for gname, _, parts in GROUPS})
     xh = {ic: x[ic].cpu().pin_memory() for ic in x}
     yh = {}
     for L in mods:
-        for name, m in L.items():
-            yh[(name, id(L))] = torch.empty(1, m.out_features, dtype=torch.bfloat16).pin_memory()
+        for name, _, parts in GROUPS:
+            for p in parts:
+                oc = next(o for n, _, o, _ in SHAPES if n == p)
+                yh[(p, id(L))] = torch.empty(1, oc, dtype=torch.bfloat16).pin_memory()
     h2d = sum(t.numel() * 2 for t in xh.values())
     d2h = sum(t.numel() * 2 for t in yh.values())
 
     def e2e_step():
         xd = {ic: xh[ic].to(device, non_blocking=True) for ic in xh}
         for L in mods:
-            for name, m in L.items():
-                yh[(name, id(L))].copy_(m(xd[m.in_features]), non_blocking=True)
+            for gname, _, parts in GROUPS:
+                m = L[gname]
+                ys = m(xd[m.in_features])
+                for p, y in zip(parts, ys if isinstance(ys, tuple) else (ys,)):
+                    yh[(p, id(L))].copy_(y, non_blocking=True)
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 1)):
@@ -320,7 +356,9 @@ def run_gpu(args, rank, world, local):
     spfp2_gbs = SPFP2_BYTES * args.steps / (ms_spfp2 * 1e-3) / 1e9
     e2e_gbs = world * STEP_BYTES * args.steps / (ms_e2e * 1e-3) / 1e9
     # SPFP2 with bf16 x: one GEMV launch; FP3 / NVFP4: activation prepare + GEMV
-    launches = args.steps * LAYERS * sum(1 if f == "spfp2" else 2 for _, f, _, _ in SHAPES)
+    launches = args.steps * LAYERS * sum(1 if f == "spfp2" else 2 for _, f, _ in GROUPS)
+    launches_pp = args.steps * LAYERS * sum(1 if f == "spfp2" else 2 for _, f, _, _ in SHAPES)
+    value_pp = world * STEP_BYTES * args.steps / (ms_pp * 1e-3) / 1e9
     traffic = load_traffic()
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -329,12 +367,14 @@ def run_gpu(args, rank, world, local):
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) bf16 activations)",
         "config": {**CONFIG, "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "hbm_frac": round(value / world / peak, 4),
-        "roofline": {"bound": "hbm", "kernel": "k_gemv_tiled<SPFP2> (+ its k_prepare_x), gate/up/down at M=1",
+        "roofline": {"bound": "hbm", "kernel": "k_gemv_tiled<SPFP2>, gate|up [19456,2560] and down [2560,9728] at M=1",
                      "achieved": round(spfp2_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(spfp2_gbs / peak, 4), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
                      if peak_kind == "measured" else "fallback 6650 GB/s",
                      "traffic": traffic},
         "gpu_launches": launches,
+        "per_projection": {"value": round(value_pp, 1), "unit": "GB/s", "ms_per_step": round(ms_pp / args.steps, 4),
+                           "gpu_launches": launches_pp},
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "spark_b200.inference_v3.V3PackedLinear, eager, pinned host I/O"},
         "clocks": clk.summary(),

@@ -97,6 +97,56 @@ class V3PackedLinear(nn.Module):
         return f"fmt={self.fmt}, in_features={self.in_features}, out_features={self.out_features}"
 
 
+def _row_aligned(fmt: str, ic: int) -> bool:
+    """True when every output row of a packed weight is a whole number of bytes,
+    so row-concatenating packed buffers equals packing the stacked matrix."""
+    if fmt == "spfp2":
+        return ic % 16 == 0          # 5-byte block pairs never straddle rows
+    if fmt == "twofour":
+        return ic % 32 == 0          # 7-byte pairs of 16-blocks
+    return fmt in ("fp3", "nvfp4")   # rows padded to whole 16-blocks
+
+
+class V3MergedLinear(nn.Module):
+    """Projections that read the same input (q/k/v, gate/up) kept as ONE
+    packed weight, their rows stacked in order: one launch streams all of
+    them.  forward(x) returns one output per part, views of the stacked
+    [..., sum(out_features)] result; each equals the part's own layer output
+    up to fp32 summation order."""
+
+    def __init__(self, parts: list[V3PackedLinear]):
+        super().__init__()
+        if not parts:
+            raise ValueError("V3MergedLinear needs at least one part")
+        fmt, ic = parts[0].fmt, parts[0].in_features
+        for p in parts:
+            if p.fmt != fmt or p.in_features != ic:
+                raise ValueError("merged parts must share the format and in_features")
+        if not _row_aligned(fmt, ic):
+            raise ValueError(f"{fmt} rows of {ic} weights are not byte-aligned; cannot merge")
+        self.splits = [p.out_features for p in parts]
+        packed = torch.cat([p.w_packed.reshape(-1) for p in parts])
+        scales = None
+        if parts[0].w_scales is not None:
+            scales = torch.cat([p.w_scales.reshape(-1) for p in parts])
+        bias = None
+        if any(p.bias is not None for p in parts):
+            ref = next(p.bias for p in parts if p.bias is not None)
+            bias = torch.cat([p.bias if p.bias is not None else
+                              torch.zeros(p.out_features, dtype=ref.dtype, device=ref.device) for p in parts])
+        self.merged = V3PackedLinear(fmt, packed, sum(self.splits), ic, scales=scales, bias=bias)
+
+    @property
+    def in_features(self) -> int:
+        return self.merged.in_features
+
+    def forward(self, x: torch.Tensor) -> tuple[torch.Tensor, ...]:
+        return self.merged(x).split(self.splits, dim=-1)
+
+    def extra_repr(self) -> str:
+        return f"fmt={self.merged.fmt}, in_features={self.in_features}, splits={self.splits}"
+
+
 class V3SPFP2Layer(V3PackedLinear):
     """Drop-in for inference_v3.V3SPFP2Layer(packed_weight, out_features, in_features, bias)."""
 

@@ -79,3 +79,18 @@ def test_fp3_nibbles_to_3bit_matches_oracle():
     cn, _ = O.fp3_pack(w)
     n = 6 * 96
     assert np.array_equal(fp3_nibbles_to_3bit(torch.from_numpy(cn), n).numpy(), c3)
+
+
+def test_merged_linear_concatenates_rows_and_rejects_straddling_rows():
+    from spark_b200.inference_v3 import V3MergedLinear, V3PackedLinear
+    g = torch.Generator().manual_seed(0)
+    a = torch.randint(0, 256, (64 * 512 // 16 * 5,), dtype=torch.uint8, generator=g)
+    b = torch.randint(0, 256, (32 * 512 // 16 * 5,), dtype=torch.uint8, generator=g)
+    m = V3MergedLinear([V3PackedLinear("spfp2", a, 64, 512), V3PackedLinear("spfp2", b, 32, 512)])
+    assert m.splits == [64, 32] and m.merged.out_features == 96 and m.in_features == 512
+    assert torch.equal(m.merged.w_packed, torch.cat([a, b]))
+    c = torch.randint(0, 256, (16 * 104 // 16 * 5,), dtype=torch.uint8, generator=g)
+    with pytest.raises(ValueError):
+        V3MergedLinear([V3PackedLinear("spfp2", c, 16, 104), V3PackedLinear("spfp2", c, 16, 104)])
+    with pytest.raises(ValueError):
+        V3MergedLinear([V3PackedLinear("spfp2", a, 64, 512), V3PackedLinear("twofour", a, 64, 512)])

@@ -1,0 +1,54 @@
+"""Row-merged projections (V3MergedLinear): one packed weight for q/k/v or
+gate/up, one launch; every part's output against an fp64 product with the
+part's own decoded weight (5e-4 max-abs, fp32 activations) and against the
+part's own layer."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+TOL = 5e-4
+
+
+def _part(fmt, oc, ic, seed):
+    from spark_b200 import ops
+    from spark_b200.inference_v3 import V3PackedLinear
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w = torch.randn(oc, ic, device="cuda", generator=g) * 0.02
+    b = torch.randn(oc, device="cuda", generator=g) * 0.1
+    if fmt == "spfp2":
+        wq, s = ops.spfp2_pack(w)[0], None
+        deq = ops.spfp2_unpack(wq, oc * ic).view(oc, ic)
+    elif fmt == "fp3":
+        wq, s = ops.fp3_pack(w)
+        deq = ops.fp3_unpack(wq, s, oc, ic)
+    elif fmt == "nvfp4":
+        wq, s = ops.nvfp4_pack(w)
+        deq = ops.nvfp4_unpack(wq, s, oc, ic)
+    else:
+        wq, s = ops.twofour_pack(w), None
+        deq = ops.twofour_unpack(wq, oc * ic).view(oc, ic)
+    return V3PackedLinear(fmt, wq, oc, ic, scales=s, bias=b), deq, b
+
+
+@pytest.mark.parametrize("fmt,ocs,ic", [("spfp2", (768, 768), 512), ("fp3", (512, 256, 256), 512),
+                                        ("nvfp4", (256, 512), 512), ("twofour", (512, 256), 1024)])
+@pytest.mark.parametrize("M", [1, 5, 300])
+def test_merged_parts_match(fmt, ocs, ic, M):
+    from spark_b200.inference_v3 import V3MergedLinear
+    parts = [_part(fmt, oc, ic, seed=11 * k + 1) for k, oc in enumerate(ocs)]
+    merged = V3MergedLinear([p for p, _, _ in parts])
+    x = torch.randn(M, ic, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+    outs = merged(x)
+    assert len(outs) == len(ocs)
+    for (layer, deq, b), y in zip(parts, outs):
+        ref = x.double() @ deq.double().T + b.double()
+        assert y.shape == (M, layer.out_features)
+        assert (y.double() - ref).abs().max().item() <= TOL
+        assert (y.double() - layer(x).double()).abs().max().item() <= TOL
+    xb = x.bfloat16()
+    for (layer, _, _), y in zip(parts, merged(xb)):
+        assert y.dtype == torch.bfloat16
+        assert torch.allclose(y.float(), layer(xb).float(), rtol=2e-2, atol=2e-2)
