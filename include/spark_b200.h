@@ -219,6 +219,10 @@ SPARK_API int spark_workspace_check(void* workspace, void* stream);
 /* Elementwise SiLU(gate) * up for the MLP between the gate/up and down projections
  * (the activation the reference model applies between its MLP linears). */
 SPARK_API int spark_silu_mul(const void* gate, const void* up, void* out, int dtype, int64_t n, void* stream);
+/* SiLU(gate) * up over [rows, cols] with gate / up rows ld_in elements apart
+ * (the halves of a row-merged gate|up output) and out rows ld_out apart. */
+SPARK_API int spark_silu_mul_rows(const void* gate, const void* up, int64_t ld_in, void* out, int64_t ld_out,
+                                  int dtype, int64_t rows, int64_t cols, void* stream);
 
 #ifdef __cplusplus
 }

@@ -350,6 +350,17 @@ def check_device_errors(device=None) -> None:
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """SiLU(gate) * up.  2-D views with unit column stride and a common row
+    stride (the two halves of a row-merged gate|up output) are read in place."""
+    if gate.shape != up.shape:
+        raise ValueError("silu_mul: gate and up shapes differ")
+    if (gate.dim() == 2 and gate.stride(1) == 1 and up.stride(1) == 1 and gate.stride(0) == up.stride(0)
+            and gate.dtype == up.dtype):
+        rows, cols = gate.shape
+        out = torch.empty(rows, cols, dtype=gate.dtype, device=gate.device)
+        call("spark_silu_mul_rows", _p(gate), _p(up), gate.stride(0), _p(out), cols, _dt(gate), rows, cols,
+             _stream(gate))
+        return out
     g, u = gate.contiguous(), up.contiguous()
     out = torch.empty_like(g)
     call("spark_silu_mul", _p(g), _p(u), _p(out), _dt(g), g.numel(), _stream(g))

@@ -50,17 +50,20 @@ class TPMLP(torch.nn.Module):
     def __init__(self, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor, rank: int = 0, world: int = 1,
                  group=None):
         super().__init__()
-        from .inference_v3 import V3PackedLinear
+        from .inference_v3 import V3MergedLinear, V3PackedLinear
         from . import ops
         self.world, self.group = world, group
         g, u, d = shard_rows(gate, rank, world), shard_rows(up, rank, world), shard_cols(down, rank, world)
-        self.gate = V3PackedLinear("spfp2", ops.spfp2_pack(g.contiguous())[0], g.shape[0], g.shape[1])
-        self.up = V3PackedLinear("spfp2", ops.spfp2_pack(u.contiguous())[0], u.shape[0], u.shape[1])
+        gate_l = V3PackedLinear("spfp2", ops.spfp2_pack(g.contiguous())[0], g.shape[0], g.shape[1])
+        up_l = V3PackedLinear("spfp2", ops.spfp2_pack(u.contiguous())[0], u.shape[0], u.shape[1])
+        # gate and up read the same x: one row-merged weight, one launch
+        self.gate_up = V3MergedLinear([gate_l, up_l])
         self.down = V3PackedLinear("spfp2", ops.spfp2_pack(d.contiguous())[0], d.shape[0], d.shape[1])
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         from . import ops
-        y = self.down(ops.silu_mul(self.gate(x), self.up(x)))
+        g, u = self.gate_up(x)
+        y = self.down(ops.silu_mul(g, u))
         if self.world > 1:
             dist.all_reduce(y, group=self.group)
         return y

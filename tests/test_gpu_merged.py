@@ -52,3 +52,33 @@ def test_merged_parts_match(fmt, ocs, ic, M):
     for (layer, _, _), y in zip(parts, merged(xb)):
         assert y.dtype == torch.bfloat16
         assert torch.allclose(y.float(), layer(xb).float(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_silu_mul_on_merged_halves(dtype):
+    from spark_b200 import ops
+    gu = torch.randn(37, 2 * 300, device="cuda", generator=torch.Generator(device="cuda").manual_seed(3)).to(dtype)
+    g, u = gu.split(300, dim=-1)
+    out = ops.silu_mul(g, u)
+    ref = torch.nn.functional.silu(g.float()) * u.float()
+    assert out.shape == (37, 300) and out.is_contiguous()
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert torch.allclose(out.float(), ref, rtol=tol, atol=tol)
+    assert torch.equal(out, ops.silu_mul(g.contiguous(), u.contiguous()))
+
+
+def test_tp_mlp_single_rank_matches_fp64():
+    from spark_b200 import ops
+    from spark_b200.tp import TPMLP
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    H, I = 512, 1024
+    gate = torch.randn(I, H, device="cuda", generator=gen) * 0.05
+    up = torch.randn(I, H, device="cuda", generator=gen) * 0.05
+    down = torch.randn(H, I, device="cuda", generator=gen) * 0.05
+    mlp = TPMLP(gate, up, down)
+    x = torch.randn(64, H, device="cuda", generator=gen)
+    dec = lambda w: ops.spfp2_unpack(ops.spfp2_pack(w)[0], w.numel()).view_as(w).double()
+    h = torch.nn.functional.silu(x.double() @ dec(gate).T) * (x.double() @ dec(up).T)
+    want = h @ dec(down).T
+    got = mlp(x).double()
+    assert (got - want).abs().max().item() <= 1e-3 * max(1.0, want.abs().max().item())
