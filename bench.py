@@ -371,7 +371,7 @@ def run_gpu(args, rank, world, local):
                      "achieved": round(spfp2_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(spfp2_gbs / peak, 4), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
                      if peak_kind == "measured" else "fallback 6650 GB/s",
-                     "traffic": traffic},
+                     "traffic": traffic, "bytes_per_launch": round(SPFP2_BYTES / (LAYERS * 2))},
         "gpu_launches": launches,
         "per_projection": {"value": round(value_pp, 1), "unit": "GB/s", "ms_per_step": round(ms_pp / args.steps, 4),
                            "gpu_launches": launches_pp},
