@@ -355,9 +355,9 @@ def run_gpu(args, rank, world, local):
     value = world * STEP_BYTES * args.steps / (ms_total * 1e-3) / 1e9
     spfp2_gbs = SPFP2_BYTES * args.steps / (ms_spfp2 * 1e-3) / 1e9
     e2e_gbs = world * STEP_BYTES * args.steps / (ms_e2e * 1e-3) / 1e9
-    # SPFP2 with bf16 x: one GEMV launch; FP3 / NVFP4: activation prepare + GEMV
-    launches = args.steps * LAYERS * sum(1 if f == "spfp2" else 2 for _, f, _ in GROUPS)
-    launches_pp = args.steps * LAYERS * sum(1 if f == "spfp2" else 2 for _, f, _, _ in SHAPES)
+    # bf16 x on the tiled weights: one GEMV launch per linear, every format
+    launches = args.steps * LAYERS * len(GROUPS)
+    launches_pp = args.steps * LAYERS * len(SHAPES)
     value_pp = world * STEP_BYTES * args.steps / (ms_pp * 1e-3) / 1e9
     traffic = load_traffic()
     line = {

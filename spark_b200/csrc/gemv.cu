@@ -120,6 +120,12 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
     return d;
 }
 
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 // two e4m3 bytes (low 16 bits of a) -> f16x2, exact
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t a) {
     uint32_t d;
@@ -250,6 +256,37 @@ __device__ __forceinline__ void decode_nvfp4(const uint32_t* c, uint32_t scale_w
     e2m1x8_to_f16x2(c[s], u);
 #pragma unroll
     for (int j = 0; j < 4; ++j) A[j] = hmul2(u[j], s2);
+}
+
+// FP3 / NVFP4 for a bf16 MMA on the caller's bf16 x (no prepared copy): the
+// natural column pair (2j, 2j+1) is one field of the packed codes -- FP3 the
+// 6 bits at 6j of the step's 24-bit group, NVFP4 byte j of the step's word --
+// and indexes a shared-memory table of unscaled bf16x2 values; one bf16x2
+// multiply by the block's e4m3 scale (also tabled as bf16x2) finishes the
+// pair.  Exact: an FP3 / e2m1 value has at most 2 significant bits, an e4m3
+// scale at most 4, so every product fits bf16's 8.
+template <int FMT>
+__device__ __forceinline__ void decode_scaled_bf16(const uint32_t* c, uint32_t scale_word, int s,
+                                                   const uint32_t* pair_tab, const uint32_t* scale_tab, uint32_t* A) {
+    const uint32_t s2 = scale_tab[(scale_word >> (8 * (s >> 1))) & 0xffu];
+    if constexpr (FMT == SPARK_FMT_FP3) {
+        const uint32_t v = window<6>(c, 24 * s);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) A[j] = bmul2(pair_tab[(v >> (6 * j)) & 63u], s2);
+    } else {
+        const uint32_t v = c[s];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) A[j] = bmul2(pair_tab[(v >> (8 * j)) & 0xffu], s2);
+    }
+}
+
+// bf16 bits of an FP3 (3-bit) or e2m1 (4-bit) code: sign in the top bit,
+// magnitudes 0, .5, 1, 1.5 (FP3) or 0, .5, 1, 1.5, 2, 3, 4, 6 (e2m1)
+__device__ __forceinline__ uint32_t code_bf16(int fmt, uint32_t code) {
+    const int bits = fmt == SPARK_FMT_FP3 ? 3 : 4;
+    const uint32_t mag = code & ((1u << (bits - 1)) - 1u), neg = code >> (bits - 1);
+    const float tab[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    return (__float_as_uint(tab[mag]) >> 16) | (neg << 15);
 }
 
 // 2:4 SPFP2 (two_four.py:158-189): 28-bit slot per 16-block, 4 groups of 4
@@ -772,9 +809,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
     constexpr int FW = frag_words<FMT>();
     constexpr int NV = FW / 4;
     constexpr int UB = unit_bytes_tiled<FMT>();
-    static_assert(!BF || FMT == SPARK_FMT_SPFP2 || FMT == SPARK_FMT_TWOFOUR, "bf16 path: SPFP2 / 2:4 only");
+
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint2 lut[16];
+    __shared__ uint32_t pair_tab[FMT == SPARK_FMT_FP3 || FMT == SPARK_FMT_NVFP4 ? 256 : 1];
+    __shared__ uint32_t scale_tab[FMT == SPARK_FMT_FP3 || FMT == SPARK_FMT_NVFP4 ? 256 : 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     // ring slot (stage, vector) of this thread: 16 bytes each
@@ -803,6 +842,18 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
             const uint32_t E = 117u + threadIdx.x;
             const uint32_t H = E >> 1, L = (E & 1u) << 7;
             lut[threadIdx.x] = make_uint2(H * 0x101u + 0x8000u, L * 0x101u);
+        }
+        __syncthreads();
+    }
+    if constexpr (BF && (FMT == SPARK_FMT_FP3 || FMT == SPARK_FMT_NVFP4)) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+            // e4m3 values are exact in bf16: the top half of the fp32 bits
+            const uint32_t sb = __float_as_uint(e4m3_to_f32((uint32_t)i)) >> 16;
+            scale_tab[i] = sb | (sb << 16);
+            const int bits = FMT == SPARK_FMT_FP3 ? 3 : 4;
+            if (i < (1 << (2 * bits)))
+                pair_tab[i] = code_bf16(FMT, (uint32_t)i & ((1u << bits) - 1u)) |
+                              (code_bf16(FMT, (uint32_t)i >> bits) << 16);
         }
         __syncthreads();
     }
@@ -886,9 +937,12 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
                 if constexpr (FMT == SPARK_FMT_SPFP2) {
                     decode_spfp2_bf16(c0, s, lut, A0);
                     decode_spfp2_bf16(c1, s, lut, A1);
-                } else {
+                } else if constexpr (FMT == SPARK_FMT_TWOFOUR) {
                     decode_twofour_t<true>(c0, s, A0);
                     decode_twofour_t<true>(c1, s, A1);
+                } else {
+                    decode_scaled_bf16<FMT>(c0, sw0, s, pair_tab, scale_tab, A0);
+                    decode_scaled_bf16<FMT>(c1, sw1, s, pair_tab, scale_tab, A1);
                 }
                 uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
                 if (tok0) x0 = ldg_nc_v4(xb0 + col0 + 8 * s);
@@ -1150,9 +1204,7 @@ int launch_gemv_tiled(const GemvArgs& a, int64_t T, cudaStream_t stream) {
 
 template <int FMT>
 int launch_fmt_tiled(const GemvArgs& a, int NT, int XS, bool bf, int64_t T, cudaStream_t s) {
-    if constexpr (FMT == SPARK_FMT_SPFP2 || FMT == SPARK_FMT_TWOFOUR) {
-        if (bf) return NT == 1 ? launch_gemv_tiled<FMT, 1, 1, true>(a, T, s) : launch_gemv_tiled<FMT, 2, 1, true>(a, T, s);
-    }
+    if (bf) return NT == 1 ? launch_gemv_tiled<FMT, 1, 1, true>(a, T, s) : launch_gemv_tiled<FMT, 2, 1, true>(a, T, s);
     if (XS == 1) return NT == 1 ? launch_gemv_tiled<FMT, 1, 1, false>(a, T, s) : launch_gemv_tiled<FMT, 2, 1, false>(a, T, s);
     return NT == 1 ? launch_gemv_tiled<FMT, 1, 2, false>(a, T, s) : launch_gemv_tiled<FMT, 2, 2, false>(a, T, s);
 }
@@ -1312,9 +1364,8 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
         const int mc = (int)std::min<int64_t>(kMaxTokens, M - m0);
         const uint8_t* xb = static_cast<const uint8_t*>(x) + m0 * ldx * (x_dtype == SPARK_DTYPE_F32 ? 4 : 2);
         const int XS = x_dtype == SPARK_DTYPE_BF16 ? 1 : 2;
-        // SPFP2 / 2:4 on tiled weights with bf16 x: bf16 MMA straight on x, no prepare
-        const bool bf = tiled && x_dtype == SPARK_DTYPE_BF16 &&
-                        (fmt == SPARK_FMT_SPFP2 || fmt == SPARK_FMT_TWOFOUR) && (ldx % 8) == 0 && aligned(x, 16);
+        // tiled weights with bf16 x: bf16 MMA straight on x, no prepare launch
+        const bool bf = tiled && x_dtype == SPARK_DTYPE_BF16 && (ldx % 8) == 0 && aligned(x, 16);
         a.x_raw = xb;
         a.ldx = ldx;
         const int perm = fmt == SPARK_FMT_FP3 ? kPermFp3 : (fmt == SPARK_FMT_SPFP2 && !tiled ? kPermSpfp2 : kPermNatural);
