@@ -843,19 +843,30 @@ int launch_n(int N, const CUtensorMap& wmap, const CUtensorMap& smap, const CUte
         case 16: return launch<FMT, 16>(wmap, smap, xmap, p, s);
         case 64: return launch<FMT, 64>(wmap, smap, xmap, p, s);
         case 128: return launch<FMT, 128>(wmap, smap, xmap, p, s);
+        case 192: return launch<FMT, 192>(wmap, smap, xmap, p, s);
         default: return launch<FMT, 256>(wmap, smap, xmap, p, s);
     }
 }
 
-// Tokens per tile.  Above 128 tokens: 256 unless 128-token tiles need far
-// fewer token-rows per CTA once whole jobs are dealt out in rounds (per flop
-// a 128-token tile runs ~35% slower: the same decode feeds half the MMA work).
+// Tokens per tile.  Above 128 tokens: the tile of 128, 192 or 256 tokens that
+// needs the fewest token-rows per CTA once whole jobs are dealt out in rounds,
+// weighted by the per-flop cost of a narrower tile (the same decode feeds
+// less MMA work: ~35% slower at 128 tokens, ~13% at 192).  A 2560-row layer at
+// 2048 tokens: 160 jobs of 256 tokens take two rounds on 148 SMs, the second
+// nearly empty; 220 jobs of 192 take the same two rounds with 25% less work
+// per job.
 int token_tile(int64_t M, int64_t n_rb, int ctas) {
     if (M <= 16) return 16;
     if (M <= 64) return 64;
     if (M <= 128) return 128;
-    auto rounds = [&](int64_t n) { return (n_rb * ((M + n - 1) / n) + ctas - 1) / ctas; };
-    return (double)rounds(128) * 128 * 1.4 < (double)rounds(256) * 256 ? 128 : 256;
+    auto cost = [&](int64_t n, double per_flop) {
+        return (double)((n_rb * ((M + n - 1) / n) + ctas - 1) / ctas) * (double)n * per_flop;
+    };
+    int best = 256;
+    double c = cost(256, 1.0);
+    if (cost(192, 1.13) < c) { best = 192; c = cost(192, 1.13); }
+    if (cost(128, 1.4) < c) best = 128;
+    return best;
 }
 
 }  // namespace tc
