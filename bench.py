@@ -331,11 +331,14 @@ def run_gpu(args, rank, world, local):
     # ---------------- prefill: PREFILL_M bf16 tokens through the
     # 7 linears of one layer, reference-layout weights -> the tcgen05 GEMM
     xs = {ic: torch.randn(PREFILL_M, ic, device=device, generator=g).bfloat16() for ic in (2560, 4096, 9728)}
-    ys = {name: torch.empty(PREFILL_M, oc, device=device, dtype=torch.bfloat16) for name, _, oc, _ in SHAPES}
+
+    yg = {name: torch.empty(PREFILL_M, oc, device=device, dtype=torch.bfloat16)
+          for name, (_, _, _, oc, _, _) in merged[0].items()}
 
     def prefill_step():
-        for name, (fmt, wq, s, oc, ic, _) in layers[0].items():
-            ops.linear(fmt, wq, s, xs[ic], oc, ic, out=ys[name])
+        # the row-merged launches of the decode step, on the reference-layout bytes
+        for name, (fmt, wq, s, oc, ic, _) in merged[0].items():
+            ops.linear(fmt, wq, s, xs[ic], oc, ic, out=yg[name])
 
     with torch.cuda.stream(stream):
         prefill_step()
@@ -380,8 +383,8 @@ def run_gpu(args, rank, world, local):
         "clocks": clk.summary(),
         "prefill": {
             "workload": f"BASELINE config 3: M={PREFILL_M} bf16 tokens through the 7 linears of one layer "
-                        "(SPFP2 gate/up/down, FP3 q/k/v, NVFP4 out_proj), reference-layout weights, "
-                        "one CUDA graph per step",
+                        "(SPFP2 gate/up/down, FP3 q/k/v, NVFP4 out_proj) as 4 row-merged launches (q|k|v, "
+                        "out, gate|up, down), reference-layout weights, one CUDA graph per step",
             "value": round(pre_tflops, 1), "unit": "TFLOP/s", "steps": pre_steps,
             "ms_per_step": round(ms_pre / pre_steps, 4), "flops_per_step": pre_flops,
             "kernel": "k_tc_linear<FMT, 128 or 256 tokens> (tcgen05.mma kind::f16, A = decoded weights in TMEM)",
