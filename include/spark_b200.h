@@ -103,6 +103,14 @@ SPARK_API int spark_nvfp4_pack(const void* w, int w_dtype, int64_t oc, int64_t i
 /* nvfp4_unpack -- 01_core/nvfp4_emu.py:109. */
 SPARK_API int spark_nvfp4_unpack(const uint8_t* codes, const uint8_t* scales, int64_t oc, int64_t ic, void* out,
                        int out_dtype, void* stream);
+/* NVFP4 embedding lookup -- the forward of NVFP4EmbeddingQAT, 02_model/quant_linear.py:527-537
+ * (F.embedding of the NVFP4 table), on the packed table (codes [rows, pad16(dim)/2], scales
+ * [rows, pad16(dim)/16]): out[i, :] = decode(row ids[i]), int64 ids.  An id outside
+ * [0, num_embeddings) gives a zero row and, when err is non-null, stores error code 7 there (pass
+ * a spark_linear workspace and read it with spark_workspace_check). */
+SPARK_API int spark_nvfp4_embedding(const uint8_t* codes, const uint8_t* scales, int64_t num_embeddings, int64_t dim,
+                                    const int64_t* ids, int64_t n_ids, void* out, int out_dtype, int* err,
+                                    void* stream);
 /* nvfp4_fake_quant -- 01_core/nvfp4_emu.py:37 (NVFP4STE backward is the identity, :66-68). */
 SPARK_API int spark_nvfp4_fake_quant(const void* w, int w_dtype, int64_t oc, int64_t ic, void* out, int out_dtype,
                            void* stream);

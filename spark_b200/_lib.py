@@ -83,6 +83,7 @@ _SIGNATURES = {
     "spark_tile_weights": (_i, [_i, _p, _p, _i64, _i64, _p, _p]),
     "spark_silu_mul": (_i, [_p, _p, _p, _i, _i64, _p]),
     "spark_silu_mul_rows": (_i, [_p, _p, _i64, _p, _i64, _i, _i64, _i64, _p]),
+    "spark_nvfp4_embedding": (_i, [_p, _p, _i64, _i64, _p, _i64, _p, _i, _p, _p]),
 }
 
 _lib = None

@@ -1443,7 +1443,8 @@ int spark_workspace_check(void* workspace, void* stream) {
     if (e != cudaSuccess) return set_error((int)e, "spark_workspace_check: %s", cudaGetErrorString(e));
     if (flag != 0) {
         cudaMemsetAsync(workspace, 0, sizeof(int), s);
-        return set_error(SPARK_ERR_DEVICE, "a kernel reported error %d (bounded wait expired)", flag);
+        return set_error(SPARK_ERR_DEVICE, "a kernel reported error %d (%s)", flag,
+                         flag == 7 ? "embedding id out of range" : "bounded wait expired");
     }
     return SPARK_OK;
 }

@@ -415,6 +415,39 @@ __global__ void __launch_bounds__(kThreads) k_nvfp4_unpack(const uint8_t* __rest
     }
 }
 
+// NVFP4 embedding lookup: out[i, :] = decode(row ids[i]) of a packed
+// [num_embeddings, dim] table -- the forward of NVFP4EmbeddingQAT
+// (quant_linear.py:507-537, F.embedding of the quantised table) reading only
+// the looked-up rows' codes.  One thread per (id, 16-block), the arithmetic
+// of k_nvfp4_unpack.  An id outside [0, num_embeddings) yields a zero row
+// and records error code 7 in *err (the caller's workspace word).
+__global__ void __launch_bounds__(kThreads) k_nvfp4_embedding(const uint8_t* __restrict__ codes,
+                                                              const uint8_t* __restrict__ scales, int64_t rows,
+                                                              int64_t dim, const int64_t* __restrict__ ids,
+                                                              int64_t n_ids, void* __restrict__ out, int dtype,
+                                                              int* err) {
+    const int64_t nbr = (dim + 15) / 16;
+    const int64_t t = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    if (t >= n_ids * nbr) return;
+    const int64_t i = t / nbr, blk = t - i * nbr, c0 = blk * 16;
+    const int64_t r = ids[i];
+    if (r < 0 || r >= rows) {
+        if (blk == 0) report_device_error(err, 7);
+        for (int k = 0; k < 16; ++k)
+            if (c0 + k < dim) store_from_float(out, dtype, i * dim + c0 + k, 0.0f);
+        return;
+    }
+    const int64_t b = r * nbr + blk;
+    const float s = e4m3_to_f32(scales[b]);
+    const uint8_t* q = codes + 8 * b;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const uint32_t code = (k & 1) ? (q[k / 2] >> 4) : (q[k / 2] & 0xf);
+        const float v = code < 8 ? kE2m1Pos[code] : -kE2m1Pos[code - 8];
+        if (c0 + k < dim) store_from_float(out, dtype, i * dim + c0 + k, scaled(v, s));
+    }
+}
+
 // nvfp4_fake_quant: sign(x) * E2M1(|x|) * s with sign(NaN) = 0 (nvfp4_emu.py:26-30)
 __global__ void __launch_bounds__(kThreads) k_nvfp4_fake_quant(const void* __restrict__ w, int in_dtype, int64_t oc,
                                                                int64_t ic, void* __restrict__ out, int out_dtype) {
@@ -681,6 +714,20 @@ int spark_nvfp4_unpack(const uint8_t* codes, const uint8_t* scales, int64_t oc, 
     if (nb == 0) return SPARK_OK;
     k_nvfp4_unpack<<<grid_for(nb), kThreads, 0, S(stream)>>>(codes, scales, oc, ic, out, out_dtype);
     return check_launch("spark_nvfp4_unpack");
+}
+
+int spark_nvfp4_embedding(const uint8_t* codes, const uint8_t* scales, int64_t num_embeddings, int64_t dim,
+                          const int64_t* ids, int64_t n_ids, void* out, int out_dtype, int* err, void* stream) {
+    SPARK_REQUIRE(num_embeddings >= 0 && dim >= 0 && n_ids >= 0, SPARK_ERR_INVALID,
+                  "spark_nvfp4_embedding: negative size");
+    if (n_ids == 0 || dim == 0) return SPARK_OK;
+    SPARK_REQUIRE(codes && scales && out && ids, SPARK_ERR_INVALID, "spark_nvfp4_embedding: null pointer");
+    SPARK_REQUIRE(dtype_ok(out_dtype), SPARK_ERR_INVALID, "spark_nvfp4_embedding: bad dtype %d", out_dtype);
+    const int64_t n = n_ids * ((dim + 15) / 16);
+    if (n == 0) return SPARK_OK;
+    k_nvfp4_embedding<<<grid_for(n), kThreads, 0, S(stream)>>>(codes, scales, num_embeddings, dim, ids, n_ids, out,
+                                                               out_dtype, err);
+    return check_launch("spark_nvfp4_embedding");
 }
 
 int spark_nvfp4_fake_quant(const void* w, int w_dtype, int64_t oc, int64_t ic, void* out, int out_dtype,

@@ -156,12 +156,47 @@ class V3SPFP2Layer(V3PackedLinear):
         super().__init__("spfp2", packed_weight, out_features, in_features, bias=bias)
 
 
+class V3NVFP4Embedding(nn.Module):
+    """Packed-resident NVFP4 embedding table: the inference form of
+    quant_linear.NVFP4EmbeddingQAT (quant_linear.py:507-537), whose forward is
+    F.embedding of the NVFP4-quantised table.  Codes [rows, pad16(dim)/2] and
+    e4m3 scales [rows, pad16(dim)/16] stay on the GPU; a lookup decodes only
+    the rows it reads.  padding_idx only affects gradients, as in
+    F.embedding, so the forward ignores it."""
+
+    def __init__(self, codes: torch.Tensor, scales: torch.Tensor, num_embeddings: int, embedding_dim: int,
+                 padding_idx=None, dtype=torch.bfloat16):
+        super().__init__()
+        self.num_embeddings = num_embeddings
+        self.embedding_dim = embedding_dim
+        self.padding_idx = padding_idx
+        self.dtype = dtype
+        self.register_buffer("codes", codes.view(torch.uint8))
+        self.register_buffer("scales", scales.view(torch.uint8))
+
+    def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        return ops.nvfp4_embedding(self.codes, self.scales, self.num_embeddings, self.embedding_dim, input_ids,
+                                   dtype=self.dtype)
+
+    def extra_repr(self) -> str:
+        return f"{self.num_embeddings}, {self.embedding_dim}, nvfp4"
+
+
 def build_v3_layers(model: nn.Module, state: dict, device="cuda") -> int:
     """Replace every nn.Linear that has packed weights in `state` by a packed-
     resident layer (the reference's build_v3_model, inference_v3.py:60-105,
-    extended from MLP SPFP2 to every tier).  Returns the number replaced."""
+    extended from MLP SPFP2 to every tier), and every nn.Embedding with NVFP4
+    codes by a V3NVFP4Embedding.  Returns the number replaced."""
     n = 0
     for name, module in list(model.named_modules()):
+        if isinstance(module, nn.Embedding) and name + "_nvfp4_codes" in state and name + "_meta" in state:
+            rows, dim = (int(v) for v in state[name + "_meta"][:2])
+            emb = V3NVFP4Embedding(state[name + "_nvfp4_codes"].to(device), state[name + "_nvfp4_scales"].to(device),
+                                   rows, dim, padding_idx=module.padding_idx, dtype=module.weight.dtype)
+            parent = model.get_submodule(".".join(name.split(".")[:-1])) if "." in name else model
+            setattr(parent, name.split(".")[-1], emb)
+            n += 1
+            continue
         if not isinstance(module, nn.Linear):
             continue
         fmt = None

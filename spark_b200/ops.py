@@ -166,6 +166,23 @@ def nvfp4_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------ 2:4
+def nvfp4_embedding(codes: torch.Tensor, scales: torch.Tensor, num_embeddings: int, dim: int,
+                    ids: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
+    """Rows `ids` of a packed NVFP4 [num_embeddings, dim] table, decoded:
+    F.embedding(ids, nvfp4_unpack(table)) without unpacking the table.  Out-of-
+    range ids give zero rows and an error that check_device_errors() raises."""
+    if not ids.is_cuda:
+        raise RuntimeError("spark_b200.nvfp4_embedding: ids must be a CUDA tensor")
+    flat = ids.reshape(-1).to(torch.int64).contiguous()
+    out = torch.empty(flat.numel(), dim, dtype=dtype, device=ids.device)
+    if out.numel() == 0:
+        return out.reshape(*ids.shape, dim)
+    ws = workspace(ids.device, 1 << 20)
+    call("spark_nvfp4_embedding", _p(_bytes(codes)), _p(_bytes(scales)), num_embeddings, dim, _p(flat), flat.numel(),
+         _p(out), _dt(out), _p(ws), _stream(ids))
+    return out.reshape(*ids.shape, dim)
+
+
 def twofour_pack(w: torch.Tensor) -> torch.Tensor:
     x = _cuda(w.detach())
     oc, ic = x.shape
