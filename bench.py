@@ -496,8 +496,9 @@ def run_tp_mlp(args, rank, world, local):
     parallel over the `world` ranks (gate/up column-parallel, down row-parallel
     + one NCCL all-reduce per layer).  Prints its own JSON line."""
     from spark_b200 import ops
-    from spark_b200.tp import TPMLP
+    from spark_b200.tp import TPMLP, PeerAllReduce
     device = torch.device("cuda", local)
+    peer = PeerAllReduce(TP_M * TP_H, dtype=torch.float32) if args.tp_allreduce == "peer" else None
     g = torch.Generator(device=device)
     layers = []
     for li in range(TP_LAYERS):
@@ -505,7 +506,7 @@ def run_tp_mlp(args, rank, world, local):
         gate = torch.randn(TP_I, TP_H, device=device, generator=g) * 0.015
         up = torch.randn(TP_I, TP_H, device=device, generator=g) * 0.015
         down = torch.randn(TP_H, TP_I, device=device, generator=g) * 0.015
-        layers.append(TPMLP(gate, up, down, rank, world))
+        layers.append(TPMLP(gate, up, down, rank, world, peer=peer))
         del gate, up, down
     g.manual_seed(4)
     x0 = torch.randn(TP_M, TP_H, device=device, generator=g).bfloat16()
@@ -546,8 +547,13 @@ def run_tp_mlp(args, rank, world, local):
     ms = max_over_ranks(e0.elapsed_time(e1), world)
     finite = bool(torch.isfinite(out["y"].float()).all().item())
     ops.check_device_errors()
+    if peer is not None:
+        peer.check()
     barrier(world)
     del graph
+    if peer is not None:
+        peer.close()
+        barrier(world)
     packed_total = TP_LAYERS * 3 * (TP_I * TP_H // 16 * 5)
     peak, peak_kind = peaks()
     sec = ms * 1e-3 / k
@@ -559,7 +565,9 @@ def run_tp_mlp(args, rank, world, local):
                          "peak_source": peak_kind},
             "config": {"workload": "BASELINE config 4: 32 x (gate/up [12288,4096], down [4096,12288]) SPFP2, "
                                    "N(0,0.015), M=64 bf16, SiLU(gate)*up", "tp": world,
-                       "parallelism": f"tp{world}: gate/up column-parallel, down row-parallel + NCCL all-reduce",
+                       "parallelism": f"tp{world}: gate/up column-parallel, down row-parallel + "
+                                      + ("one-shot peer all-reduce (spark_peer_allreduce, fp32 partials)"
+                                         if peer is not None else "NCCL all-reduce"),
                        "graph": bool(args.tp_graph)},
             "finite": finite}
     if rank == 0:
@@ -650,6 +658,8 @@ def main():
     ap.add_argument("--copies", type=int, default=0, help="profile mode: weight copies to rotate over")
     ap.add_argument("--tp-mlp", action="store_true", help="run the config-4 tensor-parallel MLP stack instead")
     ap.add_argument("--tp-graph", type=int, default=1, help="tp-mlp: replay each step as a CUDA graph")
+    ap.add_argument("--tp-allreduce", default="nccl", choices=["nccl", "peer"],
+                    help="tp-mlp: all-reduce of the down projection's partial sums")
     ap.add_argument("--oc", type=int, default=0, help="profile mode: output features")
     ap.add_argument("--ic", type=int, default=0, help="profile mode: input features")
     args = ap.parse_args()

@@ -227,6 +227,27 @@ SPARK_API int spark_workspace_check(void* workspace, void* stream);
 /* Elementwise SiLU(gate) * up for the MLP between the gate/up and down projections
  * (the activation the reference model applies between its MLP linears). */
 SPARK_API int spark_silu_mul(const void* gate, const void* up, void* out, int dtype, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------- peer all-reduce (tensor parallel)
+ * One-shot all-reduce of the row-parallel down projection's partial sums over
+ * peer memory, the NCCL all-reduce of the tensor-parallel MLP (config 4)
+ * done by this library.  bufs[r] = rank r's partial (fp32 or bf16, n
+ * elements, mapped into this process), flags[r] = rank r's flag array of
+ * spark_peer_flags_count(world) zeroed ints; epochs = this rank's
+ * spark_peer_flags_count(1) zeroed ints; err = an error word (code 5 when a peer did not arrive within 2 s).
+ * Every rank issues the same sequence of calls; a rank may overwrite its
+ * partial buffer only after the next call's barrier (alternate two buffers).
+ * out = sum over ranks 0..world-1 in that order (fp32), identical on every rank. */
+#define SPARK_MAX_PEERS 8
+#define SPARK_IPC_HANDLE_BYTES 64
+SPARK_API int spark_peer_flags_count(int world);
+SPARK_API int spark_peer_allreduce(const void* const* bufs, int* const* flags, int world, int rank, int64_t n,
+                                   int in_dtype, void* out, int out_dtype, int* epochs, int* err, void* stream);
+/* Legacy CUDA IPC: handle (SPARK_IPC_HANDLE_BYTES) + offset of the allocation holding ptr;
+ * open maps another process's buffer on the current device; close unmaps it. */
+SPARK_API int spark_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+SPARK_API int spark_ipc_open(const void* handle, int64_t offset, void** ptr);
+SPARK_API int spark_ipc_close(void* ptr, int64_t offset);
 /* SiLU(gate) * up over [rows, cols] with gate / up rows ld_in elements apart
  * (the halves of a row-merged gate|up output) and out rows ld_out apart. */
 SPARK_API int spark_silu_mul_rows(const void* gate, const void* up, int64_t ld_in, void* out, int64_t ld_out,

@@ -78,7 +78,9 @@ class V3PackedLinear(nn.Module):
         b = state.get(f"param::{name}.bias")
         return cls(fmt, packed, oc, ic, scales=scales, bias=b.to(device) if b is not None else None)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """out: optional preallocated [M, out_features] result (its dtype is the
+        output dtype; x.dtype otherwise)."""
         ic = self.in_features
         if self.fmt in ("spfp2", "spfp2_v1") and ic % 8:
             # the layer classes pack rows padded to whole 8-blocks (quant_linear.py:183-192)
@@ -89,9 +91,9 @@ class V3PackedLinear(nn.Module):
         # GEMM, which reads the reference-layout bytes
         if self.w_tiled is not None and ic == self.in_features and x.numel() <= 16 * ic:
             return ops.linear(self.fmt, self.w_tiled, None, x, self.out_features, ic, bias=self.bias,
-                              out_dtype=x.dtype, tiled=True)
+                              out_dtype=x.dtype, out=out, tiled=True)
         return ops.linear(self.fmt, self.w_packed, self.w_scales, x, self.out_features, ic,
-                          bias=self.bias, out_dtype=x.dtype)
+                          bias=self.bias, out_dtype=x.dtype, out=out)
 
     def extra_repr(self) -> str:
         return f"fmt={self.fmt}, in_features={self.in_features}, out_features={self.out_features}"

@@ -40,6 +40,125 @@ def shard_cols(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     return w[:, lo:hi]
 
 
+# Peer allocations mapped into this process: IPC handle -> [base pointer,
+# users].  A handle names a whole allocation, and one allocation can hold
+# several shared buffers; CUDA maps it once per process.
+_IPC_MAPS: dict[bytes, list] = {}
+
+
+def _ipc_map(handle: bytes) -> int:
+    import ctypes
+    from . import _lib
+    m = _IPC_MAPS.get(handle)
+    if m is None:
+        p = ctypes.c_void_p()
+        _lib.call("spark_ipc_open", (ctypes.c_uint8 * 64).from_buffer_copy(handle), 0, ctypes.byref(p))
+        m = _IPC_MAPS[handle] = [p.value, 0]
+    m[1] += 1
+    return m[0]
+
+
+def _ipc_unmap(handle: bytes) -> None:
+    import ctypes
+    from . import _lib
+    m = _IPC_MAPS[handle]
+    m[1] -= 1
+    if m[1] == 0:
+        _lib.call("spark_ipc_close", ctypes.c_void_p(m[0]), 0)
+        del _IPC_MAPS[handle]
+
+
+class PeerAllReduce:
+    """One-shot all-reduce of per-rank partial sums over peer memory
+    (spark_peer_allreduce): the NCCL all-reduce after the row-parallel down
+    projection, done by this library's kernel on NVLink peer loads.
+
+    Each rank owns two alternating partial buffers of `numel` elements and a
+    flag array; their CUDA IPC handles are exchanged once through the process
+    group, so every rank maps every other rank's buffers.  Use:
+    ``buf = ar.buffer()``, write this rank's partial into it (e.g. as the
+    down projection's output), then ``ar(out)``.  Every rank must make the same
+    sequence of calls; a captured CUDA graph must hold an even number of them
+    (the buffers alternate by call)."""
+
+    def __init__(self, numel: int, dtype=torch.float32, group=None):
+        import ctypes
+        from . import _lib
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 8:
+            raise ValueError("PeerAllReduce: at most 8 ranks")
+        self.numel = numel
+        self.dtype = dtype
+        dev = torch.device("cuda", torch.cuda.current_device())
+        L = _lib.lib()
+        self._lib, self._ct = L, ctypes
+        n_pad = (numel + 7) // 8 * 8
+        self.local = torch.zeros(2, n_pad, dtype=dtype, device=dev)
+        self.flags = torch.zeros(L.spark_peer_flags_count(self.world), dtype=torch.int32, device=dev)
+        self.epochs = torch.zeros(L.spark_peer_flags_count(1), dtype=torch.int32, device=dev)
+        self.err = torch.zeros(64, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+
+        def handle(t):
+            h = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_int64(0)
+            _lib.call("spark_ipc_handle", ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off))
+            return bytes(h), off.value
+
+        mine = (handle(self.local), handle(self.flags))
+        every = [mine]
+        if self.world > 1:
+            every = [None] * self.world
+            dist.all_gather_object(every, mine, group=group)
+        self._opened = []
+        bufs, flags = [], []
+        for r, ((hb, ob), (hf, of)) in enumerate(every):
+            if r == self.rank:
+                bufs.append(self.local.data_ptr())
+                flags.append(self.flags.data_ptr())
+                continue
+            bufs.append(_ipc_map(hb) + ob)
+            flags.append(_ipc_map(hf) + of)
+            self._opened += [hb, hf]
+        half = n_pad * self.local.element_size()
+        P = ctypes.c_void_p * self.world
+        self._bufs = [P(*[b + k * half for b in bufs]) for k in (0, 1)]
+        self._flags = P(*flags)
+        self.calls = 0
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def buffer(self) -> torch.Tensor:
+        """This rank's partial buffer for the next call."""
+        return self.local[self.calls % 2][: self.numel]
+
+    def __call__(self, out: torch.Tensor) -> torch.Tensor:
+        from . import _lib, ops
+        if out.numel() != self.numel or not out.is_contiguous():
+            raise ValueError("PeerAllReduce: out must be a contiguous tensor of numel elements")
+        ct = self._ct
+        _lib.call("spark_peer_allreduce", ct.cast(self._bufs[self.calls % 2], ct.c_void_p),
+                  ct.cast(self._flags, ct.c_void_p), self.world, self.rank, self.numel, ops._dt(self.local),
+                  ct.c_void_p(out.data_ptr()), ops._dt(out), ct.c_void_p(self.epochs.data_ptr()),
+                  ct.c_void_p(self.err.data_ptr()), ops._stream(out))
+        self.calls += 1
+        return out
+
+    def check(self) -> None:
+        """Raise if a call's barrier gave up waiting for a peer (synchronises)."""
+        from . import _lib
+        _lib.call("spark_workspace_check", self._ct.c_void_p(self.err.data_ptr()),
+                  self._ct.c_void_p(torch.cuda.current_stream().cuda_stream))
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers (after every call using them has finished)."""
+        torch.cuda.synchronize()
+        for h in self._opened:
+            _ipc_unmap(h)
+        self._opened = []
+
+
 class TPMLP(torch.nn.Module):
     """One SPFP2 MLP layer, tensor-parallel over the default process group:
     y = all_reduce( down_r( silu(gate_r x) * up_r x ) ).
@@ -48,8 +167,12 @@ class TPMLP(torch.nn.Module):
     given already packed via from_packed)."""
 
     def __init__(self, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor, rank: int = 0, world: int = 1,
-                 group=None):
+                 group=None, peer: PeerAllReduce | None = None):
+        """peer: a PeerAllReduce sized M x hidden replaces the NCCL all-reduce
+        (the down projection then writes its fp32 partial straight into the
+        peer buffer)."""
         super().__init__()
+        self.peer = peer
         from .inference_v3 import V3MergedLinear, V3PackedLinear
         from . import ops
         self.world, self.group = world, group
@@ -63,7 +186,12 @@ class TPMLP(torch.nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         from . import ops
         g, u = self.gate_up(x)
-        y = self.down(ops.silu_mul(g, u))
+        h = ops.silu_mul(g, u)
+        if self.peer is not None:
+            d = self.down
+            d(h, out=self.peer.buffer().view(h.shape[0], d.out_features))
+            return self.peer(torch.empty(h.shape[0], d.out_features, dtype=x.dtype, device=x.device))
+        y = self.down(h)
         if self.world > 1:
             dist.all_reduce(y, group=self.group)
         return y
