@@ -574,6 +574,79 @@ def run_tp_mlp(args, rank, world, local):
         print(json.dumps(line), flush=True)
 
 
+QAT_TOKENS, QAT_H, QAT_I = 8 * 4096, 2560, 9728     # BASELINE config 5 (QAT variant)
+
+
+def run_qat(args):
+    """BASELINE config 5, QAT variant: STE fake-quant forward + backward on the
+    gate/up/down projections (ChannelFP2QATLinear, bf16 weights) for a training
+    micro-batch of 8 x 4096 tokens, hidden 2560.  Each step bumps the weight
+    version (as an optimizer step does), so every step re-runs the SPFP2 window
+    search + fake quant of all three weights on the GPU; the linears and their
+    backward are torch GEMMs.  Reports the fake-quant kernels alone against the
+    HBM roofline (bf16 in + bf16 out per weight) and the whole step."""
+    from spark_b200 import ops
+    from spark_b200 import quant_linear as ql
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device).manual_seed(11)
+    layers = []
+    for name, oc, ic in (("gate", QAT_I, QAT_H), ("up", QAT_I, QAT_H), ("down", QAT_H, QAT_I)):
+        m = ql.ChannelFP2QATLinear(ic, oc, bias=False, device=device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            m.weight.copy_(torch.randn(oc, ic, device=device, generator=g) * 0.02)
+        layers.append(m.train())
+    gate, up, down = layers
+    x = torch.randn(QAT_TOKENS, QAT_H, device=device, generator=g).bfloat16().requires_grad_(True)
+
+    def step():
+        ql.bump_wq_version()
+        y = down(torch.nn.functional.silu(gate(x)) * up(x))
+        y.float().square().mean().backward()
+
+    def fq():
+        for m in layers:
+            ops.spfp2_fake_quant(m.weight.detach())
+
+    def timed(fn, k):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(k):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / k
+
+    ms_fq = timed(fq, max(20, args.steps))
+    ms_step = timed(step, max(5, args.steps // 20))
+    w_down = down.weight.detach()
+    ms_24 = timed(lambda: ops.twofour_fake_quant(w_down), max(20, args.steps))
+    ops.check_device_errors()
+    n_w = sum(m.weight.numel() for m in layers)
+    fq_bytes = n_w * 4                                  # bf16 weight in, bf16 fake-quant out
+    peak, peak_kind = peaks()
+    gbs = fq_bytes / (ms_fq * 1e-3) / 1e9
+    gbs24 = w_down.numel() * 4 / (ms_24 * 1e-3) / 1e9
+    flops = 3 * 2.0 * QAT_TOKENS * (2 * QAT_I * QAT_H + QAT_H * QAT_I)
+    print(json.dumps({
+        "metric": "config-5 QAT: SPFP2 STE fake-quant of gate/up/down + micro-batch step", "n_gpus": 1,
+        "fake_quant": {"ms": round(ms_fq, 4), "GBps": round(gbs, 1), "weights": n_w,
+                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                                    "frac": round(gbs / peak, 4), "peak_source": peak_kind}},
+        "twofour_fake_quant_down": {"ms": round(ms_24, 4), "GBps": round(gbs24, 1)},
+        "step": {"ms": round(ms_step, 3), "tokens_per_s": round(QAT_TOKENS / (ms_step * 1e-3), 1),
+                 "fake_quant_share": round(ms_fq / ms_step, 4),
+                 "gemm_TFLOPs": round(flops / (ms_step * 1e-3) / 1e12, 1),
+                 "note": "forward + backward of the three linears are torch (cuBLAS) GEMMs; the STE backward "
+                         "is the identity"},
+        "config": {"workload": "BASELINE config 5 QAT variant: ChannelFP2QATLinear gate/up [9728,2560], down "
+                               "[2560,9728], bf16, micro-batch 8x4096 tokens, hidden 2560, SiLU(gate)*up",
+                   "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)"}}), flush=True)
+
+
 def run_profile(args):
     """Timing of one linear shape on its own (also the target of ncu captures).
 
@@ -657,6 +730,7 @@ def main():
                     help="profile mode: tiled-layout GEMV, tcgen05 kernel, or reference-layout GEMV")
     ap.add_argument("--copies", type=int, default=0, help="profile mode: weight copies to rotate over")
     ap.add_argument("--tp-mlp", action="store_true", help="run the config-4 tensor-parallel MLP stack instead")
+    ap.add_argument("--qat", action="store_true", help="run the config-5 QAT fake-quant measurement instead")
     ap.add_argument("--tp-graph", type=int, default=1, help="tp-mlp: replay each step as a CUDA graph")
     ap.add_argument("--tp-allreduce", default="nccl", choices=["nccl", "peer"],
                     help="tp-mlp: all-reduce of the down projection's partial sums")
@@ -665,6 +739,9 @@ def main():
     args = ap.parse_args()
     if args.profile:
         run_profile(args)
+        return
+    if args.qat:
+        run_qat(args)
         return
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
