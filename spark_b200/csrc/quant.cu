@@ -37,6 +37,28 @@ __device__ __forceinline__ void load_block(const void* w, int dtype, int64_t bas
         }
         return;
     }
+    if (dtype != SPARK_DTYPE_F32 && N % 8 == 0 && base + N <= limit && ((base & 7) == 0) &&
+        aligned_dev(reinterpret_cast<const uint16_t*>(w) + base)) {
+        // 8 bf16 / fp16 values per 16-byte load
+        const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w) + base);
+#pragma unroll
+        for (int i = 0; i < N / 8; ++i) {
+            const uint4 q = __ldg(p + i);
+            const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (dtype == SPARK_DTYPE_BF16) {
+                    v[8 * i + 2 * k] = __uint_as_float(u[k] << 16);
+                    v[8 * i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+                } else {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+                    v[8 * i + 2 * k] = f.x;
+                    v[8 * i + 2 * k + 1] = f.y;
+                }
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < N; ++i) v[i] = (base + i < limit) ? load_as_float(w, dtype, base + i) : 0.0f;
 }
@@ -246,6 +268,21 @@ __global__ void __launch_bounds__(kThreads) k_spfp2_fake_quant(const void* __res
         float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + base);
         o[0] = make_float4(d[0], d[1], d[2], d[3]);
         o[1] = make_float4(d[4], d[5], d[6], d[7]);
+        return;
+    }
+    if (out_dtype != SPARK_DTYPE_F32 && aligned_dev(reinterpret_cast<uint16_t*>(out) + base)) {
+        uint32_t u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (out_dtype == SPARK_DTYPE_BF16) {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(d[2 * k], d[2 * k + 1]);
+                u[k] = *reinterpret_cast<const uint32_t*>(&h);
+            } else {
+                const __half2 h = __floats2half2_rn(d[2 * k], d[2 * k + 1]);
+                u[k] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+        }
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + base) = make_uint4(u[0], u[1], u[2], u[3]);
         return;
     }
 #pragma unroll
