@@ -66,6 +66,8 @@ CONFIG = {
     "graph": "each step replayed as one CUDA graph",
     "projections": "q|k|v and gate|up row-merged into one packed weight each (V3MergedLinear): 4 GEMV "
                    "launches per layer; per_projection repeats the step with one launch per linear",
+    "prefetch": "each GEMV requests the next launch's weight into L2 while it runs (chain_prefetch); every "
+                "weight is still read from HBM once per step",
 }
 METRIC = "dequant-GEMV HBM GB/s (% of 8 TB/s) at M=1; prefill dequant-GEMM TFLOP/s"
 PREFILL_M = 2048               # prefill tokens through one layer's 7 linears
@@ -240,12 +242,13 @@ def run_gpu(args, rank, world, local):
     ops.workspace(device, max_ws, stream=stream)
 
     def step(only=None, which=None):
-        for L in (which or merged):
-            for name, (fmt, wq, s, oc, ic, wt) in L.items():
-                if only and fmt != only:
-                    continue
-                key = (name, id(L))
-                outs[key] = ops.linear(fmt, wt, None, x[ic], oc, ic, out=outs.get(key), tiled=True)
+        # every decode GEMV pulls the next launch's weight into L2 (the last
+        # one the first's: the next token starts over)
+        seq = [((name, id(L)), fmt, oc, ic, wt) for L in (which or merged) for name, (fmt, _, _, oc, ic, wt)
+               in L.items() if not only or fmt == only]
+        for k, (key, fmt, oc, ic, wt) in enumerate(seq):
+            nxt = seq[(k + 1) % len(seq)][4]
+            outs[key] = ops.linear(fmt, wt, None, x[ic], oc, ic, out=outs.get(key), tiled=True, prefetch=nxt)
 
     # warm every path once eagerly (allocates outputs), then capture
     with torch.cuda.stream(stream):
@@ -288,12 +291,13 @@ def run_gpu(args, rank, world, local):
     ops.check_device_errors()
 
     # ---------------- e2e through the public layer API with host buffers
-    from spark_b200.inference_v3 import V3MergedLinear, V3PackedLinear
+    from spark_b200.inference_v3 import V3MergedLinear, V3PackedLinear, chain_prefetch
     mods = []
     for L in layers:
         lin = {name: V3PackedLinear.from_packed(fmt, wq, s, oc, ic) for name, (fmt, wq, s, oc, ic, _) in L.items()}
         mods.append({gname: V3MergedLinear([lin[p] for p in parts]) if len(parts) > 1 else lin[parts[0]]
                      for gname, _, parts in GROUPS})
+    chain_prefetch([L[gname] for L in mods for gname, _, _ in GROUPS])
     xh = {ic: x[ic].cpu().pin_memory() for ic in x}
     yh = {}
     for L in mods:
@@ -685,8 +689,10 @@ def run_profile(args):
     stream = torch.cuda.Stream(device)
 
     def one_pass():
-        for (wq, s), y in zip(ws, ys):
-            ops.linear(args.profile, wq, s, x, oc, ic, out=y, tiled=args.path == "tiled", tcgen05=args.path == "tc")
+        for k, ((wq, s), y) in enumerate(zip(ws, ys)):
+            nxt = ws[(k + 1) % len(ws)][0] if args.prefetch else None
+            ops.linear(args.profile, wq, s, x, oc, ic, out=y, tiled=args.path == "tiled", tcgen05=args.path == "tc",
+                       prefetch=nxt)
 
     with torch.cuda.stream(stream):
         one_pass()
@@ -731,6 +737,7 @@ def main():
     ap.add_argument("--copies", type=int, default=0, help="profile mode: weight copies to rotate over")
     ap.add_argument("--tp-mlp", action="store_true", help="run the config-4 tensor-parallel MLP stack instead")
     ap.add_argument("--qat", action="store_true", help="run the config-5 QAT fake-quant measurement instead")
+    ap.add_argument("--prefetch", action="store_true", help="profile: each launch prefetches the next copy into L2")
     ap.add_argument("--tp-graph", type=int, default=1, help="tp-mlp: replay each step as a CUDA graph")
     ap.add_argument("--tp-allreduce", default="nccl", choices=["nccl", "peer"],
                     help="tp-mlp: all-reduce of the down projection's partial sums")

@@ -154,6 +154,14 @@ SPARK_API size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int
 SPARK_API int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
                  int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype,
                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+/* spark_linear plus an L2 prefetch hint: `prefetch_bytes` bytes at `prefetch`
+ * (16-byte aligned; typically the next layer's weight) are requested into L2
+ * by the decode GEMV while it runs, so the next launch finds them there.  The
+ * hint changes no result; other paths ignore it.  No reference counterpart. */
+SPARK_API int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype,
+                                    int64_t M, int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype,
+                                    void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                                    const void* prefetch, int64_t prefetch_bytes, void* stream);
 
 /* spark_linear without a workspace argument, for callers that may not allocate
  * device memory when they run a linear (a runtime whose memory plan is fixed

@@ -75,6 +75,8 @@ _SIGNATURES = {
     "spark_int8_unpack": (_i, [_p, _p, _i64, _i64, _p, _i, _p]),
     "spark_linear_workspace_size": (_sz, [_i, _i64, _i64, _i64]),
     "spark_linear": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p]),
+    "spark_linear_prefetch": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p,
+                                   _i64, _p]),
     "spark_linear_chain_workspace_size": (_sz, [_i]),
     "spark_linear_chain": (_i, [_p, _i, _i64, _p, _sz, _p]),
     "spark_linear_noalloc": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p]),

@@ -409,6 +409,8 @@ struct GemvArgs {
     int64_t row_bytes, scale_row_bytes;
     int64_t n_rg, n_kc, units;
     int M, bias_dtype, y_dtype;
+    const uint8_t* pf;      // bytes the next launch will read (L2 prefetch hint), or null
+    int64_t pf_bytes;
 };
 
 // ---------------------------------------------------------------- prepare x
@@ -792,6 +794,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // the next kDepthT units into a private shared-memory ring (cp.async), so no
 // synchronisation beyond the thread's own wait_group is needed.
 constexpr int kDepthT = 4;
+constexpr int64_t kPrefetchChunk = 32 * 1024;   // bytes per L2 prefetch instruction
 
 // acquire-release counter bump: the partials written before it are visible to
 // whoever observes the count, and the last arriver sees everybody's partials
@@ -835,6 +838,17 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
         }
         cp_async_commit();
     };
+    // Hint for the next launch: this CTA's share of the bytes it will read
+    // goes to L2 now, streaming from DRAM while this launch decodes.
+    if (a.pf && threadIdx.x == 0) {
+        const int64_t g = a.pf_bytes / 16;
+        const int64_t g0 = g * blockIdx.x / gridDim.x, g1 = g * (blockIdx.x + 1) / gridDim.x;
+        for (int64_t c = g0; c < g1; c += kPrefetchChunk / 16) {
+            const int64_t left = g1 - c;
+            const uint32_t bytes = (uint32_t)(left < kPrefetchChunk / 16 ? left : kPrefetchChunk / 16) * 16u;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.pf + c * 16), "r"(bytes) : "memory");
+        }
+    }
 #pragma unroll
     for (int i = 0; i < kDepthT; ++i) issue(u0 + i, i);
     if constexpr (BF && FMT == SPARK_FMT_SPFP2) {
@@ -1279,6 +1293,16 @@ size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int64_t ic) {
 int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
                  int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype,
                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+    return spark_linear_prefetch(fmt, wq, scales, x, x_dtype, M, oc, ic, ldx, bias, bias_dtype, y, y_dtype, ldy,
+                                 workspace, workspace_bytes, nullptr, 0, stream);
+}
+
+int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
+                          int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype, void* y, int y_dtype,
+                          int64_t ldy, void* workspace, size_t workspace_bytes, const void* prefetch,
+                          int64_t prefetch_bytes, void* stream) {
+    SPARK_REQUIRE(prefetch_bytes >= 0 && (!prefetch || aligned(prefetch, 16)), SPARK_ERR_ALIGNMENT,
+                  "spark_linear_prefetch: the prefetch range must start on 16 bytes");
     const bool tiled = (fmt & SPARK_LAYOUT_TILED) != 0;
     const bool tcgen05 = (fmt & SPARK_PATH_TCGEN05) != 0;
     fmt &= ~(SPARK_LAYOUT_TILED | SPARK_PATH_TCGEN05);
@@ -1359,6 +1383,8 @@ int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* 
         default: a.row_bytes = Fmt<SPARK_FMT_TWOFOUR>::row_bytes(ic); break;
     }
     a.scale_row_bytes = ic / 16;
+    a.pf = static_cast<const uint8_t*>(prefetch);
+    a.pf_bytes = prefetch ? prefetch_bytes / 16 * 16 : 0;
 
     for (int64_t m0 = 0; m0 < M; m0 += kMaxTokens) {
         const int mc = (int)std::min<int64_t>(kMaxTokens, M - m0);

@@ -41,7 +41,11 @@ class V3PackedLinear(nn.Module):
 
     fmt: "spfp2" (paired 5 B / 16 w), "spfp2_v1" (3 B / 8 w), "fp3" (3-bit codes +
     e4m3 scales), "nvfp4" (e2m1 nibbles + e4m3 scales) or "twofour" (7 B / 32 w).
+    prefetch_next: a tensor (the next layer's weight, see chain_prefetch) the
+    decode GEMV pulls into L2 while it runs.
     """
+
+    prefetch_next: torch.Tensor | None = None
 
     def __init__(self, fmt: str, packed: torch.Tensor, out_features: int, in_features: int,
                  scales: torch.Tensor | None = None, bias: torch.Tensor | None = None):
@@ -91,7 +95,7 @@ class V3PackedLinear(nn.Module):
         # GEMM, which reads the reference-layout bytes
         if self.w_tiled is not None and ic == self.in_features and x.numel() <= 16 * ic:
             return ops.linear(self.fmt, self.w_tiled, None, x, self.out_features, ic, bias=self.bias,
-                              out_dtype=x.dtype, out=out, tiled=True)
+                              out_dtype=x.dtype, out=out, tiled=True, prefetch=self.prefetch_next)
         return ops.linear(self.fmt, self.w_packed, self.w_scales, x, self.out_features, ic,
                           bias=self.bias, out_dtype=x.dtype, out=out)
 
@@ -147,6 +151,16 @@ class V3MergedLinear(nn.Module):
 
     def extra_repr(self) -> str:
         return f"fmt={self.merged.fmt}, in_features={self.in_features}, splits={self.splits}"
+
+
+def chain_prefetch(modules: list) -> None:
+    """Layers in call order (V3PackedLinear or V3MergedLinear): each one's decode
+    GEMV pulls the next one's weight into L2 while it runs, the last one the
+    first's (a decode loop starts over).  Only a hint: results do not change."""
+    lin = [m.merged if isinstance(m, V3MergedLinear) else m for m in modules]
+    for i, m in enumerate(lin):
+        nxt = lin[(i + 1) % len(lin)]
+        m.prefetch_next = nxt.w_tiled if nxt.w_tiled is not None else nxt.w_packed
 
 
 class V3SPFP2Layer(V3PackedLinear):

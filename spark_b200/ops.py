@@ -276,10 +276,13 @@ def tile_weights(fmt, wq: torch.Tensor, scales, oc: int, ic: int) -> torch.Tenso
 
 
 def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bias=None, out_dtype=None,
-           out: torch.Tensor | None = None, tiled: bool = False, tcgen05: bool = False) -> torch.Tensor:
+           out: torch.Tensor | None = None, tiled: bool = False, tcgen05: bool = False,
+           prefetch: torch.Tensor | None = None) -> torch.Tensor:
     """y[..., oc] = x[..., ic] . decode(W)^T (+ bias) with W packed in `fmt`
     (reference layout, or the tile_weights copy with tiled=True).  tcgen05=True
-    runs the tensor-memory kernel (SPFP2 reference layout, bf16 x)."""
+    runs the tensor-memory kernel (SPFP2 reference layout, bf16 x).  prefetch:
+    a tensor (typically the next layer's weight) the decode GEMV pulls into L2
+    while it runs."""
     f = FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
     if tcgen05:
         f |= PATH_TCGEN05
@@ -301,8 +304,13 @@ def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bia
     y = out if out is not None else torch.empty(M, oc, dtype=out_dtype or x.dtype, device=x.device)
     nbytes = workspace_size(f & 0xff, M, oc, ic)
     ws = workspace(x.device, nbytes)
-    call("spark_linear", f, _p(w), _p(s), _p(x2), _dt(x2), M, oc, ic, x2.stride(0), _p(b),
-         _dt(b) if b is not None else DTYPE_F32, _p(y), _dt(y), y.stride(0), _p(ws), ws.numel(), _stream(x))
+    if prefetch is None:
+        call("spark_linear", f, _p(w), _p(s), _p(x2), _dt(x2), M, oc, ic, x2.stride(0), _p(b),
+             _dt(b) if b is not None else DTYPE_F32, _p(y), _dt(y), y.stride(0), _p(ws), ws.numel(), _stream(x))
+    else:
+        call("spark_linear_prefetch", f, _p(w), _p(s), _p(x2), _dt(x2), M, oc, ic, x2.stride(0), _p(b),
+             _dt(b) if b is not None else DTYPE_F32, _p(y), _dt(y), y.stride(0), _p(ws), ws.numel(),
+             _p(prefetch), prefetch.numel() * prefetch.element_size(), _stream(x))
     return y.reshape(*lead, oc)
 
 

@@ -82,3 +82,20 @@ def test_tp_mlp_single_rank_matches_fp64():
     want = h @ dec(down).T
     got = mlp(x).double()
     assert (got - want).abs().max().item() <= 1e-3 * max(1.0, want.abs().max().item())
+
+
+def test_prefetch_hint_changes_nothing():
+    from spark_b200 import ops
+    from spark_b200.inference_v3 import V3PackedLinear, chain_prefetch
+    g = torch.Generator(device="cuda").manual_seed(2)
+    a = V3PackedLinear("spfp2", ops.spfp2_pack(torch.randn(512, 768, device="cuda", generator=g) * 0.02)[0], 512, 768)
+    b = V3PackedLinear("spfp2", ops.spfp2_pack(torch.randn(768, 512, device="cuda", generator=g) * 0.02)[0], 768, 512)
+    x = torch.randn(3, 768, device="cuda", generator=g).bfloat16()
+    want_a = a(x)
+    want_b = b(want_a)
+    chain_prefetch([a, b])
+    assert a.prefetch_next is b.w_tiled and b.prefetch_next is a.w_tiled
+    ya = a(x)
+    assert torch.equal(ya, want_a) and torch.equal(b(ya), want_b)
+    odd = torch.empty(1000, dtype=torch.uint8, device="cuda")      # length not a multiple of 16
+    assert torch.equal(ops.linear("spfp2", a.w_tiled, None, x, 512, 768, tiled=True, prefetch=odd[:999]), want_a)
