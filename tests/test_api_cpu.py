@@ -94,3 +94,18 @@ def test_merged_linear_concatenates_rows_and_rejects_straddling_rows():
         V3MergedLinear([V3PackedLinear("spfp2", c, 16, 104), V3PackedLinear("spfp2", c, 16, 104)])
     with pytest.raises(ValueError):
         V3MergedLinear([V3PackedLinear("spfp2", a, 64, 512), V3PackedLinear("twofour", a, 64, 512)])
+
+
+def test_chain_prefetch_links_layers_in_call_order():
+    from spark_b200.inference_v3 import V3MergedLinear, V3NVFP4Embedding, V3PackedLinear, chain_prefetch
+    g = torch.Generator().manual_seed(1)
+    mk = lambda oc, ic: V3PackedLinear("spfp2", torch.randint(0, 256, (oc * ic // 16 * 5,), dtype=torch.uint8,
+                                                              generator=g), oc, ic)
+    a, b, c = mk(64, 256), mk(32, 256), mk(256, 64)
+    m = V3MergedLinear([a, b])
+    chain_prefetch([m, c])
+    # CPU layers keep no tiled copy: the hint falls back to the packed bytes
+    assert m.merged.prefetch_next is c.w_packed and c.prefetch_next is m.merged.w_packed
+    emb = V3NVFP4Embedding(torch.zeros(10, 8, dtype=torch.uint8), torch.zeros(10, 1, dtype=torch.uint8), 10, 16,
+                           padding_idx=3)
+    assert emb.codes.dtype == torch.uint8 and emb.padding_idx == 3 and "nvfp4" in emb.extra_repr()
