@@ -4,21 +4,26 @@
 // formats.  The work is HBM-bound: every packed byte is read exactly once.
 //
 // Data flow per launch
-//   1. k_prepare_x: x (bf16/f16/f32) -> fp16 scaled by a per-token power of two
-//      sigma (max|x|/sigma in [2^14, 2^15)), written in the column order the
-//      format's decoder produces (so a 16-byte load is a ready MMA B fragment).
-//      Products stay exact: every decoded weight has <= 6 significant bits.
-//   2. k_gemv<FMT, NT>: persistent grid, every warp owns a contiguous range of
-//      "units" (16 rows x 256 columns, 512 for 2:4) in row-group-major order.
-//      A warp streams its units through a private ring of shared-memory stages
-//      filled by bulk async copies (cp.async.bulk + mbarrier complete_tx), one
-//      copy per row segment.  Each thread decodes the packed codes of two rows
-//      straight into fp16 A fragments and issues mma.sync m16n8k16 (fp32
-//      accumulate) against the prepared x.  The tensor pipe is nearly idle at
-//      these M; the limits are the HBM stream and the decode instructions.
-//   3. Row groups split between warps are reduced deterministically: each
-//      contributor writes its fp32 partial to the workspace, bumps a per-row-
-//      group counter, and the last arriver sums the partials in warp order.
+//   * Decode path (the one layers use): k_gemv_tiled<FMT, NT, XS, BF> on the
+//     fragment-major copy made once by spark_tile_weights.  Persistent grid of
+//     2 CTAs x 8 warps per SM; every warp owns a contiguous range of "units"
+//     (16 rows x 256 columns, 512 for 2:4) in row-group-major order and streams
+//     them through a private 4-stage cp.async ring (each lane reads back only
+//     the 16-byte vectors it copied).  Each thread decodes two rows straight
+//     into MMA A fragments and issues mma.sync m16n8k16 (fp32 accumulate).
+//     With bf16 activations every format runs a bf16 MMA on the caller's x
+//     (SPFP2 / 2:4 weights are powers of two, FP3 / NVFP4 pairs times an e4m3
+//     scale fit bf16 exactly); fp32 / fp16 activations take the fp16 path below.
+//   * fp16 path (fp32 / fp16 x, and the reference-layout k_gemv<FMT, NT, XS>):
+//     k_prepare_x first writes x as fp16 scaled by a per-token power of two
+//     sigma (max|x|/sigma in [2^14, 2^15)), in the column order the format's
+//     decoder produces, plus the fp16 remainder of fp32 / fp16 inputs.
+//     Products stay exact: every decoded weight has <= 6 significant bits.
+//   * Row groups split between warps are reduced deterministically: each
+//     contributor writes its fp32 partial to the workspace, bumps a per-row-
+//     group counter, and the last arriver sums the partials in warp order.
+//   * Optional: the launch requests the next launch's weight into L2
+//     (spark_linear_prefetch).
 //
 // The packed layouts are the reference's (DJAzzs/SPARK 01_core/*_emu.py).
 #include <algorithm>
