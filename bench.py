@@ -383,7 +383,7 @@ def run_gpu(args, rank, world, local):
         "per_projection": {"value": round(value_pp, 1), "unit": "GB/s", "ms_per_step": round(ms_pp / args.steps, 4),
                            "gpu_launches": launches_pp},
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "spark_b200.inference_v3.V3PackedLinear, eager, pinned host I/O"},
+                "api": "spark_b200.inference_v3.V3MergedLinear / V3PackedLinear, eager, pinned host I/O"},
         "clocks": clk.summary(),
         "prefill": {
             "workload": f"BASELINE config 3: M={PREFILL_M} bf16 tokens through the 7 linears of one layer "
