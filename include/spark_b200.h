@@ -57,6 +57,10 @@ extern "C" {
  * ic a multiple of 256, 16-byte aligned weights and x, ldx a multiple of 8);
  * SPARK_ERR_UNSUPPORTED when the call does not meet those conditions. */
 #define SPARK_PATH_TCGEN05 0x200
+/* Fused MLP activation: the weight's rows come in 16-row groups of 8 gate rows
+ * then the matching 8 up rows (V3GateUpSiLU builds this order); y gets
+ * SiLU(gate) * up, oc / 2 columns wide.  Decode GEMV paths only. */
+#define SPARK_EPILOGUE_SILU 0x400
 
 SPARK_API const char* spark_last_error(void);
 SPARK_API int spark_version(void);

@@ -25,6 +25,7 @@ DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 FMT_SPFP2, FMT_SPFP2_V1, FMT_FP3, FMT_NVFP4, FMT_TWOFOUR = 0, 1, 2, 3, 4
 LAYOUT_TILED = 0x100
 PATH_TCGEN05 = 0x200
+EPILOGUE_SILU = 0x400
 
 
 CHAIN_LINEAR, CHAIN_SILU_MUL = 0, 1

@@ -416,6 +416,7 @@ struct GemvArgs {
     int M, bias_dtype, y_dtype;
     const uint8_t* pf;      // bytes the next launch will read (L2 prefetch hint), or null
     int64_t pf_bytes;
+    int silu_pairs;         // rows 16k..16k+7 gate, 16k+8.. up: write SiLU(gate) * up, oc / 2 columns
 };
 
 // ---------------------------------------------------------------- prepare x
@@ -544,6 +545,27 @@ template <int NT>
 __device__ __forceinline__ void write_rows(const GemvArgs& a, int64_t rg, const float (*acc)[4], int lane,
                                            const float* sig) {
     const int g = lane >> 2, t = lane & 3;
+    if (a.silu_pairs) {
+        // this thread holds gate row 16rg+g (acc[.][0..1]) and its up row
+        // 16rg+g+8 (acc[.][2..3]): h[tok, 8rg+g] = SiLU(gate) * up
+        const int64_t rgate = rg * 16 + g, rup = rgate + 8;
+        const float bg = a.bias ? load_as_float(a.bias, a.bias_dtype, rgate) : 0.0f;
+        const float bu = a.bias ? load_as_float(a.bias, a.bias_dtype, rup) : 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int tok = nt * 8 + 2 * t + i;
+                if (tok < a.M) {
+                    const float s = sig ? sig[tok] : 1.0f;
+                    const float gv = (sig ? acc[nt][i] * s : acc[nt][i]) + bg;
+                    const float uv = (sig ? acc[nt][2 + i] * s : acc[nt][2 + i]) + bu;
+                    store_from_float(a.y, a.y_dtype, (int64_t)tok * a.ldy + rg * 8 + g,
+                                     gv / (1.0f + __expf(-gv)) * uv);
+                }
+            }
+        return;
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -1310,14 +1332,17 @@ int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, con
                   "spark_linear_prefetch: the prefetch range must start on 16 bytes");
     const bool tiled = (fmt & SPARK_LAYOUT_TILED) != 0;
     const bool tcgen05 = (fmt & SPARK_PATH_TCGEN05) != 0;
-    fmt &= ~(SPARK_LAYOUT_TILED | SPARK_PATH_TCGEN05);
+    const bool silu = (fmt & SPARK_EPILOGUE_SILU) != 0;
+    fmt &= ~(SPARK_LAYOUT_TILED | SPARK_PATH_TCGEN05 | SPARK_EPILOGUE_SILU);
     SPARK_REQUIRE(fmt >= SPARK_FMT_SPFP2 && fmt <= SPARK_FMT_TWOFOUR, SPARK_ERR_INVALID, "spark_linear: bad format %d", fmt);
     SPARK_REQUIRE(!tiled || tiled_bytes(fmt, oc, ic) > 0, SPARK_ERR_INVALID,
                   "spark_linear: no tiled layout for format %d [%lld, %lld]", fmt, (long long)oc, (long long)ic);
     SPARK_REQUIRE(wq && x && y, SPARK_ERR_INVALID, "spark_linear: null pointer");
     SPARK_REQUIRE(M >= 0 && oc >= 0 && ic >= 0, SPARK_ERR_INVALID, "spark_linear: negative size");
-    SPARK_REQUIRE(ldx >= ic && ldy >= oc, SPARK_ERR_INVALID, "spark_linear: ldx %lld < ic or ldy %lld < oc",
-                  (long long)ldx, (long long)ldy);
+    SPARK_REQUIRE(ldx >= ic && ldy >= (silu ? oc / 2 : oc), SPARK_ERR_INVALID,
+                  "spark_linear: ldx %lld < ic or ldy %lld below the output width", (long long)ldx, (long long)ldy);
+    SPARK_REQUIRE(!silu || oc % 16 == 0, SPARK_ERR_INVALID,
+                  "spark_linear: the fused SiLU epilogue takes whole 16-row groups (8 gate + 8 up rows)");
     SPARK_REQUIRE(tiled || (fmt != SPARK_FMT_FP3 && fmt != SPARK_FMT_NVFP4) || scales, SPARK_ERR_INVALID,
                   "spark_linear: FP3/NVFP4 need scales");
     SPARK_REQUIRE(x_dtype >= 0 && x_dtype <= 2 && y_dtype >= 0 && y_dtype <= 2 && bias_dtype >= 0 && bias_dtype <= 2,
@@ -1328,6 +1353,9 @@ int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, con
     const bool tc_ok = !tiled && tc_linear_ok(fmt, wq, scales, x, x_dtype, ic, ldx);
     // 2:4 weights: the tcgen05 kernel at every token count (its decode GEMV is far slower)
     if (tcgen05 || (tc_ok && (M > kMaxTokens || fmt == SPARK_FMT_TWOFOUR))) {
+        SPARK_REQUIRE(!silu, SPARK_ERR_UNSUPPORTED,
+                      "spark_linear: the fused SiLU epilogue runs on the decode GEMV (tiled weights, or up to 16 "
+                      "tokens on the reference layout)");
         SPARK_REQUIRE(tc_ok, SPARK_ERR_UNSUPPORTED,
                       "spark_linear: the tcgen05 path takes SPFP2, FP3 or NVFP4 in the reference layout, bf16 x, "
                       "ic %% 256 == 0, 16-byte aligned weights, scales and x, ldx %% 8 == 0");
@@ -1346,6 +1374,7 @@ int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, con
     if (tiled) {
         SPARK_REQUIRE(aligned(wq, 16), SPARK_ERR_ALIGNMENT, "spark_linear: tiled weights must be 16-byte aligned");
     } else if (!fast_path_ok(fmt, wq, scales, oc, ic)) {
+        SPARK_REQUIRE(!silu, SPARK_ERR_UNSUPPORTED, "spark_linear: no fused SiLU epilogue for this shape / alignment");
         k_linear_generic<<<(unsigned)((oc + 7) / 8), 256, 0, s>>>(fmt, wq, scales, x, x_dtype, M, oc, ic, ldx, bias,
                                                                   bias_dtype, y, y_dtype, ldy);
         return check_launch("spark_linear (generic)");
@@ -1388,6 +1417,7 @@ int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, con
         default: a.row_bytes = Fmt<SPARK_FMT_TWOFOUR>::row_bytes(ic); break;
     }
     a.scale_row_bytes = ic / 16;
+    a.silu_pairs = silu ? 1 : 0;
     a.pf = static_cast<const uint8_t*>(prefetch);
     a.pf_bytes = prefetch ? prefetch_bytes / 16 * 16 : 0;
 

@@ -153,11 +153,63 @@ class V3MergedLinear(nn.Module):
         return f"fmt={self.merged.fmt}, in_features={self.in_features}, splits={self.splits}"
 
 
+class V3GateUpSiLU(nn.Module):
+    """SiLU(gate(x)) * up(x) of an MLP as one launch: gate and up are kept as
+    one packed weight whose rows come in 16-row groups -- 8 gate rows, then the
+    same 8 up rows -- so each thread of the decode GEMV holds a gate value and
+    its up value and writes SiLU(gate) * up straight from the accumulators (no
+    [M, 2I] intermediate, no separate SiLU launch).  Above 16 tokens the stacked
+    linear runs on the tcgen05 GEMM and spark_silu_mul pairs the halves."""
+
+    def __init__(self, gate: V3PackedLinear, up: V3PackedLinear):
+        super().__init__()
+        if (gate.fmt != up.fmt or gate.in_features != up.in_features or gate.out_features != up.out_features
+                or gate.out_features % 8):
+            raise ValueError("V3GateUpSiLU: gate and up must share format and shape, out_features % 8 == 0")
+        fmt, ic, inter = gate.fmt, gate.in_features, gate.out_features
+        if not _row_aligned(fmt, ic):
+            raise ValueError(f"{fmt} rows of {ic} weights are not byte-aligned; cannot interleave")
+        self.out_features = inter
+        # row order: gate 8k..8k+7, up 8k..8k+7 for every k
+        k = torch.arange(inter // 8, device=gate.w_packed.device)
+        order = torch.stack([k * 8, k * 8 + inter], dim=1).repeat_interleave(8, dim=1)
+        order = (order + torch.arange(8, device=order.device).repeat(2)).reshape(-1)
+
+        def interleave(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+            both = torch.cat([a.reshape(inter, -1), b.reshape(inter, -1)])
+            return both[order].reshape(-1)
+
+        scales = interleave(gate.w_scales, up.w_scales) if gate.w_scales is not None else None
+        bias = None
+        if gate.bias is not None or up.bias is not None:
+            ref = gate.bias if gate.bias is not None else up.bias
+            zero = torch.zeros(inter, dtype=ref.dtype, device=ref.device)
+            bias = interleave(gate.bias if gate.bias is not None else zero, up.bias if up.bias is not None else zero)
+        self.merged = V3PackedLinear(fmt, interleave(gate.w_packed, up.w_packed), 2 * inter, ic, scales=scales,
+                                     bias=bias)
+
+    @property
+    def in_features(self) -> int:
+        return self.merged.in_features
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        m = self.merged
+        if m.w_tiled is not None and x.shape[-1] == m.in_features and x.numel() <= 16 * m.in_features:
+            return ops.linear(m.fmt, m.w_tiled, None, x, m.out_features, m.in_features, bias=m.bias,
+                              out_dtype=x.dtype, tiled=True, prefetch=m.prefetch_next, silu=True)
+        y = m(x).reshape(-1, self.out_features // 8, 2, 8)
+        h = ops.silu_mul(y[:, :, 0, :].reshape(-1, self.out_features), y[:, :, 1, :].reshape(-1, self.out_features))
+        return h.reshape(*x.shape[:-1], self.out_features)
+
+    def extra_repr(self) -> str:
+        return f"fmt={self.merged.fmt}, in_features={self.in_features}, out_features={self.out_features}, silu"
+
+
 def chain_prefetch(modules: list) -> None:
     """Layers in call order (V3PackedLinear or V3MergedLinear): each one's decode
     GEMV pulls the next one's weight into L2 while it runs, the last one the
     first's (a decode loop starts over).  Only a hint: results do not change."""
-    lin = [m.merged if isinstance(m, V3MergedLinear) else m for m in modules]
+    lin = [m.merged if isinstance(m, (V3MergedLinear, V3GateUpSiLU)) else m for m in modules]
     for i, m in enumerate(lin):
         nxt = lin[(i + 1) % len(lin)]
         m.prefetch_next = nxt.w_tiled if nxt.w_tiled is not None else nxt.w_packed

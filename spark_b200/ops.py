@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 from ._lib import (DTYPE_BF16, DTYPE_F16, DTYPE_F32, FMT_FP3, FMT_NVFP4, FMT_SPFP2, FMT_SPFP2_V1,
-                   FMT_TWOFOUR, LAYOUT_TILED, PATH_TCGEN05, call)
+                   FMT_TWOFOUR, LAYOUT_TILED, PATH_TCGEN05, EPILOGUE_SILU, call)
 
 _DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
 
@@ -277,18 +277,22 @@ def tile_weights(fmt, wq: torch.Tensor, scales, oc: int, ic: int) -> torch.Tenso
 
 def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bias=None, out_dtype=None,
            out: torch.Tensor | None = None, tiled: bool = False, tcgen05: bool = False,
-           prefetch: torch.Tensor | None = None) -> torch.Tensor:
+           prefetch: torch.Tensor | None = None, silu: bool = False) -> torch.Tensor:
     """y[..., oc] = x[..., ic] . decode(W)^T (+ bias) with W packed in `fmt`
     (reference layout, or the tile_weights copy with tiled=True).  tcgen05=True
     runs the tensor-memory kernel (SPFP2 reference layout, bf16 x).  prefetch:
     a tensor (typically the next layer's weight) the decode GEMV pulls into L2
-    while it runs."""
+    while it runs.  silu: the weight holds gate/up rows in groups of 8 + 8
+    (V3GateUpSiLU) and the result is SiLU(gate) * up, oc // 2 wide (decode
+    GEMV paths)."""
     f = FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
     if tcgen05:
         f |= PATH_TCGEN05
     if tiled:
         f |= LAYOUT_TILED
         scales = None
+    if silu:
+        f |= EPILOGUE_SILU
     if not x.is_cuda:
         raise RuntimeError("spark_b200.linear: x must be a CUDA tensor")
     lead = x.shape[:-1]
@@ -301,7 +305,8 @@ def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bia
     w = _bytes(wq)
     s = _bytes(scales) if scales is not None else None
     b = bias.contiguous() if bias is not None else None
-    y = out if out is not None else torch.empty(M, oc, dtype=out_dtype or x.dtype, device=x.device)
+    width = oc // 2 if silu else oc
+    y = out if out is not None else torch.empty(M, width, dtype=out_dtype or x.dtype, device=x.device)
     nbytes = workspace_size(f & 0xff, M, oc, ic)
     ws = workspace(x.device, nbytes)
     if prefetch is None:
@@ -311,7 +316,7 @@ def linear(fmt, wq: torch.Tensor, scales, x: torch.Tensor, oc: int, ic: int, bia
         call("spark_linear_prefetch", f, _p(w), _p(s), _p(x2), _dt(x2), M, oc, ic, x2.stride(0), _p(b),
              _dt(b) if b is not None else DTYPE_F32, _p(y), _dt(y), y.stride(0), _p(ws), ws.numel(),
              _p(prefetch), prefetch.numel() * prefetch.element_size(), _stream(x))
-    return y.reshape(*lead, oc)
+    return y.reshape(*lead, width)
 
 
 class ChainOp:

@@ -99,3 +99,28 @@ def test_prefetch_hint_changes_nothing():
     assert torch.equal(ya, want_a) and torch.equal(b(ya), want_b)
     odd = torch.empty(1000, dtype=torch.uint8, device="cuda")      # length not a multiple of 16
     assert torch.equal(ops.linear("spfp2", a.w_tiled, None, x, 512, 768, tiled=True, prefetch=odd[:999]), want_a)
+
+
+@pytest.mark.parametrize("fmt", ["spfp2", "fp3", "nvfp4"])
+@pytest.mark.parametrize("M", [1, 7, 40])
+def test_gate_up_silu_epilogue(fmt, M):
+    from spark_b200.inference_v3 import V3GateUpSiLU
+    (gate, _, _), (up, _, _) = _part(fmt, 512, 768, seed=3), _part(fmt, 512, 768, seed=4)
+    fused = V3GateUpSiLU(gate, up)
+    x = torch.randn(M, 768, device="cuda", generator=torch.Generator(device="cuda").manual_seed(8))
+    want = torch.nn.functional.silu(gate(x).double()) * up(x).double()
+    got = fused(x)
+    assert got.shape == (M, 512) and got.dtype == torch.float32
+    assert torch.allclose(got.double(), want, rtol=1e-4, atol=1e-5)
+    xb = x.bfloat16()
+    wb = torch.nn.functional.silu(gate(xb).float()) * up(xb).float()
+    assert torch.allclose(fused(xb).float(), wb, rtol=3e-2, atol=3e-2)
+
+
+def test_silu_epilogue_rejected_off_the_gemv():
+    from spark_b200 import ops
+    from spark_b200._lib import SparkError
+    (gate, _, _) = _part("spfp2", 512, 768, seed=5)
+    x = torch.randn(300, 768, device="cuda").bfloat16()
+    with pytest.raises(SparkError):
+        ops.linear("spfp2", gate.w_packed, None, x, 512, 768, silu=True)   # 300 tokens -> tcgen05 path
