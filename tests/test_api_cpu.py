@@ -109,3 +109,27 @@ def test_chain_prefetch_links_layers_in_call_order():
     emb = V3NVFP4Embedding(torch.zeros(10, 8, dtype=torch.uint8), torch.zeros(10, 1, dtype=torch.uint8), 10, 16,
                            padding_idx=3)
     assert emb.codes.dtype == torch.uint8 and emb.padding_idx == 3 and "nvfp4" in emb.extra_repr()
+
+
+def test_gate_up_silu_interleaves_rows_in_groups_of_eight():
+    from spark_b200.inference_v3 import V3GateUpSiLU, V3PackedLinear
+    inter, ic = 24, 64
+    rb, sb = ic // 2, ic // 16                                      # NVFP4 row bytes, scale bytes
+    g = torch.Generator().manual_seed(3)
+    gc, uc = (torch.randint(0, 256, (inter * rb,), dtype=torch.uint8, generator=g) for _ in range(2))
+    gs, us = (torch.randint(0, 256, (inter * sb,), dtype=torch.uint8, generator=g) for _ in range(2))
+    gb, ub = torch.randn(inter, generator=g), torch.randn(inter, generator=g)
+    m = V3GateUpSiLU(V3PackedLinear("nvfp4", gc, inter, ic, scales=gs, bias=gb),
+                     V3PackedLinear("nvfp4", uc, inter, ic, scales=us, bias=ub))
+    assert m.out_features == inter and m.merged.out_features == 2 * inter
+    rows = m.merged.w_packed.view(2 * inter, rb)
+    srows = m.merged.w_scales.view(2 * inter, sb)
+    for k in range(inter // 8):
+        for i in range(8):
+            assert torch.equal(rows[16 * k + i], gc.view(inter, rb)[8 * k + i])
+            assert torch.equal(rows[16 * k + 8 + i], uc.view(inter, rb)[8 * k + i])
+            assert torch.equal(srows[16 * k + 8 + i], us.view(inter, sb)[8 * k + i])
+            assert m.merged.bias[16 * k + i] == gb[8 * k + i] and m.merged.bias[16 * k + 8 + i] == ub[8 * k + i]
+    with pytest.raises(ValueError):
+        V3GateUpSiLU(V3PackedLinear("nvfp4", gc[: 12 * rb], 12, ic, scales=gs[: 12 * sb]),
+                     V3PackedLinear("nvfp4", uc[: 12 * rb], 12, ic, scales=us[: 12 * sb]))
