@@ -299,23 +299,27 @@ def run_gpu(args, rank, world, local):
                      for gname, _, parts in GROUPS})
     chain_prefetch([L[gname] for L in mods for gname, _, _ in GROUPS])
     xh = {ic: x[ic].cpu().pin_memory() for ic in x}
-    yh = {}
+    # every projection's output lands in one device buffer (the layers' out=
+    # argument), copied to pinned host memory once per step
+    width = {gname: sum(next(o for n, _, o, _ in SHAPES if n == p) for p in parts) for gname, _, parts in GROUPS}
+    total = LAYERS * sum(width.values())
+    ydev = torch.empty(1, total, dtype=torch.bfloat16, device=device)
+    yhost = torch.empty(1, total, dtype=torch.bfloat16).pin_memory()
+    yslot, off = {}, 0
     for L in mods:
-        for name, _, parts in GROUPS:
-            for p in parts:
-                oc = next(o for n, _, o, _ in SHAPES if n == p)
-                yh[(p, id(L))] = torch.empty(1, oc, dtype=torch.bfloat16).pin_memory()
+        for gname, _, _ in GROUPS:
+            yslot[(gname, id(L))] = ydev[:, off:off + width[gname]]
+            off += width[gname]
     h2d = sum(t.numel() * 2 for t in xh.values())
-    d2h = sum(t.numel() * 2 for t in yh.values())
+    d2h = yhost.numel() * 2
 
     def e2e_step():
         xd = {ic: xh[ic].to(device, non_blocking=True) for ic in xh}
         for L in mods:
-            for gname, _, parts in GROUPS:
+            for gname, _, _ in GROUPS:
                 m = L[gname]
-                ys = m(xd[m.in_features])
-                for p, y in zip(parts, ys if isinstance(ys, tuple) else (ys,)):
-                    yh[(p, id(L))].copy_(y, non_blocking=True)
+                m(xd[m.in_features], out=yslot[(gname, id(L))])
+        yhost.copy_(ydev, non_blocking=True)
 
     def time_e2e(run, k):
         with torch.cuda.stream(stream):

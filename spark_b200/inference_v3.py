@@ -146,8 +146,9 @@ class V3MergedLinear(nn.Module):
     def in_features(self) -> int:
         return self.merged.in_features
 
-    def forward(self, x: torch.Tensor) -> tuple[torch.Tensor, ...]:
-        return self.merged(x).split(self.splits, dim=-1)
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> tuple[torch.Tensor, ...]:
+        """out: optional preallocated [M, sum(out_features)] result."""
+        return self.merged(x, out=out).split(self.splits, dim=-1)
 
     def extra_repr(self) -> str:
         return f"fmt={self.merged.fmt}, in_features={self.in_features}, splits={self.splits}"
