@@ -290,6 +290,35 @@ def run_gpu(args, rank, world, local):
     ms_pp = timed(graph_pp, args.steps)
     ops.check_device_errors()
 
+    # config 2 also names 4 and 16 tokens: the merged step at those M (the
+    # decode GEMV serves up to 16 tokens per launch), bytes counted as above
+    decode_tokens = {}
+    for m_tok in (4, 16):
+        xm = {ic: torch.randn(m_tok, ic, device=device, generator=g).bfloat16() for ic in x}
+        om = {}
+
+        def step_m():
+            seq = [((name, id(L)), fmt, oc, ic, wt) for L in merged for name, (fmt, _, _, oc, ic, wt) in L.items()]
+            for k, (key, fmt, oc, ic, wt) in enumerate(seq):
+                om[key] = ops.linear(fmt, wt, None, xm[ic], oc, ic, out=om.get(key), tiled=True,
+                                     prefetch=seq[(k + 1) % len(seq)][4])
+
+        with torch.cuda.stream(stream):
+            step_m()
+            step_m()
+        torch.cuda.synchronize()
+        gm = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gm, stream=stream):
+            step_m()
+        k_m = max(5, args.steps // 5)
+        ms_m = timed(gm, k_m)
+        bytes_m = LAYERS * sum(linear_bytes(f, oc, ic, M=m_tok) for _, f, oc, ic in SHAPES)
+        decode_tokens[str(m_tok)] = {"value": round(world * bytes_m * k_m / (ms_m * 1e-3) / 1e9, 1), "unit": "GB/s",
+                                     "ms_per_step": round(ms_m / k_m, 4),
+                                     "tokens_per_s": round(world * m_tok * k_m / (ms_m * 1e-3), 1)}
+        del gm
+    ops.check_device_errors()
+
     # ---------------- e2e through the public layer API with host buffers
     from spark_b200.inference_v3 import V3MergedLinear, V3PackedLinear, chain_prefetch
     mods = []
@@ -409,6 +438,7 @@ def run_gpu(args, rank, world, local):
         "gpu_launches": launches,
         "per_projection": {"value": round(value_pp, 1), "unit": "GB/s", "ms_per_step": round(ms_pp / args.steps, 4),
                            "gpu_launches": launches_pp},
+        "decode_tokens": decode_tokens,
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "spark_b200.inference_v3.V3MergedLinear / V3PackedLinear called per step with its pinned "
                        "host<->device copies", "mode": e2e_mode,
