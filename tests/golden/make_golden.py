@@ -1,9 +1,9 @@
 """Generate the golden vectors that pin the oracle to the reference emulators.
 
-Run in a container where the DJAzzs/SPARK tree is readable (default
-``/root/reference``, override with ``SPARK_REFERENCE``)::
+Run where a checkout of the DJAzzs/SPARK tree is readable, naming its root
+in ``SPARK_REFERENCE`` or as the first argument::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path to the SPARK checkout>
 
 It imports the reference's own emulators (``01_core/block_fp2_emu.py``,
 ``fp3_emu.py``, ``nvfp4_emu.py``, ``two_four.py``) read-only, runs them on
@@ -21,7 +21,10 @@ import sys
 import numpy as np
 import torch
 
-REF = os.environ.get("SPARK_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPARK_REFERENCE", "")
+if not os.path.isdir(os.path.join(REF, "01_core")):
+    sys.exit("make_golden.py: pass the SPARK checkout's root (it holds 01_core/) as the first argument "
+             "or in SPARK_REFERENCE")
 sys.path.insert(0, os.path.join(REF, "01_core"))
 
 import block_fp2_emu as fp2  # noqa: E402
