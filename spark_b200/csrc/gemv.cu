@@ -901,10 +901,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // one token tile: the second MMA of each step accumulates separately, so
+    // the second MMA of each step and token tile accumulates separately, so
     // consecutive MMAs do not wait on each other
-    float acc[NT][4], accb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    float* acc2 = NT == 1 ? accb : acc[0];
+    float acc[NT][4], accb[4] = {0.0f, 0.0f, 0.0f, 0.0f}, accc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float* acc2 = accb;                           // second MMA of token tile 0
+    float* acc3 = NT > 1 ? accc : acc[NT - 1];    // second MMA of token tile 1
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -992,7 +993,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
                 mma_16816_bf16(acc2, A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
                 if (NT > 1) {
                     mma_16816_bf16(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
-                    mma_16816_bf16(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
+                    mma_16816_bf16(acc3, A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
                 }
             } else {
                 decode_step<FMT>(c0, sw0, s, A0);
@@ -1007,16 +1008,18 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
                     mma_16816(acc2, A0[2], A1[2], A0[3], A1[3], x0.z, x0.w);
                     if (NT > 1) {
                         mma_16816(acc[NT - 1], A0[0], A1[0], A0[1], A1[1], x1.x, x1.y);
-                        mma_16816(acc[NT - 1], A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
+                        mma_16816(acc3, A0[2], A1[2], A0[3], A1[3], x1.z, x1.w);
                     }
                 }
             }
         }
         const int u = u0 + i;
         if (++ckc == nkc || i + 1 == n) {
-            if constexpr (NT == 1) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) { acc[0][q] += accb[q]; accb[q] = 0.0f; }
+            for (int q = 0; q < 4; ++q) { acc[0][q] += accb[q]; accb[q] = 0.0f; }
+            if constexpr (NT > 1) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) { acc[NT - 1][q] += accc[q]; accc[q] = 0.0f; }
             }
             flush(crg, seg0, u + 1);
 #pragma unroll
