@@ -170,11 +170,13 @@ SPARK_API int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* s
 /* spark_linear without a workspace argument, for callers that may not allocate
  * device memory when they run a linear (a runtime whose memory plan is fixed
  * before the first token, a C host with no device allocator).  No counterpart in
- * the reference.  Same arguments, formats and results as spark_linear; it
- * allocates nothing.  Its scratch is one static 8 MiB array per device inside
- * the library, so ic is limited to what fits (spark_linear_workspace_size(fmt,
- * M, oc, ic) <= 8 MiB: ic <= 51,192 on a 148-SM GPU); a larger ic returns
- * SPARK_ERR_WORKSPACE.
+ * the reference.  Same arguments, formats and results as spark_linear (both
+ * the decode GEMV and the tcgen05 GEMM routes); it allocates nothing.  Its
+ * scratch is one static 16 MiB array per device inside the library, so a call
+ * must fit it: spark_linear_workspace_size(fmt, M, oc, ic) <= 16 MiB, which
+ * holds for every token count up to ic = 182,264 on a 148-SM GPU.  A call
+ * that does not fit returns SPARK_ERR_WORKSPACE with a message naming this
+ * entry point.
  *   - The first call on a device (with that device current) looks the scratch
  *     up, clears it and synchronises `stream`; make it before any stream capture
  *     (during a capture it returns SPARK_ERR_INVALID).

@@ -1519,15 +1519,19 @@ int spark_workspace_check(void* workspace, void* stream) {
 // Some callers may not allocate device memory when they run a linear: an
 // inference runtime whose memory plan is fixed before the first token, a host
 // that hands its whole budget to a caching allocator it cannot re-enter from
-// the decode loop, or a C caller with no allocator at all.  The stream-K GEMV
-// still needs scratch (error word, row-group counters, split partials,
-// per-token scales and prepared activations).  spark_linear_noalloc takes
-// that scratch from one statically sized array in this module (one copy per
-// device) instead of a caller-provided workspace, and allocates nothing.
+// the decode loop, or a C caller with no allocator at all.  Both kernels
+// behind spark_linear still need scratch: the decode GEMV its error word,
+// row-group counters, split partials, per-token scales and prepared
+// activations; the tcgen05 GEMM its error word, job counters and stream-K
+// partials.  spark_linear_noalloc takes that scratch from one statically sized
+// array in this module (one copy per device) instead of a caller-provided
+// workspace, and allocates nothing.  16 MiB covers the tcgen05 route at any
+// token count (262,656 + 2 * SMs * 64 * 128 * 4 bytes: 9.96 MB on 148 SMs) and
+// the decode GEMV up to ic = 182,264 on 148 SMs.
 namespace spark {
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kNoAllocMaxDevices = 64;
@@ -1576,11 +1580,14 @@ extern "C" int spark_linear_noalloc(int fmt, const uint8_t* wq, const uint8_t* s
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return set_error((int)e, "spark_linear_noalloc: %s", cudaGetErrorString(e));
-    const size_t need = ws_layout(ic, max_warps(dev)).total;
+    // the larger of the two routes' needs (decode GEMV and tcgen05 GEMM), so
+    // the check does not depend on which kernel spark_linear picks
+    SPARK_REQUIRE(M >= 0 && oc >= 0, SPARK_ERR_INVALID, "spark_linear_noalloc: negative size");
+    const size_t need = spark_linear_workspace_size(fmt & 0xff, M, oc, ic);
     SPARK_REQUIRE(need <= kNoAllocScratchBytes, SPARK_ERR_WORKSPACE,
-                  "spark_linear_noalloc: ic = %lld needs %zu bytes of scratch, above the static %zu bytes "
+                  "spark_linear_noalloc: M = %lld, ic = %lld needs %zu bytes of scratch, above the static %zu bytes "
                   "(use spark_linear with a caller-provided workspace)",
-                  (long long)ic, need, kNoAllocScratchBytes);
+                  (long long)M, (long long)ic, need, kNoAllocScratchBytes);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     void* scratch = nullptr;
     const int rc = noalloc_scratch(dev, s, &scratch);

@@ -57,6 +57,8 @@ def weights(name, oc, ic, tiled, seed):
         wq, s = ops().spfp2_pack(W)[0], None
     elif name == "fp3":
         wq, s = ops().fp3_pack(W)
+    elif name == "twofour":
+        wq, s = ops().twofour_pack(W), None
     else:
         wq, s = ops().nvfp4_pack(W)
     fmt = ops().FORMATS[name]
@@ -71,6 +73,11 @@ CASES = [
     ("spfp2", 9728, 2560, 1, True, torch.bfloat16, torch.float32, False),   # bf16 MMA, no prepared x
     ("fp3", 4096, 2560, 20, False, torch.float32, torch.float32, False),    # prepared hi/lo x, two token chunks
     ("nvfp4", 2560, 4096, 4, True, torch.bfloat16, torch.bfloat16, True),   # prepared x, bias, bf16 out
+    # the tcgen05 GEMM route: bf16 x on the reference layout above 16 tokens,
+    # and 2:4 at every token count (its stream-K partials live in the scratch)
+    ("spfp2", 4096, 2560, 64, False, torch.bfloat16, torch.float32, False),
+    ("fp3", 2560, 4096, 300, False, torch.bfloat16, torch.bfloat16, True),
+    ("twofour", 2560, 9728, 4, False, torch.bfloat16, torch.float32, False),
 ]
 
 
