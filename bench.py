@@ -18,9 +18,13 @@ timed region.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 With torchrun (N > 1) every rank runs its own replica (weak scaling); the
-step time is the max over ranks.  `--impl reference` times the reference's
-CPU path (decode + fp32 matmul per call, ported to C in oracle/) on the host
-cores.
+step time is the max over ranks.  The same line carries `tp_mlp`: BASELINE
+config 4 (a 32-layer SPFP2 MLP stack at 64 tokens) tensor-parallel over the N
+ranks (gate/up column-split, down row-split, one NCCL all-reduce of fp32
+partials per layer), with a parity check of a 2-layer slice against an fp64
+evaluation of the unsharded weights.  `--impl reference` times the
+reference's CPU path (decode + fp32 matmul per call, ported to C in oracle/)
+on the host cores.
 """
 from __future__ import annotations
 
@@ -108,6 +112,28 @@ def tensor_peak():
             return float(json.load(f)["bf16_tflops"]), "measured MEASURED_PEAKS.json bf16_tflops (burst)"
     except Exception:
         return 1590.0, "fallback 1590 TFLOP/s"
+
+
+def host_threads() -> int:
+    """Host threads this process may run on (torchrun sets OMP_NUM_THREADS=1 per
+    rank; the CPU legs set their thread counts from this instead)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def host_info() -> dict:
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except Exception:
+        pass
+    return {"cpu_model": model, "cpu_count": os.cpu_count(), "threads": host_threads(), "torch": torch.__version__}
 
 
 # ------------------------------------------------------------------ clocks
@@ -284,8 +310,12 @@ def run_gpu(args, rank, world, local):
         torch.cuda.synchronize()
         return max_over_ranks(ms, world)
 
-    with Clocks(local) as clk:
-        ms_total = timed(graph, args.steps)
+    # clocks are sampled from the first timed replay through the prefill and
+    # the tensor-parallel stack (the decode step alone lasts milliseconds,
+    # shorter than one nvidia-smi sample)
+    clk = Clocks(local)
+    clk.__enter__()
+    ms_total = timed(graph, args.steps)
     ms_spfp2 = timed(graph_spfp2, args.steps)
     ms_pp = timed(graph_pp, args.steps)
     ops.check_device_errors()
@@ -406,9 +436,14 @@ def run_gpu(args, rank, world, local):
     graph_pre = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_pre, stream=stream):
         prefill_step()
-    pre_steps = max(5, args.steps // 20)
+    pre_steps = max(50, args.steps // 10)
     ms_pre = timed(graph_pre, pre_steps)
     ops.check_device_errors()
+    del graph_pre, graph, graph_spfp2, graph_pp
+
+    # ---------------- BASELINE config 4, tensor-parallel over the ranks of this run
+    tp = tp_mlp_measure(args, rank, world, local)
+    clk.__exit__(None, None, None)
     pre_flops = sum(2.0 * PREFILL_M * oc * ic for _, _, oc, ic in SHAPES)
     pre_tflops = world * pre_flops * pre_steps / (ms_pre * 1e-3) / 1e12
     tpeak, tpeak_kind = tensor_peak()
@@ -445,6 +480,7 @@ def run_gpu(args, rank, world, local):
                 "eager": {"value": round(e2e_eager_gbs, 1), "unit": "GB/s",
                           "note": "the same calls dispatched from Python every step"}},
         "clocks": clk.summary(),
+        "tp_mlp": tp,
         "prefill": {
             "workload": f"BASELINE config 3: M={PREFILL_M} bf16 tokens through the 7 linears of one layer "
                         "(SPFP2 gate/up/down, FP3 q/k/v, NVFP4 out_proj) as 4 row-merged launches (q|k|v, "
@@ -503,9 +539,31 @@ def cpu_step(layer, xs):
             O.cpu_nvfp4_linear(wq, s, x, oc, ic)
 
 
-def cpu_baseline(args, budget_s=15.0):
-    """Time the reference's CPU path (decode + fp32 matmul per call) on a bounded sample."""
+def _cpu_decode_layer(layer):
+    """Decode-at-load form of a CPU layer: fp32 weights as torch tensors (what
+    the reference's apply_spark_state leaves in the model, 02_model/spark_loader.py:102-163)."""
     from oracle import oracle as O
+    out = {}
+    for name, (fmt, wq, s, oc, ic) in layer.items():
+        if fmt == "spfp2":
+            W = O.unpack_blockwise_paired(wq, oc * ic)
+        elif fmt == "fp3":
+            W = O.fp3_unpack_3bit(wq, s, oc, ic)
+        else:
+            W = O.nvfp4_unpack(wq, s, oc, ic)
+        out[name] = (ic, torch.from_numpy(np.ascontiguousarray(W, dtype=np.float32).reshape(oc, ic)))
+    return out
+
+
+def cpu_baseline(args, budget_s=15.0):
+    """Time the reference's CPU path on a bounded sample, on all host threads:
+    (b) decode + fp32 matmul per call (the online path the GPU kernels run) as
+    the value, and (a) decode once at load + torch fp32 matmul per call (what
+    the reference ships) beside it."""
+    from oracle import oracle as O
+    threads = host_threads()
+    O.set_num_threads(threads)
+    torch.set_num_threads(threads)
     layer = cpu_layer(1)
     rng = np.random.default_rng(2)
     xs = {ic: rng.standard_normal((1, ic)).astype(np.float32) for ic in (2560, 4096, 9728)}
@@ -516,15 +574,35 @@ def cpu_baseline(args, budget_s=15.0):
         n += 1
     dt = time.perf_counter() - t0
     per_layer = STEP_BYTES / LAYERS
+    dec = _cpu_decode_layer(layer)
+    xt = {ic: torch.from_numpy(v) for ic, v in xs.items()}
+
+    def load_step():
+        for ic, W in dec.values():
+            torch.matmul(xt[ic], W.T)
+
+    load_step()
+    na, t1 = 0, time.perf_counter()
+    while time.perf_counter() - t1 < budget_s / 2 and na < 2000:
+        load_step()
+        na += 1
+    da = time.perf_counter() - t1
     return {"value": round(per_layer * n / dt / 1e9, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
             "sample": f"{n} passes over one config-2 layer (7 linears) at M=1 in {dt:.1f} s: "
-                      "decode + fp32 matmul per call, rows split over OpenMP threads"}
+                      "decode + fp32 matmul per call, rows split over OpenMP threads",
+            "decode_at_load": {"value": round(per_layer * na / da / 1e9, 3), "unit": "GB/s",
+                               "ms_per_layer": round(da * 1e3 / na, 3), "threads": torch.get_num_threads(),
+                               "sample": f"{na} passes: weights decoded to fp32 once, torch CPU matmul per call "
+                                         "(bytes counted as the packed layer, as for the value)"},
+            "host": host_info()}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
     from oracle import oracle as O
+    # every host thread, whatever OMP_NUM_THREADS the launcher set
+    O.set_num_threads(host_threads())
     layer = cpu_layer(1)
     rng = np.random.default_rng(2)
     xs = {ic: rng.standard_normal((1, ic)).astype(np.float32) for ic in (2560, 4096, 9728)}
@@ -537,15 +615,31 @@ def run_reference(args, rank, world):
         cpu_step(layer, xs)
     dt = time.perf_counter() - t0
     value = STEP_BYTES / LAYERS * args.steps / dt / 1e9
+    # beside it: decode once at load + torch fp32 matmul per call (the form the
+    # reference ships), same steps
+    torch.set_num_threads(host_threads())
+    dec = _cpu_decode_layer(layer)
+    xt = {ic: torch.from_numpy(v) for ic, v in xs.items()}
+    for ic, W in dec.values():
+        torch.matmul(xt[ic], W.T)
+    t1 = time.perf_counter()
+    for _ in range(args.steps):
+        for ic, W in dec.values():
+            torch.matmul(xt[ic], W.T)
+    da = time.perf_counter() - t1
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (reference CPU emulator path)",
-        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)", "config": CONFIG, "impl": "reference",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+        "config": {**CONFIG, "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}, "impl": "reference",
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
                          "sample": f"{args.steps} steps, each one token through one config-2 layer (7 linears), "
                                    "decode + fp32 matmul per call (oracle/spark_oracle.c port of the reference's "
-                                   "CPU path)"},
+                                   "CPU path)", "host": host_info(),
+                         "decode_at_load": {"value": round(STEP_BYTES / LAYERS * args.steps / da / 1e9, 3),
+                                            "unit": "GB/s", "ms_per_step": round(da * 1e3 / args.steps, 3),
+                                            "threads": torch.get_num_threads()}},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -554,27 +648,41 @@ def run_reference(args, rank, world):
 TP_LAYERS, TP_H, TP_I, TP_M = 32, 4096, 12288, 64
 
 
-def run_tp_mlp(args, rank, world, local):
-    """BASELINE config 4: a 32-layer SPFP2 MLP stack (hidden 4096, intermediate
-    12288, N(0, 0.015) weights, SiLU(gate) * up), 64 bf16 tokens, tensor-
-    parallel over the `world` ranks (gate/up column-parallel, down row-parallel
-    + one NCCL all-reduce per layer).  Prints its own JSON line."""
+def _tp_stack(rank, world, device, peer=None, keep_full=0):
+    """The config-4 stack as TPMLP layers of this rank, and (keep_full > 0) the
+    first keep_full layers' unsharded weights decoded from their SPFP2 packing
+    (the GPU unpack, bit-exact against the reference emulator) in fp64."""
     from spark_b200 import ops
-    from spark_b200.tp import TPMLP, PeerAllReduce
-    device = torch.device("cuda", local)
-    peer = PeerAllReduce(TP_M * TP_H, dtype=torch.float32) if args.tp_allreduce == "peer" else None
+    from spark_b200.tp import TPMLP
     g = torch.Generator(device=device)
-    layers = []
+    layers, full = [], []
     for li in range(TP_LAYERS):
         g.manual_seed(4000 + li)
         gate = torch.randn(TP_I, TP_H, device=device, generator=g) * 0.015
         up = torch.randn(TP_I, TP_H, device=device, generator=g) * 0.015
         down = torch.randn(TP_H, TP_I, device=device, generator=g) * 0.015
         layers.append(TPMLP(gate, up, down, rank, world, peer=peer))
+        if li < keep_full:
+            full.append(tuple(ops.spfp2_unpack(ops.spfp2_pack(w)[0], w.numel()).view(w.shape).double()
+                              for w in (gate, up, down)))
         del gate, up, down
-    g.manual_seed(4)
-    x0 = torch.randn(TP_M, TP_H, device=device, generator=g).bfloat16()
-    stream = torch.cuda.Stream(device)
+    return layers, full
+
+
+def _tp_reference(x, full):
+    """fp64 evaluation of the unsharded layers with the stack's rounding points:
+    gate / up outputs, SiLU(gate) * up and each layer's output are bf16."""
+    def bf(t):
+        return t.to(torch.bfloat16).double()
+    y = x.double()
+    for wg, wu, wd in full:
+        gv, uv = bf(y @ wg.T), bf(y @ wu.T)
+        h = bf(gv * torch.sigmoid(gv) * uv)
+        y = bf(h @ wd.T)
+    return y
+
+
+def _time_stack(layers, x0, stream, warmup, k, world, graph_it=True):
     out = {}
 
     def step():
@@ -588,15 +696,14 @@ def run_tp_mlp(args, rank, world, local):
         step()
     torch.cuda.synchronize()
     graph = None
-    if args.tp_graph:
+    if graph_it:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             step()
         torch.cuda.synchronize()
     run = graph.replay if graph is not None else step
-    k = max(5, args.steps // 10)
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
+        for _ in range(max(3, warmup)):
             run()
     torch.cuda.synchronize()
     barrier(world)
@@ -610,30 +717,105 @@ def run_tp_mlp(args, rank, world, local):
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world)
     finite = bool(torch.isfinite(out["y"].float()).all().item())
+    del graph
+    return ms / k, finite
+
+
+def tp_mlp_measure(args, rank, world, local):
+    """BASELINE config 4: a 32-layer SPFP2 MLP stack (hidden 4096, intermediate
+    12288, N(0, 0.015) weights, SiLU(gate) * up), 64 bf16 tokens, tensor-
+    parallel over the `world` ranks (gate/up column-parallel, down row-parallel
+    + one all-reduce of fp32 partials per layer: NCCL, or this library's peer
+    all-reduce with --tp-allreduce peer).  Every rank returns the same dict.
+
+    Parity: rank 0's output of layers 0-1 (all ranks run them, the all-reduces
+    included) against _tp_reference of the unsharded weights; the bound is two
+    bf16 units in the last place at the output's largest magnitude (fp32 vs
+    fp64 accumulation may flip a bf16 rounding at any of the rounding points).
+    At world > 1 rank 0 also times the unsharded stack on its own GPU (TP1) for
+    the strong-scaling efficiency tp1_ms / (world * ms)."""
+    import math
+    from spark_b200 import ops
+    from spark_b200.tp import PeerAllReduce
+    device = torch.device("cuda", local)
+    peer = PeerAllReduce(TP_M * TP_H, dtype=torch.float32) if args.tp_allreduce == "peer" else None
+    layers, full = _tp_stack(rank, world, device, peer=peer, keep_full=2 if rank == 0 else 0)
+    g = torch.Generator(device=device).manual_seed(4)
+    x0 = torch.randn(TP_M, TP_H, device=device, generator=g).bfloat16()
+    stream = torch.cuda.Stream(device)
+
+    # parity of a 2-layer slice (every rank takes part in its all-reduces)
+    with torch.cuda.stream(stream):
+        y2 = layers[1](layers[0](x0))
+    torch.cuda.synchronize()
+    parity = None
+    if rank == 0:
+        ref = _tp_reference(x0, full)
+        err = float((y2.double() - ref).abs().max().item())
+        ymax = float(ref.abs().max().item())
+        tol = 2.0 ** (math.floor(math.log2(max(ymax, 2.0 ** -20))) - 6)
+        parity = {"layers": 2, "max_abs": err, "bound": tol, "ok": bool(err <= tol), "max_abs_ref": ymax,
+                  "reference": "fp64 of the unsharded SPFP2-decoded weights, bf16 at the stack's rounding points"}
+        del ref
+    del full, y2
+
+    k = max(20, args.steps // 10)
+    sec, finite = _time_stack(layers, x0, stream, args.warmup, k, world, graph_it=bool(args.tp_graph))
+    sec *= 1e-3
     ops.check_device_errors()
     if peer is not None:
         peer.check()
     barrier(world)
-    del graph
     if peer is not None:
         peer.close()
+    del layers
+    torch.cuda.empty_cache()
+
+    tp1 = None
+    if world > 1:
+        if rank == 0:
+            solo, _ = _tp_stack(0, 1, device)
+            tp1, _ = _time_stack(solo, x0, stream, args.warmup, k, 1)
+            tp1 *= 1e-3
+            del solo
+            torch.cuda.empty_cache()
+        t = torch.tensor([tp1 or 0.0], dtype=torch.float64, device=device)
+        if world > 1:
+            import torch.distributed as dist
+            dist.broadcast(t, 0)
+        tp1 = float(t.item())
         barrier(world)
+    else:
+        tp1 = sec
+
     packed_total = TP_LAYERS * 3 * (TP_I * TP_H // 16 * 5)
     peak, peak_kind = peaks()
-    sec = ms * 1e-3 / k
-    line = {"metric": "config-4 tensor-parallel SPFP2 MLP stack", "n_gpus": world, "steps": k,
-            "ms_per_step": round(ms / k, 4), "tokens_per_s": round(TP_M / sec, 1),
-            "weight_GBps_total": round(packed_total / sec / 1e9, 1),
-            "roofline": {"bound": "hbm", "achieved": round(packed_total / world / sec / 1e9, 1), "peak": peak,
-                         "unit": "GB/s per GPU", "frac": round(packed_total / world / sec / 1e9 / peak, 4),
-                         "peak_source": peak_kind},
-            "config": {"workload": "BASELINE config 4: 32 x (gate/up [12288,4096], down [4096,12288]) SPFP2, "
-                                   "N(0,0.015), M=64 bf16, SiLU(gate)*up", "tp": world,
-                       "parallelism": f"tp{world}: gate/up column-parallel, down row-parallel + "
-                                      + ("one-shot peer all-reduce (spark_peer_allreduce, fp32 partials)"
-                                         if peer is not None else "NCCL all-reduce"),
-                       "graph": bool(args.tp_graph)},
-            "finite": finite}
+    per_gpu = packed_total / world / sec / 1e9
+    return {
+        "metric": "config-4 tensor-parallel SPFP2 MLP stack", "n_gpus": world, "steps": k,
+        "ms_per_step": round(sec * 1e3, 4), "tokens_per_s": round(TP_M / sec, 1),
+        "weight_GBps_total": round(packed_total / sec / 1e9, 1),
+        "tp1_ms_per_step": round(tp1 * 1e3, 4),
+        "strong_scaling_eff": round(tp1 / (world * sec), 4),
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s per GPU",
+                     "frac": round(per_gpu / peak, 4), "peak_source": peak_kind},
+        "parity": parity, "finite": finite,
+        "config": {"workload": "BASELINE config 4: 32 x (gate/up [12288,4096], down [4096,12288]) SPFP2, "
+                               "N(0,0.015), M=64 bf16, SiLU(gate)*up", "tp": world,
+                   "parallelism": f"tp{world}: gate/up column-parallel (one row-merged launch), down "
+                                  "row-parallel + " + ("one-shot peer all-reduce (spark_peer_allreduce)"
+                                                       if peer is not None else "NCCL all-reduce")
+                                  + " of fp32 partials", "graph": bool(args.tp_graph)},
+    }
+
+
+def run_tp_mlp(args, rank, world, local):
+    """--tp-mlp: config 4 alone, its own JSON line."""
+    clk = Clocks(local)
+    clk.__enter__()
+    line = tp_mlp_measure(args, rank, world, local)
+    clk.__exit__(None, None, None)
+    line["clocks"] = clk.summary()
     if rank == 0:
         print(json.dumps(line), flush=True)
 

@@ -64,6 +64,7 @@ def lib():
             "spo_twofour_fake_quant": (None, [_f32p, _i64, _f32p]),
             "spo_linear_f64": (None, [_f32p, _i64, _i64, _f32p, _i64, _f32p, _f64p]),
             "spo_num_threads": (ctypes.c_int, []),
+            "spo_set_num_threads": (None, [ctypes.c_int]),
             "spo_cpu_spfp2_linear": (None, [_u8p, _f32p, _i64, _i64, _i64, _f32p]),
             "spo_cpu_fp3_linear": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i64, _f32p]),
             "spo_cpu_nvfp4_linear": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i64, _f32p]),
@@ -289,6 +290,10 @@ def linear_f64(x, W, bias=None) -> np.ndarray:
 
 def num_threads() -> int:
     return lib().spo_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    lib().spo_set_num_threads(int(n))
 
 
 def cpu_spfp2_linear(packed5, x, oc, ic) -> np.ndarray:

@@ -646,6 +646,16 @@ SPO_API int spo_num_threads(void) {
 #endif
 }
 
+/* Thread count of the OpenMP regions below (launchers such as torchrun set
+ * OMP_NUM_THREADS=1 per process; the CPU baseline sets it explicitly). */
+SPO_API void spo_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* CPU baseline of the reference's online path (decode + fp32 matmul per
  * call, the arithmetic of unpack_blockwise_paired followed by
  * x.float() @ W.T): one SPFP2 paired linear, rows split across threads. */

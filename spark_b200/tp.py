@@ -90,6 +90,7 @@ class PeerAllReduce:
             raise ValueError("PeerAllReduce: at most 8 ranks")
         self.numel = numel
         self.dtype = dtype
+        self._group = group
         dev = torch.device("cuda", torch.cuda.current_device())
         L = _lib.lib()
         self._lib, self._ct = L, ctypes
@@ -152,8 +153,12 @@ class PeerAllReduce:
                   self._ct.c_void_p(torch.cuda.current_stream().cuda_stream))
 
     def close(self) -> None:
-        """Unmap the other ranks' buffers (after every call using them has finished)."""
+        """Unmap the other ranks' buffers.  Every rank calls it: after the local
+        synchronize, a barrier over the group makes sure no peer's last call still
+        reads this rank's buffers before any rank unmaps or frees them."""
         torch.cuda.synchronize()
+        if self.world > 1 and dist.is_initialized():
+            dist.barrier(group=self._group)
         for h in self._opened:
             _ipc_unmap(h)
         self._opened = []
@@ -191,10 +196,14 @@ class TPMLP(torch.nn.Module):
             d = self.down
             d(h, out=self.peer.buffer().view(h.shape[0], d.out_features))
             return self.peer(torch.empty(h.shape[0], d.out_features, dtype=x.dtype, device=x.device))
-        y = self.down(h)
-        if self.world > 1:
-            dist.all_reduce(y, group=self.group)
-        return y
+        if self.world == 1:
+            return self.down(h)
+        # the ranks' partial sums meet in fp32 (as in the peer path), rounded
+        # to the activation dtype once, after the sum
+        d = self.down
+        y = d(h, out=torch.empty(h.shape[0], d.out_features, dtype=torch.float32, device=x.device))
+        dist.all_reduce(y, group=self.group)
+        return y.to(x.dtype)
 
 
 def pack_layers_split(weights: list[torch.Tensor], pack: Callable[[torch.Tensor], torch.Tensor], rank: int,
