@@ -72,10 +72,14 @@ SPARK_API int spark_version(void);
 SPARK_API int spark_spfp2_pack(const void* w, int w_dtype, int64_t n, uint8_t* packed, uint8_t* expv, void* stream);
 /* pack_blockwise_search(w, window=2) -- 01_core/block_fp2_emu.py:86.  packed: n/8*3 bytes. */
 SPARK_API int spark_spfp2_pack_v1(const void* w, int w_dtype, int64_t n, uint8_t* packed, uint8_t* expv, void* stream);
-/* unpack_blockwise_paired(packed, n_elements) -- 01_core/block_fp2_emu.py:270; replaces the
- * decode_fp32/decode_fp16 torch ops (01_core/build_spark_fp2.py:28-54) and
- * spark_decode_launch_f32/f16 (01_core/block_fp2_kernel.cu:67-87). */
+/* unpack_blockwise_paired(packed, n_elements) -- 01_core/block_fp2_emu.py:270. */
 SPARK_API int spark_spfp2_unpack(const uint8_t* packed, int64_t n_elements, void* out, int out_dtype, void* stream);
+/* The legacy single-exponent layout (5 B per 16 weights: 32-bit code word + exponent in
+ * the low nibble of byte 4) -- replaces spark_decode_launch_f32/f16
+ * (01_core/block_fp2_kernel.cu:67-87, kernels :3-62) behind the decode_fp32/decode_fp16
+ * torch ops (01_core/build_spark_fp2.py:28-54).  out: 16 * n_blocks values. */
+SPARK_API int spark_spfp2_legacy_decode(const uint8_t* packed, int64_t n_blocks, void* out, int out_dtype,
+                                        void* stream);
 /* unpack_blockwise(packed) (3-byte) -- 01_core/block_fp2_emu.py:204. */
 SPARK_API int spark_spfp2_unpack_v1(const uint8_t* packed, int64_t n_blocks, void* out, int out_dtype, void* stream);
 /* channel_fake_quantize(w) forward -- 01_core/block_fp2_emu.py:365 (STE backward is the
@@ -174,7 +178,7 @@ SPARK_API int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* s
  * the decode GEMV and the tcgen05 GEMM routes); it allocates nothing.  Its
  * scratch is one static 16 MiB array per device inside the library, so a call
  * must fit it: spark_linear_workspace_size(fmt, M, oc, ic) <= 16 MiB, which
- * holds for every token count up to ic = 182,264 on a 148-SM GPU.  A call
+ * holds for every token count up to ic = 182,204 on a 148-SM GPU.  A call
  * that does not fit returns SPARK_ERR_WORKSPACE with a message naming this
  * entry point.
  *   - The first call on a device (with that device current) looks the scratch
@@ -222,6 +226,27 @@ typedef struct {
 } SparkChainOp;
 SPARK_API size_t spark_linear_chain_workspace_size(int n_ops);
 SPARK_API int spark_linear_chain(const SparkChainOp* ops, int n_ops, int64_t M, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* A batch of decode-sized dequant linears (1 to 48 ops, M <= 16 tokens, bf16
+ * activations) in ONE persistent launch: the weights of every op stream from
+ * HBM through one shared-memory ring per SM without a gap at op boundaries.
+ * No counterpart in the reference (it runs one linear per call,
+ * 01_core/spark_v3_kernel.cu:172-214); it replaces a sequence of spark_linear
+ * calls, e.g. the projections of a decoder layer.  Each op is a SparkChainOp
+ * of kind SPARK_CHAIN_LINEAR with fmt = SPARK_FMT_SPFP2 / FP3 / NVFP4 |
+ * SPARK_LAYOUT_TILED (weights from spark_tile_weights, 16-byte aligned), optionally
+ * | SPARK_EPILOGUE_SILU; x bf16 [M, ic] (16-byte aligned, ldx a multiple of 8),
+ * ic a multiple of 256; y [M, oc] (oc / 2 with SiLU) of y_dtype, row stride ldy;
+ * dep[] = earlier ops whose output this op reads (-1: none): the op's
+ * activations are read only after those ops complete, its weights stream
+ * earlier.  Results equal spark_linear's within fp32 summation order.
+ * workspace: spark_linear_batch_workspace_size(ops, n_ops, M) bytes, 256-byte
+ * aligned, zero-filled before its first use (it may be shared with
+ * spark_linear calls on the same stream); launches that share it must not
+ * overlap on the GPU.  The launch is cooperative (one CTA per SM). */
+SPARK_API size_t spark_linear_batch_workspace_size(const SparkChainOp* ops, int n_ops, int64_t M);
+SPARK_API int spark_linear_batch(const SparkChainOp* ops, int n_ops, int64_t M, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
 /* Fragment-major copy of a packed weight for spark_linear(fmt | SPARK_LAYOUT_TILED):

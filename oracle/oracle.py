@@ -64,6 +64,7 @@ def lib():
             "spo_twofour_fake_quant": (None, [_f32p, _i64, _f32p]),
             "spo_linear_f64": (None, [_f32p, _i64, _i64, _f32p, _i64, _f32p, _f64p]),
             "spo_num_threads": (ctypes.c_int, []),
+            "spo_spfp2_legacy_decode": (None, [_u8p, _i64, _f32p]),
             "spo_set_num_threads": (None, [ctypes.c_int]),
             "spo_cpu_spfp2_linear": (None, [_u8p, _f32p, _i64, _i64, _i64, _f32p]),
             "spo_cpu_fp3_linear": (None, [_u8p, _u8p, _f32p, _i64, _i64, _i64, _f32p]),
@@ -135,6 +136,15 @@ def unpack_blockwise_paired(packed5, n_elements: int) -> np.ndarray:
     npairs = p.size // 5
     out = np.zeros(n_elements, np.float32)
     lib().spo_spfp2_unpack_paired(_p(p, _u8p), npairs, n_elements, _p(out, _f32p))
+    return out
+
+
+def spfp2_legacy_decode(packed5) -> np.ndarray:
+    """block_fp2_kernel.cu's 16-weight single-exponent blocks (decode_fp32 / decode_fp16)."""
+    p = _u8(packed5)
+    nb = p.size // 5
+    out = np.zeros(nb * 16, np.float32)
+    lib().spo_spfp2_legacy_decode(_p(p, _u8p), nb, _p(out, _f32p))
     return out
 
 

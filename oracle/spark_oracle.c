@@ -191,6 +191,20 @@ SPO_API void spo_spfp2_unpack3(const uint8_t* p3, int64_t nb, float* out) {
     }
 }
 
+/* Legacy single-exponent blocks of the reference's decode_fp32 / decode_fp16 ops --
+ * block_fp2_kernel.cu:3-34: 5 bytes per 16 weights, a little-endian 32-bit word of
+ * 2-bit codes and the exponent in the low nibble of byte 4; value = (+1, -1, 0, 0)[code]
+ * * 2^(e-10).  The reference forms the scale with __powf(2, e - 10); this restatement
+ * takes it as the exact power of two (parity unpinned: that kernel is built for
+ * sm_120 and has no golden vectors). */
+SPO_API void spo_spfp2_legacy_decode(const uint8_t* p5, int64_t nb, float* out) {
+    for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* q = p5 + 5 * b;
+        spfp2_decode8((uint16_t)(q[0] | (q[1] << 8)), q[4] & 0x0f, out + 16 * b);
+        spfp2_decode8((uint16_t)(q[2] | (q[3] << 8)), q[4] & 0x0f, out + 16 * b + 8);
+    }
+}
+
 /* unpack_blockwise_paired -- block_fp2_emu.py:270-308 (truncated to n_elements) */
 SPO_API void spo_spfp2_unpack_paired(const uint8_t* p5, int64_t n_pairs, int64_t n_elements, float* out) {
     float tmp[16];

@@ -58,6 +58,7 @@ _SIGNATURES = {
     "spark_spfp2_pack": (_i, [_p, _i, _i64, _p, _p, _p]),
     "spark_spfp2_pack_v1": (_i, [_p, _i, _i64, _p, _p, _p]),
     "spark_spfp2_unpack": (_i, [_p, _i64, _p, _i, _p]),
+    "spark_spfp2_legacy_decode": (_i, [_p, _i64, _p, _i, _p]),
     "spark_spfp2_unpack_v1": (_i, [_p, _i64, _p, _i, _p]),
     "spark_spfp2_fake_quant": (_i, [_p, _i, _i64, _p, _i, _p]),
     "spark_fp3_pack": (_i, [_p, _i, _i64, _i64, _p, _p, _p]),
@@ -78,6 +79,8 @@ _SIGNATURES = {
     "spark_linear": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p]),
     "spark_linear_prefetch": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p,
                                    _i64, _p]),
+    "spark_linear_batch_workspace_size": (_sz, [_p, _i, _i64]),
+    "spark_linear_batch": (_i, [_p, _i, _i64, _p, _sz, _p]),
     "spark_linear_chain_workspace_size": (_sz, [_i]),
     "spark_linear_chain": (_i, [_p, _i, _i64, _p, _sz, _p]),
     "spark_linear_noalloc": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p]),

@@ -784,21 +784,31 @@ __global__ void __launch_bounds__(256) k_tile(const uint8_t* __restrict__ wq, co
         }
     }
     if constexpr (FMT == SPARK_FMT_SPFP2) {
-        // swap codes (1,2) and (5,6) of every 16-bit mantissa word so the
-        // decoders emit registers in natural column order
-        uint8_t* b = reinterpret_cast<uint8_t*>(w);
+        // Stream layout (the decoders of stream.cu): per 8-column block s of
+        // the chunk, word s = codes of row g (low half) | row g + 8 (high
+        // half), block column i at bits 4i and column 4 + i at bits 4i + 2;
+        // words 8-9: byte s % 4 of word 8 + s / 4 = e(row g) | e(row g + 8) << 4.
+        // The reference pair layout holds, per 16 columns, mantissa words
+        // m0, m1 (column j at bits 2j) and the exponent byte e0 | e1 << 4.
+        const uint8_t* b = reinterpret_cast<const uint8_t*>(w);
+        uint32_t out[10] = {};
 #pragma unroll
         for (int half = 0; half < 2; ++half)
 #pragma unroll
-            for (int pr = 0; pr < 4; ++pr)
+            for (int blk = 0; blk < 8; ++blk) {
+                const uint8_t* q = b + half * 20 + (blk >> 1) * 5;
+                const int h = blk & 1;
+                const uint32_t m = (uint32_t)q[2 * h] | ((uint32_t)q[2 * h + 1] << 8);
+                const uint32_t e = h ? (q[4] >> 4) : (q[4] & 0xfu);
+                uint32_t p = 0;
 #pragma unroll
-                for (int mw = 0; mw < 2; ++mw) {
-                    uint8_t* q = b + half * 20 + pr * 5 + mw * 2;
-                    const uint32_t m = (uint32_t)q[0] | ((uint32_t)q[1] << 8);
-                    const uint32_t mp = (m & 0xc3c3u) | ((m & 0x0c0cu) << 2) | ((m & 0x3030u) >> 2);
-                    q[0] = (uint8_t)mp;
-                    q[1] = (uint8_t)(mp >> 8);
-                }
+                for (int i = 0; i < 4; ++i)
+                    p |= (((m >> (2 * i)) & 3u) << (4 * i)) | (((m >> (2 * (4 + i))) & 3u) << (4 * i + 2));
+                out[blk] |= p << (16 * half);
+                out[8 + (blk >> 2)] |= e << (8 * (blk & 3) + 4 * half);
+            }
+#pragma unroll
+        for (int i = 0; i < 10; ++i) w[i] = out[i];
     }
     uint8_t* dst = tiled + u * unit_bytes_tiled<FMT>();
 #pragma unroll
@@ -1167,8 +1177,9 @@ int cols_per_unit(int fmt) { return fmt == SPARK_FMT_TWOFOUR ? 512 : 256; }
 constexpr int64_t kMaxRowGroups = 1 << 16;   // oc <= 1,048,576
 struct WsLayout {
     size_t err = 0;                            // int error word
-    size_t sigma = 256;                        // float[16]
-    size_t counters = 512;                     // int[kMaxRowGroups]
+    // [64, 4096): control block of the batched decode kernel (stream.cu)
+    size_t sigma = 4096;                       // float[16]
+    size_t counters = 4352;                    // int[kMaxRowGroups]
     size_t partials = 0;                       // float[T][2][2*32*4]
     size_t xp = 0;                             // half[2][16][ic] (hi, lo parts)
     size_t total = 0;
@@ -1298,6 +1309,14 @@ bool fast_path_ok(int fmt, const uint8_t* wq, const uint8_t* scales, int64_t oc,
 }  // namespace spark
 
 namespace spark {
+struct StreamPlan;
+int stream_plan_alloc(StreamPlan** P);
+void stream_plan_free(StreamPlan* P);
+size_t stream_plan_scratch(const StreamPlan* P);
+int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size_t counters_off,
+                int64_t max_counters, size_t scratch_off, StreamPlan* P);
+int stream_launch(const StreamPlan& P, cudaStream_t s);
+size_t stream_scratch_single(int64_t M, int64_t ic);
 size_t tc_partials_bytes(int dev, int64_t M);
 bool tc_linear_ok(int fmt, const void* wq, const void* scales, const void* x, int x_dtype, int64_t ic,
                   int64_t ldx);
@@ -1317,7 +1336,7 @@ size_t spark_linear_workspace_size(int fmt, int64_t M, int64_t oc, int64_t ic) {
     int dev = 0;
     cudaGetDevice(&dev);
     const WsLayout L = ws_layout(ic, max_warps(dev));
-    return std::max(L.total, L.partials + tc_partials_bytes(dev, M));
+    return std::max({L.total, L.partials + tc_partials_bytes(dev, M), L.partials + stream_scratch_single(M, ic)});
 }
 
 int spark_linear(int fmt, const uint8_t* wq, const uint8_t* scales, const void* x, int x_dtype, int64_t M,
@@ -1374,6 +1393,45 @@ int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, con
                                reinterpret_cast<int*>(ws + L.err), reinterpret_cast<int*>(ws + L.counters),
                                kMaxRowGroups, reinterpret_cast<float*>(ws + L.partials), s);
     }
+    if (tiled && fmt != SPARK_FMT_TWOFOUR && x_dtype == SPARK_DTYPE_BF16 && aligned(x, 16) && ldx % 8 == 0) {
+        // bf16 activations on tiled SPFP2 / FP3 / NVFP4: the batched decode
+        // kernel (stream.cu), one op per 16-token chunk
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const WsLayout L = ws_layout(ic, max_warps(dev));
+        SPARK_REQUIRE(workspace && aligned(workspace, 256), SPARK_ERR_WORKSPACE,
+                      "spark_linear: a 256-byte aligned workspace is required");
+        StreamPlan* P = nullptr;
+        int rc = stream_plan_alloc(&P);
+        if (rc) return rc;
+        for (int64_t m0 = 0; m0 < M && rc == SPARK_OK; m0 += kMaxTokens) {
+            const int64_t mc = std::min<int64_t>(kMaxTokens, M - m0);
+            SparkChainOp op = {};
+            op.kind = SPARK_CHAIN_LINEAR;
+            op.fmt = fmt | SPARK_LAYOUT_TILED | (silu ? SPARK_EPILOGUE_SILU : 0);
+            op.wq = wq;
+            op.x = static_cast<const uint16_t*>(x) + m0 * ldx;
+            op.ic = ic;
+            op.ldx = ldx;
+            op.oc = oc;
+            op.bias = bias;
+            op.bias_dtype = bias_dtype;
+            op.y = static_cast<uint8_t*>(y) + m0 * ldy * (y_dtype == SPARK_DTYPE_F32 ? 4 : 2);
+            op.y_dtype = y_dtype;
+            op.ldy = ldy;
+            op.dep[0] = op.dep[1] = -1;
+            rc = stream_plan(&op, 1, mc, static_cast<uint8_t*>(workspace), L.counters, kMaxRowGroups, L.partials, P);
+            if (rc == SPARK_OK && L.partials + stream_plan_scratch(P) > workspace_bytes)
+                rc = set_error(SPARK_ERR_WORKSPACE, "spark_linear: workspace of %zu bytes needed (got %zu)",
+                               L.partials + stream_plan_scratch(P), workspace_bytes);
+            if (rc == SPARK_OK) rc = stream_launch(*P, s);
+        }
+        stream_plan_free(P);
+        return rc;
+    }
+    SPARK_REQUIRE(!(tiled && fmt == SPARK_FMT_SPFP2), SPARK_ERR_UNSUPPORTED,
+                  "spark_linear: tiled SPFP2 weights take bf16 activations (16-byte aligned, ldx %% 8 == 0); "
+                  "use the reference layout for other activations");
     if (tiled) {
         SPARK_REQUIRE(aligned(wq, 16), SPARK_ERR_ALIGNMENT, "spark_linear: tiled weights must be 16-byte aligned");
     } else if (!fast_path_ok(fmt, wq, scales, oc, ic)) {
@@ -1442,7 +1500,6 @@ int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, con
         const int NT = mc > 8 ? 2 : 1;
         if (tiled) {
             switch (fmt) {
-                case SPARK_FMT_SPFP2: rc = launch_fmt_tiled<SPARK_FMT_SPFP2>(a, NT, XS, bf, T, s); break;
                 case SPARK_FMT_FP3: rc = launch_fmt_tiled<SPARK_FMT_FP3>(a, NT, XS, bf, T, s); break;
                 case SPARK_FMT_NVFP4: rc = launch_fmt_tiled<SPARK_FMT_NVFP4>(a, NT, XS, bf, T, s); break;
                 default: rc = launch_fmt_tiled<SPARK_FMT_TWOFOUR>(a, NT, XS, bf, T, s); break;
@@ -1498,6 +1555,38 @@ int spark_tile_weights(int fmt, const uint8_t* wq, const uint8_t* scales, int64_
     return check_launch("spark_tile_weights");
 }
 
+size_t spark_linear_batch_workspace_size(const SparkChainOp* ops, int n_ops, int64_t M) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const WsLayout L = ws_layout(0, max_warps(dev));
+    StreamPlan* P = nullptr;
+    if (stream_plan_alloc(&P)) return 0;
+    size_t need = 0;
+    if (stream_plan(ops, n_ops, M, nullptr, L.counters, kMaxRowGroups, L.partials, P) == SPARK_OK)
+        need = (L.partials + stream_plan_scratch(P) + 255) / 256 * 256;
+    stream_plan_free(P);
+    return need;
+}
+
+int spark_linear_batch(const SparkChainOp* ops, int n_ops, int64_t M, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const WsLayout L = ws_layout(0, max_warps(dev));
+    SPARK_REQUIRE(workspace && aligned(workspace, 256), SPARK_ERR_WORKSPACE,
+                  "spark_linear_batch: a 256-byte aligned workspace is required");
+    StreamPlan* P = nullptr;
+    int rc = stream_plan_alloc(&P);
+    if (rc) return rc;
+    rc = stream_plan(ops, n_ops, M, static_cast<uint8_t*>(workspace), L.counters, kMaxRowGroups, L.partials, P);
+    if (rc == SPARK_OK && L.partials + stream_plan_scratch(P) > workspace_bytes)
+        rc = set_error(SPARK_ERR_WORKSPACE, "spark_linear_batch: workspace of %zu bytes needed (got %zu)",
+                       L.partials + stream_plan_scratch(P), workspace_bytes);
+    if (rc == SPARK_OK) rc = stream_launch(*P, reinterpret_cast<cudaStream_t>(stream));
+    stream_plan_free(P);
+    return rc;
+}
+
 int spark_workspace_check(void* workspace, void* stream) {
     SPARK_REQUIRE(workspace, SPARK_ERR_INVALID, "spark_workspace_check: null workspace");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -1526,8 +1615,8 @@ int spark_workspace_check(void* workspace, void* stream) {
 // partials.  spark_linear_noalloc takes that scratch from one statically sized
 // array in this module (one copy per device) instead of a caller-provided
 // workspace, and allocates nothing.  16 MiB covers the tcgen05 route at any
-// token count (262,656 + 2 * SMs * 64 * 128 * 4 bytes: 9.96 MB on 148 SMs) and
-// the decode GEMV up to ic = 182,264 on 148 SMs.
+// token count (266,496 + 2 * SMs * 64 * 128 * 4 bytes: 9.97 MB on 148 SMs) and
+// the decode GEMV up to ic = 182,204 on 148 SMs.
 namespace spark {
 namespace {
 

@@ -237,6 +237,23 @@ __global__ void __launch_bounds__(kThreads) k_spfp2_unpack_v1(const uint8_t* __r
     for (int i = 0; i < 8; ++i) store_from_float(out, dtype, b * 8 + i, v[i]);
 }
 
+// Legacy single-exponent blocks read by the reference's decode_fp32 /
+// decode_fp16 ops (01_core/block_fp2_kernel.cu:3-34): 5 bytes per 16 weights,
+// bytes 0-3 a little-endian word of 16 2-bit codes (code j at bits 2j), byte 4
+// the exponent in its low nibble (the high nibble is ignored); value =
+// (+1, -1, 0, 0)[code] * 2^(e-10).
+__global__ void __launch_bounds__(kThreads) k_spfp2_legacy_decode(const uint8_t* __restrict__ packed, int64_t nb,
+                                                                   void* __restrict__ out, int dtype) {
+    const int64_t b = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    if (b >= nb) return;
+    const uint8_t* q = packed + 5 * b;
+    float v[16];
+    spfp2_decode8((uint32_t)q[0] | ((uint32_t)q[1] << 8), q[4] & 0xf, v);
+    spfp2_decode8((uint32_t)q[2] | ((uint32_t)q[3] << 8), q[4] & 0xf, v + 8);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) store_from_float(out, dtype, b * 16 + i, v[i]);
+}
+
 // channel_fake_quantize forward: search + 3-byte decode per flattened 8-block
 // (block_fp2_emu.py:365-375).  With `twofour`, two_four_apply follows on each
 // group of 4 (two_four.py:70-75): the first two nonzeros survive and dropped
@@ -674,6 +691,14 @@ int spark_spfp2_unpack_v1(const uint8_t* packed, int64_t n_blocks, void* out, in
     if (n_blocks == 0) return SPARK_OK;
     k_spfp2_unpack_v1<<<grid_for(n_blocks), kThreads, 0, S(stream)>>>(packed, n_blocks, out, out_dtype);
     return check_launch("spark_spfp2_unpack_v1");
+}
+
+int spark_spfp2_legacy_decode(const uint8_t* packed, int64_t n_blocks, void* out, int out_dtype, void* stream) {
+    SPARK_REQUIRE(packed && out && n_blocks >= 0, SPARK_ERR_INVALID, "spark_spfp2_legacy_decode: null pointer");
+    SPARK_REQUIRE(dtype_ok(out_dtype), SPARK_ERR_INVALID, "spark_spfp2_legacy_decode: bad dtype %d", out_dtype);
+    if (n_blocks == 0) return SPARK_OK;
+    k_spfp2_legacy_decode<<<grid_for(n_blocks), kThreads, 0, S(stream)>>>(packed, n_blocks, out, out_dtype);
+    return check_launch("spark_spfp2_legacy_decode");
 }
 
 int spark_spfp2_fake_quant(const void* w, int w_dtype, int64_t n, void* out, int out_dtype, void* stream) {

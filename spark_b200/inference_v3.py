@@ -93,11 +93,23 @@ class V3PackedLinear(nn.Module):
             ic = pad
         # up to 16 tokens: the decode GEMV on the tiled copy; more: the tcgen05
         # GEMM, which reads the reference-layout bytes
-        if self.w_tiled is not None and ic == self.in_features and x.numel() <= 16 * ic:
+        if self.tiled_ok(x) and ic == self.in_features:
             return ops.linear(self.fmt, self.w_tiled, None, x, self.out_features, ic, bias=self.bias,
                               out_dtype=x.dtype, out=out, tiled=True, prefetch=self.prefetch_next)
         return ops.linear(self.fmt, self.w_packed, self.w_scales, x, self.out_features, ic,
                           bias=self.bias, out_dtype=x.dtype, out=out)
+
+    def tiled_ok(self, x: torch.Tensor) -> bool:
+        """True when x (up to 16 tokens) can run on the tiled copy: any
+        activation dtype for FP3 / NVFP4; bf16 rows on 16 bytes for SPFP2,
+        whose tiled layout feeds the fp8 / bf16 tensor path of the batched
+        decode kernel.  Other activations read the reference-layout bytes."""
+        if self.w_tiled is None or x.shape[-1] != self.in_features or x.numel() > 16 * self.in_features:
+            return False
+        if self.fmt != "spfp2":
+            return True
+        return (x.dtype == torch.bfloat16 and x.stride(-1) == 1 and x.data_ptr() % 16 == 0
+                and (x.dim() == 1 or x.reshape(-1, x.shape[-1]).stride(0) % 8 == 0))
 
     def extra_repr(self) -> str:
         return f"fmt={self.fmt}, in_features={self.in_features}, out_features={self.out_features}"
@@ -195,7 +207,7 @@ class V3GateUpSiLU(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         m = self.merged
-        if m.w_tiled is not None and x.shape[-1] == m.in_features and x.numel() <= 16 * m.in_features:
+        if m.tiled_ok(x):
             return ops.linear(m.fmt, m.w_tiled, None, x, m.out_features, m.in_features, bias=m.bias,
                               out_dtype=x.dtype, tiled=True, prefetch=m.prefetch_next, silu=True)
         y = m(x).reshape(-1, self.out_features // 8, 2, 8)
@@ -204,6 +216,45 @@ class V3GateUpSiLU(nn.Module):
 
     def extra_repr(self) -> str:
         return f"fmt={self.merged.fmt}, in_features={self.in_features}, out_features={self.out_features}, silu"
+
+
+class V3LinearBatch:
+    """The forwards of several packed layers (V3PackedLinear, V3MergedLinear,
+    V3GateUpSiLU) in ONE launch of the batched decode kernel
+    (spark_linear_batch): a decode step's projections stream their weights
+    back to back instead of paying a kernel ramp and tail each.
+
+    deps[i]: indices of earlier layers whose OUTPUT layer i reads as its input
+    (at most two); the kernel then waits for them on the device.  Calls take
+    bf16 activations, one [M, in_features] tensor per layer (M <= 16, the
+    same M for all), and return one [M, width] tensor per layer: the stacked
+    output of a V3MergedLinear (split it with .split(layer.splits, -1)),
+    SiLU(gate) * up for a V3GateUpSiLU.  Layers must hold tiled weights."""
+
+    def __init__(self, layers: list, deps: list | None = None):
+        self.layers = list(layers)
+        self.deps = [list(d) for d in deps] if deps is not None else [[] for _ in self.layers]
+        if len(self.deps) != len(self.layers):
+            raise ValueError("V3LinearBatch: one deps entry per layer")
+        self._spec = []
+        for m in self.layers:
+            silu = isinstance(m, V3GateUpSiLU)
+            lin = m.merged if isinstance(m, (V3MergedLinear, V3GateUpSiLU)) else m
+            if lin.w_tiled is None:
+                raise ValueError(f"V3LinearBatch: {lin.fmt} [{lin.out_features}, {lin.in_features}] has no tiled copy")
+            width = lin.out_features // 2 if silu else lin.out_features
+            self._spec.append((lin, silu, width))
+
+    def __call__(self, inputs: list, outs: list | None = None) -> list:
+        if len(inputs) != len(self.layers):
+            raise ValueError("V3LinearBatch: one input per layer")
+        if outs is None:
+            outs = [torch.empty(x.shape[0], w, dtype=x.dtype, device=x.device)
+                    for x, (_, _, w) in zip(inputs, self._spec)]
+        batch = [ops.BatchOp(lin.fmt, lin.w_tiled, x, y, bias=lin.bias, silu=silu, deps=d)
+                 for (lin, silu, _), x, y, d in zip(self._spec, inputs, outs, self.deps)]
+        ops.linear_batch(batch)
+        return outs
 
 
 def chain_prefetch(modules: list) -> None:

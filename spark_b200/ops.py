@@ -371,6 +371,58 @@ def linear_chain(chain: list[ChainOp], stream=None) -> None:
          ctypes.c_void_p(st.cuda_stream))
 
 
+class BatchOp:
+    """One linear of linear_batch: y = x . decode(W)^T (+ bias) on tiled weights
+    (tile_weights), bf16 x [M, ic]; silu: the weight holds gate/up rows in
+    groups of 8 + 8 and y = SiLU(gate) * up, oc // 2 wide.  deps: indices of
+    earlier ops of the batch whose output this op reads."""
+
+    def __init__(self, fmt, wq_tiled: torch.Tensor, x: torch.Tensor, y: torch.Tensor, bias=None,
+                 silu: bool = False, deps=()):
+        self.fmt, self.wq, self.x, self.y, self.bias, self.silu, self.deps = fmt, wq_tiled, x, y, bias, silu, list(deps)
+
+
+def _batch_array(batch: list[BatchOp]):
+    arr = (_lib.SparkChainOp * len(batch))()
+    for k, op in enumerate(batch):
+        c = arr[k]
+        if op.x.dtype != torch.bfloat16:
+            raise TypeError("linear_batch: activations must be bfloat16")
+        if op.x.dim() != 2 or op.x.stride(1) != 1 or op.y.dim() != 2 or op.y.stride(1) != 1:
+            raise ValueError("linear_batch: x and y must be 2-D with unit column stride")
+        deps = op.deps + [-1] * (2 - len(op.deps))
+        if len(deps) > 2:
+            raise ValueError("linear_batch: at most two deps per op")
+        f = FORMATS[op.fmt] if isinstance(op.fmt, str) else int(op.fmt)
+        c.kind, c.fmt = _lib.CHAIN_LINEAR, f | LAYOUT_TILED | (EPILOGUE_SILU if op.silu else 0)
+        c.wq, c.scales = _bytes(op.wq).data_ptr(), None
+        c.x, c.ic, c.ldx = op.x.data_ptr(), op.x.shape[1], op.x.stride(0)
+        c.oc = op.y.shape[1] * (2 if op.silu else 1)
+        c.y, c.y_dtype, c.ldy = op.y.data_ptr(), _dt(op.y), op.y.stride(0)
+        if op.bias is not None:
+            c.bias, c.bias_dtype = op.bias.data_ptr(), _dt(op.bias)
+        c.dep[0], c.dep[1] = deps[0], deps[1]
+    return arr
+
+
+def linear_batch(batch: list[BatchOp], stream=None) -> None:
+    """Run the linears in one persistent launch (spark_linear_batch).  Every op
+    shares the token count M (rows of x); outputs are the ops' preallocated y."""
+    if not batch:
+        return
+    x0 = batch[0].x
+    M = x0.shape[0]
+    arr = _batch_array(batch)
+    st = stream if stream is not None else torch.cuda.current_stream(x0.device)
+    n = int(_lib.lib().spark_linear_batch_workspace_size(ctypes.cast(arr, ctypes.c_void_p), len(batch), M))
+    if n == 0:
+        # an invalid batch: let the call itself report why
+        n = 1 << 20
+    ws = workspace(x0.device, n, stream=st)
+    call("spark_linear_batch", ctypes.cast(arr, ctypes.c_void_p), len(batch), M, _p(ws), ws.numel(),
+         ctypes.c_void_p(st.cuda_stream))
+
+
 def check_device_errors(device=None) -> None:
     """Raise if a kernel left an error in a workspace (synchronises)."""
     for (dev, sh), buf in list(_ws.items()) + list(_chain_ws.items()):

@@ -87,6 +87,13 @@ def test_linear_tiled(fmt, oc, ic, M):
 @pytest.mark.parametrize("fmt", ["spfp2", "fp3", "nvfp4", "twofour"])
 def test_linear_tiled_chunks_bias_dtypes(fmt):
     check(fmt, 1024, 1024, 17, bias=True, tiled=True)
+    if fmt == "spfp2":
+        # the tiled SPFP2 layout takes bf16 activations only
+        from spark_b200._lib import SparkError
+        for xd in (torch.float32, torch.float16):
+            with pytest.raises(SparkError, match="bf16"):
+                check(fmt, 1024, 1024, 3, seed=4, x_dtype=xd, tiled=True)
+        return
     check(fmt, 1024, 1024, 3, seed=4, x_dtype=torch.float32, bias=True, tiled=True)
     check(fmt, 1000, 1024, 5, seed=6, x_dtype=torch.float16, out_dtype=torch.float16, tiled=True)
 

@@ -1,0 +1,198 @@
+"""The batched decode kernel (spark_linear_batch, and spark_linear on tiled
+weights with bf16 activations) against an fp64 accumulation of the
+oracle-decoded weights.
+
+Tolerance: max |y - y_ref| <= 5e-4 for fp32 output; for
+activations scaled away from 1 the bound scales with max |y_ref| (relative
+1e-5, the fp32 accumulation's own error at these sizes).  SPFP2 up to 4 tokens
+runs the fp8 tensor path (activations split into e4m3 parts), above that and
+for non-finite activations the bf16 path; FP3 / NVFP4 always the bf16 path.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 5e-4
+
+
+def ops():
+    from spark_b200 import ops as _ops
+    return _ops
+
+
+def make(fmt, oc, ic, seed, std=0.02):
+    g = torch.Generator().manual_seed(seed)
+    W = (torch.randn(oc, ic, generator=g) * std).cuda()
+    if fmt == "spfp2":
+        wq, s = ops().spfp2_pack(W)[0], None
+        dec = O.unpack_blockwise_paired(wq.cpu().numpy(), oc * ic).reshape(oc, ic)
+    elif fmt == "fp3":
+        wq, s = ops().fp3_pack(W)
+        dec = O.fp3_unpack_3bit(wq.cpu().numpy(), s.cpu().view(torch.uint8).numpy(), oc, ic)
+    else:
+        wq, s = ops().nvfp4_pack(W)
+        dec = O.nvfp4_unpack(wq.cpu().numpy(), s.cpu().view(torch.uint8).numpy(), oc, ic)
+    return wq, s, ops().tile_weights(fmt, wq, s, oc, ic), dec
+
+
+def ref(x, dec, bias=None):
+    return O.linear_f64(x.float().cpu().numpy(), dec, bias.float().cpu().numpy() if bias is not None else None)
+
+
+SHAPES = [("spfp2", 9728, 2560), ("spfp2", 2560, 9728), ("fp3", 4096, 2560), ("nvfp4", 2560, 4096),
+          ("spfp2", 1000, 768), ("fp3", 300, 512), ("nvfp4", 40, 2048)]
+
+
+@pytest.mark.parametrize("fmt,oc,ic", SHAPES)
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 9, 16])
+def test_single_linear(fmt, oc, ic, M):
+    wq, s, wt, dec = make(fmt, oc, ic, seed=oc + ic + M)
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn(M, ic, generator=g).bfloat16().cuda()
+    y = ops().linear(fmt, wt, None, x, oc, ic, out_dtype=torch.float32, tiled=True)
+    torch.cuda.synchronize()
+    err = np.abs(y.cpu().numpy() - ref(x, dec)).max()
+    assert err <= TOL, (fmt, oc, ic, M, err)
+    ops().check_device_errors()
+
+
+@pytest.mark.parametrize("fmt", ["spfp2", "fp3", "nvfp4"])
+def test_bias_and_output_dtypes(fmt):
+    oc, ic = 1024, 1024
+    wq, s, wt, dec = make(fmt, oc, ic, seed=5)
+    g = torch.Generator().manual_seed(6)
+    for M in (1, 4, 12):
+        x = torch.randn(M, ic, generator=g).bfloat16().cuda()
+        b = (torch.randn(oc, generator=g) * 0.1).cuda()
+        y64 = ref(x, dec, b)
+        for od in (torch.float32, torch.bfloat16, torch.float16):
+            y = ops().linear(fmt, wt, None, x, oc, ic, bias=b, out_dtype=od, tiled=True).float().cpu().numpy()
+            bound = TOL if od == torch.float32 else TOL + 2.0 ** -7 * np.abs(y64)
+            assert np.all(np.abs(y - y64) <= bound), (fmt, M, od)
+
+
+def test_spfp2_activation_range():
+    """fp8 path: the per-token power-of-two scale and four e4m3 parts keep the
+    result at fp32-accumulation accuracy whatever the activations' magnitude,
+    also with one large outlier per token."""
+    oc, ic = 512, 2560
+    wq, s, wt, dec = make("spfp2", oc, ic, seed=9)
+    g = torch.Generator().manual_seed(10)
+    for scale in (1e-6, 1e-2, 1.0, 3e4, 1e8):
+        for M in (1, 3):
+            x = torch.randn(M, ic, generator=g) * scale
+            x[:, 7] = 1000.0 * scale                      # an outlier 3 decades above the rest
+            x = x.bfloat16().cuda()
+            y = ops().linear("spfp2", wt, None, x, oc, ic, out_dtype=torch.float32, tiled=True).cpu().numpy()
+            y64 = ref(x, dec)
+            rel = np.abs(y - y64).max() / max(np.abs(y64).max(), 1e-30)
+            assert rel < 1e-5, (scale, M, rel)
+
+
+def test_spfp2_nonfinite_activations():
+    """A non-finite activation moves the op to the bf16 path: the result has the
+    same NaN / inf pattern as the reference-layout linear, the rest matches."""
+    oc, ic = 256, 1024
+    wq, s, wt, dec = make("spfp2", oc, ic, seed=11)
+    x = torch.randn(3, ic).bfloat16().cuda()
+    x[0, 5] = float("inf")
+    x[1, 9] = float("nan")              # token 2 stays finite
+    y = ops().linear("spfp2", wt, None, x, oc, ic, out_dtype=torch.float32, tiled=True).cpu()
+    y_ref = ops().linear("spfp2", wq, None, x, oc, ic, out_dtype=torch.float32).cpu()
+    assert torch.equal(torch.isnan(y), torch.isnan(y_ref))
+    assert torch.equal(torch.isinf(y), torch.isinf(y_ref))
+    fin = torch.isfinite(y_ref)
+    assert (y[fin] - y_ref[fin]).abs().max().item() <= TOL
+
+
+def test_zero_activations():
+    wq, s, wt, dec = make("spfp2", 256, 512, seed=12)
+    x = torch.zeros(1, 512, dtype=torch.bfloat16, device="cuda")
+    y = ops().linear("spfp2", wt, None, x, 256, 512, out_dtype=torch.float32, tiled=True)
+    assert torch.count_nonzero(y).item() == 0
+
+
+def test_repeat_calls_bit_identical():
+    for fmt in ("spfp2", "fp3", "nvfp4"):
+        wq, s, wt, dec = make(fmt, 2560, 9728 if fmt == "spfp2" else 4096, seed=13)
+        ic = 9728 if fmt == "spfp2" else 4096
+        x = torch.randn(2, ic).bfloat16().cuda()
+        ys = [ops().linear(fmt, wt, None, x, 2560, ic, out_dtype=torch.float32, tiled=True) for _ in range(3)]
+        assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2]), fmt
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_batch_independent_ops(M):
+    """One launch over the projections of a config-2 layer (all formats), each
+    op against its own fp64 reference."""
+    specs = [("fp3", 12288, 2560), ("nvfp4", 2560, 4096), ("spfp2", 19456, 2560), ("spfp2", 2560, 9728)]
+    g = torch.Generator().manual_seed(20 + M)
+    batch, refs = [], []
+    for i, (fmt, oc, ic) in enumerate(specs):
+        wq, s, wt, dec = make(fmt, oc, ic, seed=100 + i)
+        x = torch.randn(M, ic, generator=g).bfloat16().cuda()
+        y = torch.empty(M, oc, dtype=torch.float32, device="cuda")
+        batch.append(ops().BatchOp(fmt, wt, x, y))
+        refs.append(ref(x, dec))
+    ops().linear_batch(batch)
+    torch.cuda.synchronize()
+    for op, y64 in zip(batch, refs):
+        assert np.abs(op.y.cpu().numpy() - y64).max() <= TOL
+    ops().check_device_errors()
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_batch_dependent_chain(M):
+    """gate|up (SiLU epilogue) -> down -> a second layer, each op reading the
+    previous op's bf16 output; checked against the same sequence of separate
+    spark_linear calls (identical kernels, identical results)."""
+    H, I = 1024, 2048
+    g = torch.Generator().manual_seed(30 + M)
+    gate = (torch.randn(I, H, generator=g) * 0.02).cuda()
+    up = (torch.randn(I, H, generator=g) * 0.02).cuda()
+    down = (torch.randn(H, I, generator=g) * 0.02).cuda()
+    w2 = (torch.randn(H, H, generator=g) * 0.02).cuda()
+    from spark_b200.inference_v3 import V3GateUpSiLU, V3PackedLinear
+    gu = V3GateUpSiLU(V3PackedLinear("spfp2", ops().spfp2_pack(gate)[0], I, H),
+                      V3PackedLinear("spfp2", ops().spfp2_pack(up)[0], I, H))
+    dn = V3PackedLinear("spfp2", ops().spfp2_pack(down)[0], H, I)
+    c2, s2 = ops().nvfp4_pack(w2)
+    l2 = V3PackedLinear("nvfp4", c2, H, H, scales=s2)
+    x = torch.randn(M, H, generator=g).bfloat16().cuda()
+    h = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(M, H, dtype=torch.bfloat16, device="cuda")
+    z = torch.empty(M, H, dtype=torch.float32, device="cuda")
+    batch = [ops().BatchOp("spfp2", gu.merged.w_tiled, x, h, silu=True),
+             ops().BatchOp("spfp2", dn.w_tiled, h, y, deps=[0]),
+             ops().BatchOp("nvfp4", l2.w_tiled, y, z, deps=[1])]
+    for _ in range(2):                      # a repeated launch reuses the control block
+        ops().linear_batch(batch)
+    torch.cuda.synchronize()
+    h_ref = gu(x)
+    y_ref = dn(h_ref)
+    z_ref = ops().linear("nvfp4", l2.w_tiled, None, y_ref, H, H, out_dtype=torch.float32, tiled=True)
+    assert torch.equal(h, h_ref)
+    assert torch.equal(y, y_ref)
+    assert torch.equal(z, z_ref)
+    ops().check_device_errors()
+
+
+def test_batch_rejects_bad_ops():
+    from spark_b200._lib import SparkError
+    wq, s, wt, dec = make("spfp2", 256, 512, seed=40)
+    x = torch.randn(1, 512).bfloat16().cuda()
+    y = torch.empty(1, 256, dtype=torch.float32, device="cuda")
+    with pytest.raises(SparkError, match="dep"):
+        ops().linear_batch([ops().BatchOp("spfp2", wt, x, y, deps=[0])])
+    with pytest.raises(TypeError):
+        ops().linear_batch([ops().BatchOp("spfp2", wt, x.float(), y)])
+    xm = torch.randn(17, 512).bfloat16().cuda()
+    ym = torch.empty(17, 256, dtype=torch.float32, device="cuda")
+    with pytest.raises(SparkError, match="M must be"):
+        ops().linear_batch([ops().BatchOp("spfp2", wt, xm, ym)])
