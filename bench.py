@@ -68,10 +68,11 @@ CONFIG = {
     "layers_per_step": LAYERS,
     "l2": "weights rotate over 8 distinct layer copies (344 MB) > 126 MB L2",
     "graph": "each step replayed as one CUDA graph",
-    "projections": "q|k|v and gate|up row-merged into one packed weight each (V3MergedLinear): 4 GEMV "
-                   "launches per layer; per_projection repeats the step with one launch per linear",
-    "prefetch": "each GEMV requests the next launch's weight into L2 while it runs (chain_prefetch); every "
-                "weight is still read from HBM once per step",
+    "projections": "q|k|v and gate|up row-merged into one packed weight each (V3MergedLinear): 32 linears per "
+                   "step, all in ONE spark_linear_batch launch; per_launch repeats the step with one launch per "
+                   "linear, per_projection with one launch per unmerged projection (56)",
+    "dependencies": "none: each linear reads its layer-copy's fixed activation, as the metric's GEMVs are "
+                    "independent; spark_linear_batch also takes ops that read earlier ops' outputs",
 }
 METRIC = "dequant-GEMV HBM GB/s (% of 8 TB/s) at M=1; prefill dequant-GEMM TFLOP/s"
 PREFILL_M = 2048               # prefill tokens through one layer's 7 linears
@@ -268,26 +269,47 @@ def run_gpu(args, rank, world, local):
     ops.workspace(device, max_ws, stream=stream)
 
     def step(only=None, which=None):
-        # every decode GEMV pulls the next launch's weight into L2 (the last
-        # one the first's: the next token starts over)
+        # one spark_linear launch per linear; every decode GEMV pulls the next
+        # launch's weight into L2 (the last one the first's: the next token
+        # starts over)
         seq = [((name, id(L)), fmt, oc, ic, wt) for L in (which or merged) for name, (fmt, _, _, oc, ic, wt)
                in L.items() if not only or fmt == only]
         for k, (key, fmt, oc, ic, wt) in enumerate(seq):
             nxt = seq[(k + 1) % len(seq)][4]
             outs[key] = ops.linear(fmt, wt, None, x[ic], oc, ic, out=outs.get(key), tiled=True, prefetch=nxt)
 
+    def make_batch(xs, only=None):
+        """The step's row-merged linears as ONE spark_linear_batch launch."""
+        ys = {}
+        batch = []
+        for L in merged:
+            for name, (fmt, _, _, oc, ic, wt) in L.items():
+                if only and fmt != only:
+                    continue
+                y = torch.empty(xs[ic].shape[0], oc, dtype=torch.bfloat16, device=device)
+                ys[(name, id(L))] = y
+                batch.append(ops.BatchOp(fmt, wt, xs[ic], y))
+        return batch, ys
+
+    batch_all, _ = make_batch(x)
+    batch_spfp2, _ = make_batch(x, "spfp2")
+
     # warm every path once eagerly (allocates outputs), then capture
     with torch.cuda.stream(stream):
         for _ in range(2):
+            ops.linear_batch(batch_all)
+            ops.linear_batch(batch_spfp2)
             step()
-            step("spfp2")
             step(which=layers)
     torch.cuda.synchronize()
-    graph, graph_spfp2, graph_pp = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    graph, graph_spfp2, graph_pl, graph_pp = (torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(),
+                                              torch.cuda.CUDAGraph())
     with torch.cuda.graph(graph, stream=stream):
-        step()
+        ops.linear_batch(batch_all)
     with torch.cuda.graph(graph_spfp2, stream=stream):
-        step("spfp2")
+        ops.linear_batch(batch_spfp2)
+    with torch.cuda.graph(graph_pl, stream=stream):
+        step()
     with torch.cuda.graph(graph_pp, stream=stream):
         step(which=layers)
     torch.cuda.synchronize()
@@ -317,29 +339,24 @@ def run_gpu(args, rank, world, local):
     clk.__enter__()
     ms_total = timed(graph, args.steps)
     ms_spfp2 = timed(graph_spfp2, args.steps)
+    ms_pl = timed(graph_pl, args.steps)
     ms_pp = timed(graph_pp, args.steps)
     ops.check_device_errors()
 
-    # config 2 also names 4 and 16 tokens: the merged step at those M (the
-    # decode GEMV serves up to 16 tokens per launch), bytes counted as above
+    # config 2 also names 4 and 16 tokens: the batched step at those M (the
+    # decode kernel serves up to 16 tokens per launch), bytes counted as above
     decode_tokens = {}
     for m_tok in (4, 16):
         xm = {ic: torch.randn(m_tok, ic, device=device, generator=g).bfloat16() for ic in x}
-        om = {}
-
-        def step_m():
-            seq = [((name, id(L)), fmt, oc, ic, wt) for L in merged for name, (fmt, _, _, oc, ic, wt) in L.items()]
-            for k, (key, fmt, oc, ic, wt) in enumerate(seq):
-                om[key] = ops.linear(fmt, wt, None, xm[ic], oc, ic, out=om.get(key), tiled=True,
-                                     prefetch=seq[(k + 1) % len(seq)][4])
+        batch_m, _ = make_batch(xm)
 
         with torch.cuda.stream(stream):
-            step_m()
-            step_m()
+            ops.linear_batch(batch_m)
+            ops.linear_batch(batch_m)
         torch.cuda.synchronize()
         gm = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gm, stream=stream):
-            step_m()
+            ops.linear_batch(batch_m)
         k_m = max(5, args.steps // 5)
         ms_m = timed(gm, k_m)
         bytes_m = LAYERS * sum(linear_bytes(f, oc, ic, M=m_tok) for _, f, oc, ic in SHAPES)
@@ -350,7 +367,7 @@ def run_gpu(args, rank, world, local):
     ops.check_device_errors()
 
     # ---------------- e2e through the public layer API with host buffers
-    from spark_b200.inference_v3 import V3MergedLinear, V3PackedLinear, chain_prefetch
+    from spark_b200.inference_v3 import V3LinearBatch, V3MergedLinear, V3PackedLinear, chain_prefetch
     mods = []
     for L in layers:
         lin = {name: V3PackedLinear.from_packed(fmt, wq, s, oc, ic) for name, (fmt, wq, s, oc, ic, _) in L.items()}
@@ -372,12 +389,14 @@ def run_gpu(args, rank, world, local):
     h2d = sum(t.numel() * 2 for t in xh.values())
     d2h = yhost.numel() * 2
 
+    # the step's layers as one V3LinearBatch call (one launch)
+    order = [(L, gname) for L in mods for gname, _, _ in GROUPS]
+    step_layers = V3LinearBatch([L[gname] for L, gname in order])
+    step_outs = [yslot[(gname, id(L))] for L, gname in order]
+
     def e2e_step():
         xd = {ic: xh[ic].to(device, non_blocking=True) for ic in xh}
-        for L in mods:
-            for gname, _, _ in GROUPS:
-                m = L[gname]
-                m(xd[m.in_features], out=yslot[(gname, id(L))])
+        step_layers([xd[L[gname].in_features] for L, gname in order], step_outs)
         yhost.copy_(ydev, non_blocking=True)
 
     def time_e2e(run, k):
@@ -439,7 +458,7 @@ def run_gpu(args, rank, world, local):
     pre_steps = max(50, args.steps // 10)
     ms_pre = timed(graph_pre, pre_steps)
     ops.check_device_errors()
-    del graph_pre, graph, graph_spfp2, graph_pp
+    del graph_pre, graph, graph_spfp2, graph_pl, graph_pp
 
     # ---------------- BASELINE config 4, tensor-parallel over the ranks of this run
     tp = tp_mlp_measure(args, rank, world, local)
@@ -453,9 +472,11 @@ def run_gpu(args, rank, world, local):
     spfp2_gbs = SPFP2_BYTES * args.steps / (ms_spfp2 * 1e-3) / 1e9
     e2e_gbs = world * STEP_BYTES * args.steps / (ms_e2e * 1e-3) / 1e9
     e2e_eager_gbs = world * STEP_BYTES * args.steps / (ms_e2e_eager * 1e-3) / 1e9
-    # bf16 x on the tiled weights: one GEMV launch per linear, every format
-    launches = args.steps * LAYERS * len(GROUPS)
+    # one batched launch per step; per_launch: one launch per row-merged linear
+    launches = args.steps
+    launches_pl = args.steps * LAYERS * len(GROUPS)
     launches_pp = args.steps * LAYERS * len(SHAPES)
+    value_pl = world * STEP_BYTES * args.steps / (ms_pl * 1e-3) / 1e9
     value_pp = world * STEP_BYTES * args.steps / (ms_pp * 1e-3) / 1e9
     traffic = load_traffic()
     line = {
@@ -465,18 +486,25 @@ def run_gpu(args, rank, world, local):
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) bf16 activations)",
         "config": {**CONFIG, "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "hbm_frac": round(value / world / peak, 4),
-        "roofline": {"bound": "hbm", "kernel": "k_gemv_tiled<SPFP2>, gate|up [19456,2560] and down [2560,9728] at M=1",
-                     "achieved": round(spfp2_gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(spfp2_gbs / peak, 4), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
+        "roofline": {"bound": "hbm", "kernel": "k_stream (spark_linear_batch): the step's 32 row-merged linears "
+                                               "(FP3 q|k|v, NVFP4 out, SPFP2 gate|up and down x 8 layers) in one launch",
+                     "achieved": round(value / world, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(value / world / peak, 4), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
                      if peak_kind == "measured" else "fallback 6650 GB/s",
-                     "traffic": traffic, "bytes_per_launch": round(SPFP2_BYTES / (LAYERS * 2))},
+                     "traffic": traffic, "bytes_per_launch": STEP_BYTES},
         "gpu_launches": launches,
+        "spfp2_only": {"value": round(spfp2_gbs, 1), "unit": "GB/s", "frac": round(spfp2_gbs / peak, 4),
+                       "ms_per_step": round(ms_spfp2 / args.steps, 4),
+                       "note": "the 16 SPFP2 linears (gate|up, down) of the step in one launch"},
+        "per_launch": {"value": round(value_pl, 1), "unit": "GB/s", "ms_per_step": round(ms_pl / args.steps, 4),
+                       "gpu_launches": launches_pl,
+                       "note": "the same 32 linears as separate spark_linear launches (graph-replayed)"},
         "per_projection": {"value": round(value_pp, 1), "unit": "GB/s", "ms_per_step": round(ms_pp / args.steps, 4),
                            "gpu_launches": launches_pp},
         "decode_tokens": decode_tokens,
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "spark_b200.inference_v3.V3MergedLinear / V3PackedLinear called per step with its pinned "
-                       "host<->device copies", "mode": e2e_mode,
+                "api": "spark_b200.inference_v3.V3LinearBatch over the step's V3MergedLinear / V3PackedLinear layers, "
+                       "called per step with its pinned host<->device copies", "mode": e2e_mode,
                 "eager": {"value": round(e2e_eager_gbs, 1), "unit": "GB/s",
                           "note": "the same calls dispatched from Python every step"}},
         "clocks": clk.summary(),

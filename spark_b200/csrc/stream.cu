@@ -51,11 +51,11 @@
 namespace spark {
 namespace stream {
 
-constexpr int kCW = 16;                       // consumer warps
+constexpr int kCW = 14;                       // consumer warps (16 warps in all: 128 registers a thread)
 constexpr int kProdWarp = kCW;                // producer (lane 0 issues the copies)
 constexpr int kPrepWarp = kCW + 1;            // activation preparation
 constexpr int kThreads = (kCW + 2) * 32;
-constexpr int kStages = 5;
+constexpr int kStages = 6;
 constexpr int kSlotBytes = 2304;              // largest tiled unit (NVFP4)
 constexpr int kStageBytes = kCW * kSlotBytes;
 constexpr int kMaxOps = 48;
@@ -85,7 +85,8 @@ struct Op {
     int fmt, slot;           // slot >= 0: SPFP2 on the fp8 path (x prepared in that slot)
     int oc, n_kc, units, unit_bytes;
     int cnt_off, dep0, dep1, y_dtype;
-    int bias_dtype, silu, n_rg, pad;
+    int bias_dtype, silu, n_rg, q;       // q, rem: units per virtual warp (see "work split")
+    int rem, pad0, pad1, pad2;
 };
 
 struct Slot {
@@ -213,44 +214,19 @@ __device__ __forceinline__ bool wait_count(const int* p, int target, volatile in
 }
 
 // ---------------------------------------------------------------- work split
-// Op k's units go to CTAs in contiguous ranges (CTA order rotated by k), each
-// CTA's range to its consumer warps in contiguous sub-ranges (warp order
-// rotated by k), so the extra unit of an uneven split moves around.
-// v = cta' * kCW + warp' numbers the sub-ranges in unit order.
-__device__ __forceinline__ void cta_range(int U, int G, int cr, int& r0, int& n) {
-    r0 = (int)((int64_t)U * cr / G);
-    n = (int)((int64_t)U * (cr + 1) / G) - r0;
-}
-__device__ __forceinline__ void sub_range(int r0, int n, int wr, int& u0, int& u1) {
-    u0 = r0 + (int)((int64_t)n * wr / kCW);
-    u1 = r0 + (int)((int64_t)n * (wr + 1) / kCW);
-}
-// sub-range (virtual warp) holding unit u
-__device__ __forceinline__ int owner(int U, int G, int u) {
-    const int cr = (int)(((int64_t)(u + 1) * G - 1) / U);
-    int r0, n;
-    cta_range(U, G, cr, r0, n);
-    const int wr = (int)(((int64_t)(u - r0 + 1) * kCW - 1) / n);
-    return cr * kCW + wr;
-}
-__device__ __forceinline__ void unit_span(int U, int G, int v, int& u0, int& u1) {
-    int r0, n;
-    cta_range(U, G, v / kCW, r0, n);
-    sub_range(r0, n, v % kCW, u0, u1);
-}
-// Sub-ranges holding units [first, last], in unit order: the first is the
-// owner of `first`, each next one the owner of the unit after the previous
-// sub-range's end (sub-ranges may be empty when a CTA has fewer units than
-// warps; those hold nothing and are skipped).
-__device__ __forceinline__ int count_contributors(int U, int G, int first, int last) {
-    int n = 0, v = owner(U, G, first);
-    while (true) {
-        ++n;
-        int u0, u1;
-        unit_span(U, G, v, u0, u1);
-        if (u1 > last) return n;
-        v = owner(U, G, u1);
-    }
+// Op k's units are split evenly over T = G * kCW virtual warps in unit
+// order: virtual warp v holds q + (v < rem) units starting at
+// v * q + min(v, rem) (q = U / T, rem = U % T, computed on the host).  CTA c
+// runs virtual warps v = w' * G + c' (c' = (c + k) % G, w' = (w + k) % kCW for
+// its consumer warp w), so every CTA gets an equal share (at most one unit
+// apart) and the roles rotate from op to op.  Row-group contributors are then a
+// contiguous range of virtual warps: sub-ranges are empty only when q == 0,
+// and then only for v >= rem, after every non-empty one.
+__device__ __forceinline__ int vw_start(const Op& op, int v) { return v * op.q + min(v, op.rem); }
+__device__ __forceinline__ int vw_size(const Op& op, int v) { return op.q + (v < op.rem ? 1 : 0); }
+__device__ __forceinline__ int vw_owner(const Op& op, int u) {
+    const int big = op.rem * (op.q + 1);
+    return u < big ? u / (op.q + 1) : op.rem + (u - big) / op.q;
 }
 
 // ---------------------------------------------------------------- decoders
@@ -330,28 +306,36 @@ __device__ __forceinline__ void load_frag(const uint8_t* slot, int lane, uint32_
 }
 
 // ---------------------------------------------------------------- epilogue
-// Values of one row group for this thread: v[tok] for rows g (r = 0) and
-// g + 8 (r = 1); `have` marks the tokens this lane holds.
-template <int NTOK>
-struct RowVals {
-    float v[NTOK][2];
-    bool have[NTOK];
-};
+// A lane's values of one row group: v[idx][r] for rows g (r = 0) and g + 8
+// (r = 1).  fp8 path (F8): idx = n-tile j, token 2j + (t >> 1), held by the
+// lanes with even t; bf16 path: idx = 2j + i, token 8j + 2t + i.
+template <bool F8>
+__device__ __forceinline__ int val_token(int idx, int t) {
+    return F8 ? 2 * idx + (t >> 1) : 8 * (idx >> 1) + 2 * t + (idx & 1);
+}
 
 __device__ __forceinline__ float bias_at(const Op& op, int64_t row) {
     return op.bias ? load_as_float(op.bias, op.bias_dtype, row) : 0.0f;
 }
 
-template <int NTOK>
-__device__ __forceinline__ void write_rows(const Op& op, int M, int rg, const RowVals<NTOK>& R, const float* scale,
-                                           int g) {
+// per-token output scale: the fp8 path's power of two, 1 on the bf16 path
+__device__ __forceinline__ float tok_scale(const float4& sc, int m) {
+    return m == 0 ? sc.x : (m == 1 ? sc.y : (m == 2 ? sc.z : sc.w));
+}
+
+template <bool F8, int NV>
+__device__ __forceinline__ void write_rows(const Op& op, int M, int rg, const float (&v)[NV][2], const float4& sc,
+                                           int g, int t) {
+    if (F8 && (t & 1)) return;
     const int64_t r0 = (int64_t)rg * 16 + g, r1 = r0 + 8;
     if (op.silu) {
         const float bg = bias_at(op, r0), bu = bias_at(op, r1);
 #pragma unroll
-        for (int m = 0; m < NTOK; ++m) {
-            if (!R.have[m] || m >= M) continue;
-            const float gv = R.v[m][0] * scale[m] + bg, uv = R.v[m][1] * scale[m] + bu;
+        for (int idx = 0; idx < NV; ++idx) {
+            const int m = val_token<F8>(idx, t);
+            if (m >= M) continue;
+            const float s = F8 ? tok_scale(sc, m) : 1.0f;
+            const float gv = v[idx][0] * s + bg, uv = v[idx][1] * s + bu;
             store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + (int64_t)rg * 8 + g,
                              gv / (1.0f + __expf(-gv)) * uv);
         }
@@ -359,10 +343,12 @@ __device__ __forceinline__ void write_rows(const Op& op, int M, int rg, const Ro
     }
     const float b0 = r0 < op.oc ? bias_at(op, r0) : 0.0f, b1 = r1 < op.oc ? bias_at(op, r1) : 0.0f;
 #pragma unroll
-    for (int m = 0; m < NTOK; ++m) {
-        if (!R.have[m] || m >= M) continue;
-        if (r0 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r0, R.v[m][0] * scale[m] + b0);
-        if (r1 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r1, R.v[m][1] * scale[m] + b1);
+    for (int idx = 0; idx < NV; ++idx) {
+        const int m = val_token<F8>(idx, t);
+        if (m >= M) continue;
+        const float s = F8 ? tok_scale(sc, m) : 1.0f;
+        if (r0 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r0, v[idx][0] * s + b0);
+        if (r1 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r1, v[idx][1] * s + b1);
     }
 }
 
@@ -392,21 +378,20 @@ __device__ __forceinline__ int token_exp(unsigned maxbits) {
     return (int)((maxbits >> 23) & 0xffu) - 127 - 7;
 }
 
-// Flush the row-group segment [seg0, seg1) of op k held in R: write the rows
+// Flush the row-group segment [seg0, seg1) of op k held in v: write the rows
 // when the segment is the whole row group, else publish the partial; the
 // last contributor sums the partials in unit order and writes the rows.
-template <int NTOK>
-__device__ void flush(const Args& a, const Ctl& C, int k, int v, int rg, int seg0, int seg1, int u_first,
-                      RowVals<NTOK>& R, const float* scale, int lane) {
+template <bool F8, int NV>
+__device__ __noinline__ void flush(const Args& a, const Ctl& C, int k, int vw, int rg, int seg0, int seg1, int u_first,
+                                   const float (&v)[NV][2], float4 sc, int lane) {
     const Op& op = a.op[k];
-    const int g = lane >> 2;
+    const int g = lane >> 2, t = lane & 3;
     const int K = op.n_kc, M = a.M;
     if (seg0 == rg * K && seg1 == (rg + 1) * K) {
-        write_rows<NTOK>(op, M, rg, R, scale, g);
+        write_rows<F8, NV>(op, M, rg, v, sc, g, t);
         return;
     }
-    const int G = gridDim.x;
-    const int T = G * kCW;
+    const int T = gridDim.x * kCW;
     float* area = a.partials + (int64_t)(k % kPartRing) * a.part_stride;
     // areas are reused every kPartRing ops: the op that last used this one
     // must be finished (every warp past it, its partials read)
@@ -416,43 +401,43 @@ __device__ void flush(const Args& a, const Ctl& C, int k, int v, int rg, int seg
         if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
     }
     const int slot = (seg0 / K == u_first / K) ? 0 : 1;
-    float* mine = area + ((int64_t)v * 2 + slot) * M * 16;
+    float* mine = area + ((int64_t)vw * 2 + slot) * M * 16;
+    if (!(F8 && (t & 1))) {
 #pragma unroll
-    for (int m = 0; m < NTOK; ++m)
-        if (R.have[m] && m < M) {
-            __stcg(mine + m * 16 + g, R.v[m][0]);
-            __stcg(mine + m * 16 + g + 8, R.v[m][1]);
+        for (int idx = 0; idx < NV; ++idx) {
+            const int m = val_token<F8>(idx, t);
+            if (m < M) {
+                __stcg(mine + m * 16 + g, v[idx][0]);
+                __stcg(mine + m * 16 + g + 8, v[idx][1]);
+            }
         }
+    }
     __threadfence();
     __syncwarp();
-    const int first = rg * K, last = rg * K + K - 1;
-    const int n_contrib = count_contributors(op.units, G, first, last);
+    const int first = rg * K;
+    const int v_lo = vw_owner(op, first), v_hi = vw_owner(op, first + K - 1);
     int old = 0;
     if (lane == 0) old = atom_acq_rel_add(a.counters + op.cnt_off + rg, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != n_contrib - 1) return;
+    if (old != v_hi - v_lo) return;
     __threadfence();
-    // lane l sums row (l & 15) of tokens (l >> 4), (l >> 4) + 2, ...
+    // the first contributor holds this row group in its second slot when its
+    // sub-range began in an earlier row group
+    const bool lo_second = vw_start(op, v_lo) < first;
+    // lane l sums row (l & 15) of tokens (l >> 4) + 2i
     const int row = lane & 15;
     float sum[kMaxTok / 2];
 #pragma unroll
     for (int i = 0; i < kMaxTok / 2; ++i) sum[i] = 0.0f;
-    for (int w = owner(op.units, G, first), c = 0; c < n_contrib; ++c) {
-        int u0, u1;
-        unit_span(op.units, G, w, u0, u1);
-        // the first contributor holds this row group in its second slot when
-        // its sub-range began in an earlier row group
-        const int sl = (c == 0 && u0 < first) ? 1 : 0;
-        const float* src = area + ((int64_t)w * 2 + sl) * M * 16;
+    for (int w = v_lo; w <= v_hi; ++w) {
+        const float* src = area + ((int64_t)w * 2 + ((w == v_lo && lo_second) ? 1 : 0)) * M * 16;
 #pragma unroll
         for (int i = 0; i < kMaxTok / 2; ++i) {
             const int m = (lane >> 4) + 2 * i;
             if (m < M) sum[i] += __ldcg(src + m * 16 + row);
         }
-        if (c + 1 < n_contrib) w = owner(op.units, G, u1);
     }
     if (lane == 0) a.counters[op.cnt_off + rg] = 0;
-    // write: lane holds row (rg*16 + row) of tokens m = (lane >> 4) + 2i
     const int64_t r = (int64_t)rg * 16 + row;
     if (op.silu) {
         // rows 0-7 of the group are gate rows, 8-15 the matching up rows
@@ -465,7 +450,8 @@ __device__ void flush(const Args& a, const Ctl& C, int k, int v, int rg, int seg
             for (int i = 0; i < kMaxTok / 2; ++i) {
                 const int m = (lane >> 4) + 2 * i;
                 if (m >= M) continue;
-                const float gv = sum[i] * scale[m] + bg, uv = up[i] * scale[m] + bu;
+                const float s = F8 ? tok_scale(sc, m) : 1.0f;
+                const float gv = sum[i] * s + bg, uv = up[i] * s + bu;
                 store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + (int64_t)rg * 8 + row,
                                  gv / (1.0f + __expf(-gv)) * uv);
             }
@@ -477,7 +463,7 @@ __device__ void flush(const Args& a, const Ctl& C, int k, int v, int rg, int seg
 #pragma unroll
         for (int i = 0; i < kMaxTok / 2; ++i) {
             const int m = (lane >> 4) + 2 * i;
-            if (m < M) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r, sum[i] * scale[m] + b);
+            if (m < M) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r, sum[i] * (F8 ? tok_scale(sc, m) : 1.0f) + b);
         }
     }
 }
@@ -545,9 +531,8 @@ __device__ void producer(const Args& a, uint8_t* ring, uint64_t* full, uint64_t*
     bool stop = false;
     for (int k = 0; k < a.n_ops && !stop; ++k) {
         const Op& op = a.op[k];
-        int r0, n;
-        cta_range(op.units, G, (c + k) % G, r0, n);
-        const int S = (n + kCW - 1) / kCW;
+        const int cr = (c + k) % G;
+        const int S = op.q + (cr < op.rem ? 1 : 0);
         for (int s = 0; s < S; ++s, ++q) {
             const uint32_t st = q % kStages;
             if (!wait_phase(smem_u32(empty + st), ((q / kStages) & 1u) ^ 1u, s_abort, C.abort, C.err) || *C.abort) {
@@ -555,21 +540,20 @@ __device__ void producer(const Args& a, uint8_t* ring, uint64_t* full, uint64_t*
                 stop = true;
                 break;
             }
-            uint32_t bytes = 0;
+            // warps whose sub-range is one unit longer hold the last stage's units
+            int n_here = kCW;
+            if (s == op.q) {
+                n_here = 0;
 #pragma unroll 1
-            for (int w = 0; w < kCW; ++w) {
-                int u0, u1;
-                sub_range(r0, n, (w + k) % kCW, u0, u1);
-                if (s < u1 - u0) bytes += (uint32_t)op.unit_bytes;
+                for (int w = 0; w < kCW; ++w) n_here += ((w + k) % kCW) * G + cr < op.rem ? 1 : 0;
             }
             const uint32_t fb = smem_u32(full + st);
-            mbar_expect_tx(fb, bytes);
+            mbar_expect_tx(fb, (uint32_t)(n_here * op.unit_bytes));
 #pragma unroll 1
             for (int w = 0; w < kCW; ++w) {
-                int u0, u1;
-                sub_range(r0, n, (w + k) % kCW, u0, u1);
-                if (s >= u1 - u0) continue;
-                const uint8_t* src = op.w + (int64_t)(u0 + s) * op.unit_bytes;
+                const int v = ((w + k) % kCW) * G + cr;
+                if (s >= vw_size(op, v)) continue;
+                const uint8_t* src = op.w + (int64_t)(vw_start(op, v) + s) * op.unit_bytes;
                 const uint32_t dst = smem_u32(ring + st * kStageBytes + w * kSlotBytes);
                 asm volatile(
                     "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], "
@@ -700,18 +684,13 @@ __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uin
     bool dead = false;
     for (int k = 0; k < a.n_ops; ++k) {
         const Op& op = a.op[k];
-        const int cr = (c + k) % G, wr = (warp + k) % kCW;
-        int r0, n, u0, u1;
-        cta_range(op.units, G, cr, r0, n);
-        sub_range(r0, n, wr, u0, u1);
-        const int S = (n + kCW - 1) / kCW;
-        const int v = cr * kCW + wr;
-        const int mine = u1 - u0;
+        const int cr = (c + k) % G;
+        const int vw = ((warp + k) % kCW) * G + cr;
+        const int u0 = vw_start(op, vw), mine = vw_size(op, vw);
+        const int S = op.q + (cr < op.rem ? 1 : 0);
         // inputs: earlier ops this op reads, and the prepared fp8 activations
         bool f8 = false;
-        float scale[kMaxTok];
-#pragma unroll
-        for (int m = 0; m < kMaxTok; ++m) scale[m] = 1.0f;
+        float4 sc = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
         if (mine > 0 && !dead) {
             bool ok = true;
             if (lane == 0) {
@@ -722,14 +701,16 @@ __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uin
             dead = !__shfl_sync(0xffffffffu, ok ? 1 : 0, 0);
             if (!dead && op.slot >= 0 && __ldcg(C.slot_flag + op.slot) == 0) {
                 f8 = true;
+                float s4[kF8Tok];
 #pragma unroll
                 for (int m = 0; m < kF8Tok; ++m) {
                     const unsigned mb = m < M ? __ldcg(C.slot_max + op.slot * kF8Tok + m) : 0u;
-                    scale[m] = mb ? __uint_as_float((uint32_t)(127 + token_exp(mb)) << 23) : 1.0f;
+                    s4[m] = mb ? __uint_as_float((uint32_t)(127 + token_exp(mb)) << 23) : 1.0f;
                 }
+                sc = make_float4(s4[0], s4[1], s4[2], s4[3]);
             }
         }
-        const int rg_first = u0 / op.n_kc;
+        int kc = mine > 0 ? u0 % op.n_kc : 0, rg = mine > 0 ? u0 / op.n_kc : 0;
         int seg0 = u0;
         float accf[2][NTF][4];
         float accb[2][NTB][4];
@@ -744,22 +725,20 @@ __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uin
 #pragma unroll
                 for (int i = 0; i < 4; ++i) accb[h][j][i] = 0.0f;
         }
+        const uint8_t* parts_base = f8 ? a.parts + a.slot[op.slot].parts_off : nullptr;
         for (int s = 0; s < S; ++s, ++q) {
             const uint32_t st = q % kStages;
             const bool have = s < mine;
-            const int u = u0 + s;
-            const int kc = have ? u % op.n_kc : 0;
             // B operands of the fp8 path first: their loads overlap the stage wait
             uint2 bq[8][NTF];
             if (f8 && have) {
-                const uint8_t* pb = a.parts + a.slot[op.slot].parts_off + (int64_t)kc * 2048 * NTF;
+                const uint8_t* pb = parts_base + (int64_t)kc * 2048 * NTF + ((g * 4 + t) << 3);
 #pragma unroll
                 for (int ss = 0; ss < 8; ++ss)
 #pragma unroll
                     for (int j = 0; j < NTF; ++j)
-                        bq[ss][j] = (8 * j + g < kParts * M)
-                                        ? ldg_v2(pb + ((int64_t)(ss * 8 * NTF + 8 * j + g) * 4 + t) * 8)
-                                        : make_uint2(0u, 0u);
+                        bq[ss][j] = (8 * j + g < kParts * M) ? ldg_v2(pb + (ss * 8 * NTF + 8 * j) * 32)
+                                                             : make_uint2(0u, 0u);
             }
             if (!dead) {
                 const bool ok = __all_sync(0xffffffffu, wait_phase(smem_u32(full + st), (q / kStages) & 1u, s_abort,
@@ -792,43 +771,31 @@ __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uin
                 else if (op.fmt == SPARK_FMT_FP3) unit_bf16<SPARK_FMT_FP3, NTB>(fw, xr, xv, col, pair_fp3, scale_tab, accb);
                 else unit_bf16<SPARK_FMT_NVFP4, NTB>(fw, xr, xv, col, pair_nv, scale_tab, accb);
             }
-            if (kc == op.n_kc - 1 || u + 1 == u1) {
-                const int rg = u / op.n_kc;
+            const int u = u0 + s;
+            if (kc == op.n_kc - 1 || s + 1 == mine) {
                 if (f8) {
-                    RowVals<kF8Tok> R;
-#pragma unroll
-                    for (int m = 0; m < kF8Tok; ++m) R.have[m] = false;
                     // columns 8j + 2t, 8j + 2t + 1 hold parts 2(t & 1), 2(t & 1) + 1
                     // of token 2j + (t >> 1): scale by 2^-4p, add the lane pair
                     const float s0 = (t & 1) ? 1.0f / 256.0f : 1.0f, s1 = (t & 1) ? 1.0f / 4096.0f : 1.0f / 16.0f;
+                    float vals[NTF][2];
 #pragma unroll
                     for (int j = 0; j < NTF; ++j) {
                         float vg = (accf[0][j][0] + accf[1][j][0]) * s0 + (accf[0][j][1] + accf[1][j][1]) * s1;
                         float vh = (accf[0][j][2] + accf[1][j][2]) * s0 + (accf[0][j][3] + accf[1][j][3]) * s1;
-                        vg += __shfl_xor_sync(0xffffffffu, vg, 1);
-                        vh += __shfl_xor_sync(0xffffffffu, vh, 1);
-                        const int m = 2 * j + (t >> 1);
-                        if (!(t & 1) && m < kF8Tok) {
-                            R.v[m][0] = vg;
-                            R.v[m][1] = vh;
-                            R.have[m] = true;
-                        }
+                        vals[j][0] = vg + __shfl_xor_sync(0xffffffffu, vg, 1);
+                        vals[j][1] = vh + __shfl_xor_sync(0xffffffffu, vh, 1);
                     }
-                    flush<kF8Tok>(a, C, k, v, rg, seg0, u + 1, u0, R, scale, lane);
+                    flush<true, NTF>(a, C, k, vw, rg, seg0, u + 1, u0, vals, sc, lane);
                 } else {
-                    RowVals<8 * NTB> R;
-#pragma unroll
-                    for (int m = 0; m < 8 * NTB; ++m) R.have[m] = false;
+                    float vals[2 * NTB][2];
 #pragma unroll
                     for (int j = 0; j < NTB; ++j)
 #pragma unroll
                         for (int i = 0; i < 2; ++i) {
-                            const int m = 8 * j + 2 * t + i;
-                            R.v[m][0] = accb[0][j][i] + accb[1][j][i];
-                            R.v[m][1] = accb[0][j][2 + i] + accb[1][j][2 + i];
-                            R.have[m] = true;
+                            vals[2 * j + i][0] = accb[0][j][i] + accb[1][j][i];
+                            vals[2 * j + i][1] = accb[0][j][2 + i] + accb[1][j][2 + i];
                         }
-                    flush<8 * NTB>(a, C, k, v, rg, seg0, u + 1, u0, R, scale, lane);
+                    flush<false, 2 * NTB>(a, C, k, vw, rg, seg0, u + 1, u0, vals, sc, lane);
                 }
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
@@ -843,8 +810,11 @@ __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uin
                 }
                 seg0 = u + 1;
             }
+            if (++kc == op.n_kc) {
+                kc = 0;
+                ++rg;
+            }
         }
-        (void)rg_first;
         // this warp is done with op k (outputs and partial reads included)
         __syncwarp();
         if (lane == 0) {
@@ -1024,6 +994,8 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
         SPARK_REQUIRE(units < (1ll << 30) && o.oc < (1ll << 30), SPARK_ERR_UNSUPPORTED,
                       "spark_linear_batch: op %d too large", k);
         p.units = (int)units;
+        p.q = (int)(units / ((int64_t)G * kCW));
+        p.rem = (int)(units % ((int64_t)G * kCW));
         p.unit_bytes = unit_bytes_of(fmt);
         p.cnt_off = (int)cnt;
         cnt += p.n_rg;
