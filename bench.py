@@ -921,6 +921,35 @@ def run_qat(args):
                    "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)"}}), flush=True)
 
 
+def run_profile_step(args):
+    """The config-2 decode step (8 layer copies, 32 row-merged linears) as one
+    spark_linear_batch launch, replayed --steps times after 3 warm-up launches;
+    prints the step time and GB/s (the bench's headline step without the rest
+    of the bench around it, for ncu)."""
+    from spark_b200 import ops
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    merged = [merge_layer(L) for L in build_layers(device)]
+    g = torch.Generator(device=device).manual_seed(7)
+    x = {ic: torch.randn(args.M, ic, device=device, generator=g).bfloat16() for ic in (2560, 4096, 9728)}
+    batch = [ops.BatchOp(fmt, wt, x[ic], torch.empty(args.M, oc, dtype=torch.bfloat16, device=device))
+             for L in merged for (fmt, _, _, oc, ic, wt) in L.values()]
+    for _ in range(3):
+        ops.linear_batch(batch)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ops.linear_batch(batch)
+    e1.record()
+    torch.cuda.synchronize()
+    ops.check_device_errors()
+    ms = e0.elapsed_time(e1) / args.steps
+    step_bytes = LAYERS * sum(linear_bytes(f, oc, ic, M=args.M) for _, f, oc, ic in SHAPES)
+    print(json.dumps({"profile": "step", "M": args.M, "ms_per_step": round(ms, 4),
+                      "GBps": round(step_bytes / (ms * 1e-3) / 1e9, 1)}))
+
+
 def run_profile(args):
     """Timing of one linear shape on its own (also the target of ncu captures).
 
@@ -999,8 +1028,9 @@ def main():
     ap.add_argument("--impl", default="spark_b200", choices=["spark_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
-    ap.add_argument("--profile", choices=["spfp2", "fp3", "nvfp4", "twofour"],
-                    help="run a few plain launches of one linear (ncu captures)")
+    ap.add_argument("--profile", choices=["spfp2", "fp3", "nvfp4", "twofour", "step"],
+                    help="run a few plain launches of one linear, or 'step': the batched decode step alone "
+                         "(ncu captures)")
     ap.add_argument("--M", type=int, default=1)
     ap.add_argument("--path", default="tiled", choices=["tiled", "tc", "plain"],
                     help="profile mode: tiled-layout GEMV, tcgen05 kernel, or reference-layout GEMV")
@@ -1014,6 +1044,9 @@ def main():
     ap.add_argument("--oc", type=int, default=0, help="profile mode: output features")
     ap.add_argument("--ic", type=int, default=0, help="profile mode: input features")
     args = ap.parse_args()
+    if args.profile == "step":
+        run_profile_step(args)
+        return
     if args.profile:
         run_profile(args)
         return

@@ -8,31 +8,18 @@
 //   * a producer thread copies every op's weight units, op after op, into a
 //     5-stage shared-memory ring with bulk copies (evict-first in L2); an op
 //     boundary is only a different source address for the next stage;
-//   * 16 consumer warps each take one unit (16 rows x 256 columns) per stage,
-//     decode it in registers and feed mma.sync; a row group split between
-//     warps is summed deterministically (partials + counter, last arriver
-//     adds in unit order);
-//   * a preparation warp turns the activations of SPFP2 ops (up to 4 tokens)
-//     into the fp8 operands described below; ops may depend on earlier ops'
-//     outputs (device-side completion counters, bounded waits).
+//   * 15 consumer warps each take one unit (16 rows x 256 columns) per stage,
+//     decode it in registers and feed mma.sync (bf16, fp32 accumulation); a
+//     row group split between warps is summed deterministically (partials +
+//     counter, the last arriver adds them in unit order);
+//   * ops may read earlier ops' outputs: a consumer waits on device-side
+//     completion counters (bounded waits) before it reads such an input, while
+//     the op's weights are already streaming.
 //
-// SPFP2 on the fp8 tensor path (block_fp2_emu.py:36, :270-308).  A decoded
-// SPFP2 weight is +-2^(e-10), e in [0, 15], or 0: exact in e5m2 (exponent
-// field e + 5, no mantissa bits), so one byte permute of the block's table
-// [e5m2(+), e5m2(-), 0, 0] turns four 2-bit codes into four A-operand bytes
-// of mma.m16n8k32.e5m2.e4m3.  The activations are split per token into four
-// e4m3 parts, x = sigma * (p0 + p1/16 + p2/256 + p3/4096) with sigma a power
-// of two (max|x|/sigma in [128, 256)); each part is an N column of the MMA
-// (the columns a 1-token GEMV would waste), every product is exact, and the
-// epilogue adds the part columns with their powers of two.  Every bf16 value
-// x with |x| >= 2^-10 max|x| is represented exactly; smaller ones to within
-// 2^-24 max|x|, below the fp32 rounding of the accumulation.  Activations
-// with a non-finite value (or a max outside 2^+-100) take the bf16 path.
-//
-// bf16 path (FP3, NVFP4, and SPFP2 above 4 tokens): the decoded weights are
-// exact in bf16 (FP3 / e2m1 codes have <= 2 significant bits, e4m3 scales
-// <= 4, SPFP2 values are powers of two) and mma.m16n8k16.bf16 reads the
-// caller's x directly.
+// Every decoded weight is exact in bf16 (SPFP2 values are powers of two,
+// block_fp2_emu.py:36; FP3 / e2m1 codes have <= 2 significant bits and e4m3
+// scales <= 4, fp3_emu.py:47, nvfp4_emu.py:109-123), so mma.m16n8k16.bf16
+// reads the caller's bf16 x directly.
 //
 // Tiled layouts (spark_tile_weights): per unit, thread (g, t) of a warp owns
 // the 64-column chunk [64t, 64t + 64) of rows g and g + 8, stored as
@@ -51,30 +38,22 @@
 namespace spark {
 namespace stream {
 
-constexpr int kCW = 14;                       // consumer warps (16 warps in all: 128 registers a thread)
+constexpr int kCW = 15;                       // consumer warps
 constexpr int kProdWarp = kCW;                // producer (lane 0 issues the copies)
-constexpr int kPrepWarp = kCW + 1;            // activation preparation
-constexpr int kThreads = (kCW + 2) * 32;
-constexpr int kStages = 6;
+constexpr int kThreads = (kCW + 1) * 32;      // 16 warps: 128 registers a thread
+constexpr int kStages = 5;
 constexpr int kSlotBytes = 2304;              // largest tiled unit (NVFP4)
 constexpr int kStageBytes = kCW * kSlotBytes;
 constexpr int kMaxOps = 48;
-constexpr int kMaxSlots = 8;
 constexpr int kMaxTok = 16;
-constexpr int kF8Tok = 4;                     // tokens the fp8 path serves
-constexpr int kParts = 4;                     // e4m3 parts per token
-constexpr int kPartRing = 4;                  // partial-sum areas, reused every kPartRing ops
+constexpr size_t kPartAreaBudget = (size_t)16 << 20;   // partial-sum areas of a batch: one per op up to this
 constexpr uint64_t kWaitNs = 2000000000ull;   // bounded waits: 2 s
 
 // Control block inside the caller's workspace (bytes; the error word is at 0).
 constexpr size_t kCtlAbort = 4;
 constexpr size_t kCtlCtaDone = 8;
-constexpr size_t kCtlOpDone = 64;                                   // int[kMaxOps]
-constexpr size_t kCtlSlotCnt = kCtlOpDone + 4 * kMaxOps;            // int[kMaxSlots][2]
-constexpr size_t kCtlSlotFlag = kCtlSlotCnt + 8 * kMaxSlots;        // int[kMaxSlots]
-constexpr size_t kCtlSlotMax = kCtlSlotFlag + 4 * kMaxSlots;        // uint[kMaxSlots][kF8Tok]
-constexpr size_t kCtlEnd = kCtlSlotMax + 4 * kMaxSlots * kF8Tok;
-static_assert(kCtlEnd <= 4096, "control block overflows its 4 KB");
+constexpr size_t kCtlOpDone = 64;             // int[kMaxOps]
+static_assert(kCtlOpDone + 4 * kMaxOps <= 4096, "control block overflows its 4 KB");
 
 struct Op {
     const uint8_t* w;        // tiled weight
@@ -82,30 +61,20 @@ struct Op {
     void* y;
     const void* bias;
     int64_t ldx, ldy;
-    int fmt, slot;           // slot >= 0: SPFP2 on the fp8 path (x prepared in that slot)
-    int oc, n_kc, units, unit_bytes;
-    int cnt_off, dep0, dep1, y_dtype;
-    int bias_dtype, silu, n_rg, q;       // q, rem: units per virtual warp (see "work split")
-    int rem, pad0, pad1, pad2;
-};
-
-struct Slot {
-    const uint16_t* x;
-    int64_t ldx;
-    int64_t parts_off;       // bytes from Args::parts
-    int ic, dep0, dep1, pad;
+    int fmt, oc, n_kc, units;
+    int unit_bytes, cnt_off, dep0, dep1;
+    int y_dtype, bias_dtype, silu, n_rg;
+    int q, rem, waited, pad1;  // q, rem: units per virtual warp (see "work split"); waited: an op or a
+                               // partial-area reuse waits for this op's completion count
 };
 
 struct Args {
     Op op[kMaxOps];
-    Slot slot[kMaxSlots];
-    int n_ops, n_slots, M, ntf;   // ntf: n-tiles of the fp8 path (ceil(4 M / 8))
-    int n_cnt, pad2;              // row-group counters used by the batch
+    int n_ops, M, n_cnt, part_ring;  // part_ring: partial-sum areas, reused every part_ring ops
     uint8_t* ws;
     int* counters;
     float* partials;
-    int64_t part_stride;          // floats per ring area: T * 2 * M * 16
-    uint8_t* parts;
+    int64_t part_stride;     // floats per ring area: T * 2 * M * 16
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -121,13 +90,6 @@ __device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
     uint32_t d;
     asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
-}
-__device__ __forceinline__ void mma_f8(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                       uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.f32.e5m2.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
@@ -148,9 +110,9 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(20000u)
+        : "r"(bar), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -167,20 +129,19 @@ __device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
     asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
-__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+// activations that no op of the batch writes: read-only path; those that an
+// earlier op of the batch produced: L2 (coherent within the launch)
+__device__ __forceinline__ uint4 ld_x(const void* p, bool produced) {
     uint4 v;
-    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint2 ldg_v2(const void* p) {
-    uint2 v;
-    asm volatile("ld.global.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    if (produced)
+        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    else
+        asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
 
-// Bounded wait on a shared-memory barrier phase, all lanes of the warp.
-// False (and the abort flag raised) once kWaitNs pass, or when another warp
-// has raised the abort flag.
+// Bounded wait on a shared-memory barrier phase.  False (and the abort flags
+// raised) once kWaitNs pass, or when another warp has raised an abort flag.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* s_abort, volatile int* g_abort,
                                            int* err) {
     if (mbar_try(bar, parity)) return true;
@@ -202,7 +163,7 @@ __device__ __forceinline__ bool wait_count(const int* p, int target, volatile in
     if (ld_acquire(p) >= target) return true;
     const uint64_t dl = globaltimer_ns() + kWaitNs;
     while (true) {
-        __nanosleep(100);
+        __nanosleep(64);
         if (ld_acquire(p) >= target) return true;
         if (*abort) return false;
         if (globaltimer_ns() > dl) {
@@ -265,25 +226,18 @@ __device__ __forceinline__ void decode_scaled(const uint32_t* c, uint32_t scale_
     }
 }
 
-// SPFP2 stream layout, bf16 pairs of one row for block s: codes c0..c3 are the
-// nibbles of sA (low 16 bits), c4..c7 those of sB; e the block exponent.
-// bf16 of +-2^(e-10): biased exponent E = 117 + e, high byte sign | E >> 1,
-// low byte (E & 1) << 7.  Out: P[0..3] = column pairs (0,1) (2,3) (4,5) (6,7).
-__device__ __forceinline__ void decode_spfp2_bf16(uint32_t sA, uint32_t sB, uint32_t e, uint32_t* P) {
-    const uint32_t E = 117u + e;
-    const uint32_t TH = (E >> 1) * 0x101u + 0x8000u;     // [H, H | 0x80, 0, 0]
-    const uint32_t TL = (E & 1u) * 0x8080u;              // [L, L, 0, 0]
+// SPFP2, one row of block s: codes c0..c3 are the nibbles of sA (low 16
+// bits), c4..c7 those of sB; TH = [H, H | 0x80, 0, 0] and TL = [L, L, 0, 0]
+// are the byte tables of the block's exponent (bf16 of +-2^(e-10) has biased
+// exponent E = 117 + e: high byte sign | E >> 1, low byte (E & 1) << 7).
+// Out: P[0..3] = bf16 pairs of columns (0,1) (2,3) (4,5) (6,7).
+__device__ __forceinline__ void decode_spfp2_bf16(uint32_t sA, uint32_t sB, uint32_t TH, uint32_t TL, uint32_t* P) {
     const uint32_t hA = prmt(TH, 0u, sA), lA = prmt(TL, 0u, sA);
     const uint32_t hB = prmt(TH, 0u, sB), lB = prmt(TL, 0u, sB);
     P[0] = prmt(lA, hA, 0x5140u);
     P[1] = prmt(lA, hA, 0x7362u);
     P[2] = prmt(lB, hB, 0x5140u);
     P[3] = prmt(lB, hB, 0x7362u);
-}
-
-template <int FMT>
-__host__ __device__ constexpr int frag_words() {
-    return FMT == SPARK_FMT_SPFP2 ? 10 : (FMT == SPARK_FMT_FP3 ? 14 : 18);
 }
 
 // Words of this thread's fragment from a staged unit (lane-interleaved
@@ -305,207 +259,36 @@ __device__ __forceinline__ void load_frag(const uint8_t* slot, int lane, uint32_
     fw[4 * NV + 1] = q.y;
 }
 
-// ---------------------------------------------------------------- epilogue
-// A lane's values of one row group: v[idx][r] for rows g (r = 0) and g + 8
-// (r = 1).  fp8 path (F8): idx = n-tile j, token 2j + (t >> 1), held by the
-// lanes with even t; bf16 path: idx = 2j + i, token 8j + 2t + i.
-template <bool F8>
-__device__ __forceinline__ int val_token(int idx, int t) {
-    return F8 ? 2 * idx + (t >> 1) : 8 * (idx >> 1) + 2 * t + (idx & 1);
-}
-
-__device__ __forceinline__ float bias_at(const Op& op, int64_t row) {
-    return op.bias ? load_as_float(op.bias, op.bias_dtype, row) : 0.0f;
-}
-
-// per-token output scale: the fp8 path's power of two, 1 on the bf16 path
-__device__ __forceinline__ float tok_scale(const float4& sc, int m) {
-    return m == 0 ? sc.x : (m == 1 ? sc.y : (m == 2 ? sc.z : sc.w));
-}
-
-template <bool F8, int NV>
-__device__ __forceinline__ void write_rows(const Op& op, int M, int rg, const float (&v)[NV][2], const float4& sc,
-                                           int g, int t) {
-    if (F8 && (t & 1)) return;
-    const int64_t r0 = (int64_t)rg * 16 + g, r1 = r0 + 8;
-    if (op.silu) {
-        const float bg = bias_at(op, r0), bu = bias_at(op, r1);
-#pragma unroll
-        for (int idx = 0; idx < NV; ++idx) {
-            const int m = val_token<F8>(idx, t);
-            if (m >= M) continue;
-            const float s = F8 ? tok_scale(sc, m) : 1.0f;
-            const float gv = v[idx][0] * s + bg, uv = v[idx][1] * s + bu;
-            store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + (int64_t)rg * 8 + g,
-                             gv / (1.0f + __expf(-gv)) * uv);
-        }
-        return;
-    }
-    const float b0 = r0 < op.oc ? bias_at(op, r0) : 0.0f, b1 = r1 < op.oc ? bias_at(op, r1) : 0.0f;
-#pragma unroll
-    for (int idx = 0; idx < NV; ++idx) {
-        const int m = val_token<F8>(idx, t);
-        if (m >= M) continue;
-        const float s = F8 ? tok_scale(sc, m) : 1.0f;
-        if (r0 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r0, v[idx][0] * s + b0);
-        if (r1 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r1, v[idx][1] * s + b1);
-    }
-}
-
-// ---------------------------------------------------------------- consumer state
-struct Ctl {
-    int* err;
-    volatile int* abort;
-    int* op_done;
-    int* slot_cnt;
-    int* slot_flag;
-    unsigned* slot_max;
-};
-
-__device__ __forceinline__ Ctl ctl_of(uint8_t* ws) {
-    Ctl c;
-    c.err = reinterpret_cast<int*>(ws);
-    c.abort = reinterpret_cast<volatile int*>(ws + kCtlAbort);
-    c.op_done = reinterpret_cast<int*>(ws + kCtlOpDone);
-    c.slot_cnt = reinterpret_cast<int*>(ws + kCtlSlotCnt);
-    c.slot_flag = reinterpret_cast<int*>(ws + kCtlSlotFlag);
-    c.slot_max = reinterpret_cast<unsigned*>(ws + kCtlSlotMax);
-    return c;
-}
-
-// power-of-two scale sigma of a token: max|x| / sigma in [128, 256)
-__device__ __forceinline__ int token_exp(unsigned maxbits) {
-    return (int)((maxbits >> 23) & 0xffu) - 127 - 7;
-}
-
-// Flush the row-group segment [seg0, seg1) of op k held in v: write the rows
-// when the segment is the whole row group, else publish the partial; the
-// last contributor sums the partials in unit order and writes the rows.
-template <bool F8, int NV>
-__device__ __noinline__ void flush(const Args& a, const Ctl& C, int k, int vw, int rg, int seg0, int seg1, int u_first,
-                                   const float (&v)[NV][2], float4 sc, int lane) {
-    const Op& op = a.op[k];
-    const int g = lane >> 2, t = lane & 3;
-    const int K = op.n_kc, M = a.M;
-    if (seg0 == rg * K && seg1 == (rg + 1) * K) {
-        write_rows<F8, NV>(op, M, rg, v, sc, g, t);
-        return;
-    }
-    const int T = gridDim.x * kCW;
-    float* area = a.partials + (int64_t)(k % kPartRing) * a.part_stride;
-    // areas are reused every kPartRing ops: the op that last used this one
-    // must be finished (every warp past it, its partials read)
-    if (k >= kPartRing) {
-        bool ok = true;
-        if (lane == 0) ok = wait_count(C.op_done + (k - kPartRing), T, C.abort, C.err);
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
-    }
-    const int slot = (seg0 / K == u_first / K) ? 0 : 1;
-    float* mine = area + ((int64_t)vw * 2 + slot) * M * 16;
-    if (!(F8 && (t & 1))) {
-#pragma unroll
-        for (int idx = 0; idx < NV; ++idx) {
-            const int m = val_token<F8>(idx, t);
-            if (m < M) {
-                __stcg(mine + m * 16 + g, v[idx][0]);
-                __stcg(mine + m * 16 + g + 8, v[idx][1]);
-            }
-        }
-    }
-    __threadfence();
-    __syncwarp();
-    const int first = rg * K;
-    const int v_lo = vw_owner(op, first), v_hi = vw_owner(op, first + K - 1);
-    int old = 0;
-    if (lane == 0) old = atom_acq_rel_add(a.counters + op.cnt_off + rg, 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != v_hi - v_lo) return;
-    __threadfence();
-    // the first contributor holds this row group in its second slot when its
-    // sub-range began in an earlier row group
-    const bool lo_second = vw_start(op, v_lo) < first;
-    // lane l sums row (l & 15) of tokens (l >> 4) + 2i
-    const int row = lane & 15;
-    float sum[kMaxTok / 2];
-#pragma unroll
-    for (int i = 0; i < kMaxTok / 2; ++i) sum[i] = 0.0f;
-    for (int w = v_lo; w <= v_hi; ++w) {
-        const float* src = area + ((int64_t)w * 2 + ((w == v_lo && lo_second) ? 1 : 0)) * M * 16;
-#pragma unroll
-        for (int i = 0; i < kMaxTok / 2; ++i) {
-            const int m = (lane >> 4) + 2 * i;
-            if (m < M) sum[i] += __ldcg(src + m * 16 + row);
-        }
-    }
-    if (lane == 0) a.counters[op.cnt_off + rg] = 0;
-    const int64_t r = (int64_t)rg * 16 + row;
-    if (op.silu) {
-        // rows 0-7 of the group are gate rows, 8-15 the matching up rows
-        float up[kMaxTok / 2];
-#pragma unroll
-        for (int i = 0; i < kMaxTok / 2; ++i) up[i] = __shfl_down_sync(0xffffffffu, sum[i], 8);
-        if (row < 8) {
-            const float bg = bias_at(op, r), bu = bias_at(op, r + 8);
-#pragma unroll
-            for (int i = 0; i < kMaxTok / 2; ++i) {
-                const int m = (lane >> 4) + 2 * i;
-                if (m >= M) continue;
-                const float s = F8 ? tok_scale(sc, m) : 1.0f;
-                const float gv = sum[i] * s + bg, uv = up[i] * s + bu;
-                store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + (int64_t)rg * 8 + row,
-                                 gv / (1.0f + __expf(-gv)) * uv);
-            }
-        }
-        return;
-    }
-    if (r < op.oc) {
-        const float b = bias_at(op, r);
-#pragma unroll
-        for (int i = 0; i < kMaxTok / 2; ++i) {
-            const int m = (lane >> 4) + 2 * i;
-            if (m < M) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r, sum[i] * (F8 ? tok_scale(sc, m) : 1.0f) + b);
-        }
-    }
-}
-
-// ---------------------------------------------------------------- unit kernels
-// fp8 path: one SPFP2 unit (8 blocks per row, rows g and g + 8) into acc.
-template <int NTF>
-__device__ __forceinline__ void unit_spfp2_f8(const uint32_t* fw, const uint2 (&b)[8][NTF],
-                                              float (&acc)[2][NTF][4]) {
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-        const uint32_t E = fw[8 + (s >> 2)];
-        // e5m2 of +2^(e-10) is (e + 5) << 2: four blocks' bytes per word, and
-        // their negatives; one permute picks the block's [+, -, 0, 0] table
-        const uint32_t PL = (E & 0x0f0f0f0fu) * 4u + 0x14141414u;
-        const uint32_t PH = ((E >> 4) & 0x0f0f0f0fu) * 4u + 0x14141414u;
-        const uint32_t sel = 0x8800u | ((4u + (uint32_t)(s & 3)) << 4) | (uint32_t)(s & 3);
-        const uint32_t Tg = prmt(PL, PL | 0x80808080u, sel);
-        const uint32_t Th = prmt(PH, PH | 0x80808080u, sel);
-        const uint32_t W = fw[s];
-        const uint32_t x0 = W & 0x33333333u, x1 = (W >> 2) & 0x33333333u;
-        const uint32_t a0 = prmt(Tg, 0u, x0), a2 = prmt(Tg, 0u, x1);
-        const uint32_t a1 = prmt(Th, 0u, x0 >> 16), a3 = prmt(Th, 0u, x1 >> 16);
-#pragma unroll
-        for (int j = 0; j < NTF; ++j) mma_f8(acc[s & 1][j], a0, a1, a2, a3, b[s][j].x, b[s][j].y);
-    }
-}
-
-// bf16 path: one unit of any format; x rows read directly (16 bytes per step).
+// One unit of any format: 8 steps of 8 columns, rows g and g + 8, NTB token
+// tiles of 8; acc[0] / acc[1] take the two MMAs of a step.
 template <int FMT, int NTB>
-__device__ __forceinline__ void unit_bf16(const uint32_t* fw, const uint16_t* const (&xr)[NTB], const bool (&xv)[NTB],
-                                          int64_t col, const uint32_t* pair_tab, const uint32_t* scale_tab,
-                                          float (&acc)[2][NTB][4]) {
+__device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* const (&xr)[NTB], const bool (&xv)[NTB],
+                                         int64_t col, bool produced, const uint32_t* pair_tab,
+                                         const uint32_t* scale_tab, float (&acc)[2][NTB][4]) {
+    // one token tile: the unit's activations for all 8 steps are loaded first,
+    // so their latency overlaps the decode
+    uint4 xs[NTB == 1 ? 8 : 1];
+    if constexpr (NTB == 1) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s) xs[s] = xv[0] ? ld_x(xr[0] + col + 8 * s, produced) : make_uint4(0u, 0u, 0u, 0u);
+    }
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
         uint32_t A0[4], A1[4];
         if constexpr (FMT == SPARK_FMT_SPFP2) {
+            // exponent byte tables of four blocks at once, rows g (low
+            // nibbles) and g + 8 (high nibbles): bytes 117 + e, then H and L
+            const uint32_t E = fw[8 + (s >> 2)];
+            const uint32_t Yg = (E & 0x0f0f0f0fu) + 0x75757575u, Yh = ((E >> 4) & 0x0f0f0f0fu) + 0x75757575u;
+            const uint32_t Hg = (Yg >> 1) & 0x7f7f7f7fu, Lg = (Yg << 7) & 0x80808080u;
+            const uint32_t Hh = (Yh >> 1) & 0x7f7f7f7fu, Lh = (Yh << 7) & 0x80808080u;
+            const uint32_t k = (uint32_t)(s & 3);
+            const uint32_t selH = 0x8800u | ((4u + k) << 4) | k, selL = 0x4400u | (k << 4) | k;
             const uint32_t W = fw[s];
-            const uint32_t E = fw[8 + (s >> 2)] >> (8 * (s & 3));
-            const uint32_t sA = W & 0x3333u, sB = (W >> 2) & 0x3333u;
-            decode_spfp2_bf16(sA, sB, E & 0xfu, A0);
-            decode_spfp2_bf16((W >> 16) & 0x3333u, (W >> 18) & 0x3333u, (E >> 4) & 0xfu, A1);
+            decode_spfp2_bf16(W & 0x3333u, (W >> 2) & 0x3333u, prmt(Hg, Hg | 0x80808080u, selH), prmt(Lg, 0u, selL),
+                              A0);
+            decode_spfp2_bf16((W >> 16) & 0x3333u, (W >> 18) & 0x3333u, prmt(Hh, Hh | 0x80808080u, selH),
+                              prmt(Lh, 0u, selL), A1);
         } else {
             constexpr int CW = FMT == SPARK_FMT_FP3 ? 6 : 8;
             decode_scaled<FMT>(fw, fw[CW], s, pair_tab, scale_tab, A0);
@@ -514,11 +297,121 @@ __device__ __forceinline__ void unit_bf16(const uint32_t* fw, const uint16_t* co
 #pragma unroll
         for (int j = 0; j < NTB; ++j) {
             uint4 x = make_uint4(0u, 0u, 0u, 0u);
-            if (xv[j]) x = ldg_nc_v4(xr[j] + col + 8 * s);
+            if constexpr (NTB == 1) x = xs[s];
+            else if (xv[j]) x = ld_x(xr[j] + col + 8 * s, produced);
             mma_bf16(acc[0][j], A0[0], A1[0], A0[1], A1[1], x.x, x.y);
             mma_bf16(acc[1][j], A0[2], A1[2], A0[3], A1[3], x.z, x.w);
         }
     }
+}
+
+// ---------------------------------------------------------------- epilogue
+__device__ __forceinline__ float bias_at(const Op& op, int64_t row) {
+    return op.bias ? load_as_float(op.bias, op.bias_dtype, row) : 0.0f;
+}
+
+__device__ __forceinline__ float silu_mul(float gv, float uv) { return gv / (1.0f + __expf(-gv)) * uv; }
+
+struct Ctl {
+    int* err;
+    volatile int* abort;
+    int* op_done;
+};
+
+// Row-group segments of op k are held as v[2j + i][r] = row g (r = 0) / g + 8
+// (r = 1) of token 8j + 2t + i.  write_rows writes a whole row group;
+// flush_partial publishes the partial of a segment, and the last contributor
+// sums the partials in unit order and writes the rows.
+template <int NV>
+__device__ __forceinline__ void write_rows(const Op& op, int M, int rg, const float (&v)[NV][2], int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    {
+        const int64_t r0 = (int64_t)rg * 16 + g, r1 = r0 + 8;
+        const float b0 = r0 < op.oc ? bias_at(op, r0) : 0.0f, b1 = r1 < op.oc ? bias_at(op, r1) : 0.0f;
+#pragma unroll
+        for (int idx = 0; idx < NV; ++idx) {
+            const int m = 8 * (idx >> 1) + 2 * t + (idx & 1);
+            if (m >= M) continue;
+            if (op.silu) {
+                // rows g (gate) and g + 8 (its up row) -> column 8 rg + g
+                store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + (int64_t)rg * 8 + g,
+                                 silu_mul(v[idx][0] + b0, v[idx][1] + b1));
+                continue;
+            }
+            if (r0 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r0, v[idx][0] + b0);
+            if (r1 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r1, v[idx][1] + b1);
+        }
+    }
+}
+
+template <int NV>
+__device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int k, int vw, int rg, int slot,
+                                           const float (&v)[NV][2], int lane) {
+    const Op& op = a.op[k];
+    const int g = lane >> 2, t = lane & 3;
+    const int M = a.M;
+    float* area = a.partials + (int64_t)(k % a.part_ring) * a.part_stride;
+    // areas are reused every part_ring ops: the op that last used this one
+    // must be finished (every warp past it, its partials read)
+    if (k >= a.part_ring) {
+        bool ok = true;
+        if (lane == 0) ok = wait_count(C.op_done + (k - a.part_ring), gridDim.x * kCW, C.abort, C.err);
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
+    }
+    float* mine = area + ((int64_t)vw * 2 + slot) * M * 16;
+#pragma unroll
+    for (int idx = 0; idx < NV; ++idx) {
+        const int m = 8 * (idx >> 1) + 2 * t + (idx & 1);
+        if (m < M) {
+            __stcg(mine + m * 16 + g, v[idx][0]);
+            __stcg(mine + m * 16 + g + 8, v[idx][1]);
+        }
+    }
+    __syncwarp();
+    const int first = rg * op.n_kc;
+    const int v_lo = vw_owner(op, first), v_hi = vw_owner(op, first + op.n_kc - 1);
+    int old = 0;
+    if (lane == 0) {
+        __threadfence_block();
+        old = atom_acq_rel_add(a.counters + op.cnt_off + rg, 1);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != v_hi - v_lo) return;
+    // the first contributor holds this row group in its second slot when its
+    // sub-range began in an earlier row group
+    const int lo_slot = vw_start(op, v_lo) < first ? 1 : 0;
+    const int row = lane & 15;
+    const int64_t r = (int64_t)rg * 16 + row;
+    const float b = op.silu ? (row < 8 ? bias_at(op, r) : 0.0f) : (r < op.oc ? bias_at(op, r) : 0.0f);
+    const float bu = op.silu && row < 8 ? bias_at(op, r + 8) : 0.0f;
+    // lane l: row l & 15 of tokens (l >> 4) + 2i; partials of a batch of 4
+    // contributors are loaded before they are added (in unit order)
+    for (int i = 0; 2 * i < M; ++i) {
+        const int m = (lane >> 4) + 2 * i;
+        float sum = 0.0f;
+        if (m < M) {
+            for (int w0 = v_lo; w0 <= v_hi; w0 += 4) {
+                float p[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int w = w0 + j;
+                    p[j] = w <= v_hi ? __ldcg(area + ((int64_t)w * 2 + (w == v_lo ? lo_slot : 0)) * M * 16 + m * 16 + row)
+                                     : 0.0f;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sum += p[j];
+            }
+        }
+        if (op.silu) {
+            const float up = __shfl_down_sync(0xffffffffu, sum, 8);
+            if (m < M && row < 8)
+                store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + (int64_t)rg * 8 + row,
+                                 silu_mul(sum + b, up + bu));
+        } else if (m < M && r < op.oc) {
+            store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r, sum + b);
+        }
+    }
+    if (lane == 0) a.counters[op.cnt_off + rg] = 0;
 }
 
 // ---------------------------------------------------------------- roles
@@ -529,10 +422,22 @@ __device__ void producer(const Args& a, uint8_t* ring, uint64_t* full, uint64_t*
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
     uint32_t q = 0;
     bool stop = false;
+    const uint32_t ring0 = smem_u32(ring);
     for (int k = 0; k < a.n_ops && !stop; ++k) {
         const Op& op = a.op[k];
         const int cr = (c + k) % G;
         const int S = op.q + (cr < op.rem ? 1 : 0);
+        const uint32_t ub = (uint32_t)op.unit_bytes;
+        // per consumer warp: its first unit's address; warps with v < rem hold
+        // one unit more (the last stage's), the others q
+        const uint8_t* src[kCW];
+        int n_long = 0;
+#pragma unroll
+        for (int w = 0; w < kCW; ++w) {
+            const int v = ((w + k) % kCW) * G + cr;
+            src[w] = op.w + (int64_t)vw_start(op, v) * ub;
+            n_long += v < op.rem ? 1 : 0;
+        }
         for (int s = 0; s < S; ++s, ++q) {
             const uint32_t st = q % kStages;
             if (!wait_phase(smem_u32(empty + st), ((q / kStages) & 1u) ^ 1u, s_abort, C.abort, C.err) || *C.abort) {
@@ -540,25 +445,18 @@ __device__ void producer(const Args& a, uint8_t* ring, uint64_t* full, uint64_t*
                 stop = true;
                 break;
             }
-            // warps whose sub-range is one unit longer hold the last stage's units
-            int n_here = kCW;
-            if (s == op.q) {
-                n_here = 0;
-#pragma unroll 1
-                for (int w = 0; w < kCW; ++w) n_here += ((w + k) % kCW) * G + cr < op.rem ? 1 : 0;
-            }
+            const bool last = s == op.q;
             const uint32_t fb = smem_u32(full + st);
-            mbar_expect_tx(fb, (uint32_t)(n_here * op.unit_bytes));
-#pragma unroll 1
+            mbar_expect_tx(fb, (uint32_t)((last ? n_long : kCW) * op.unit_bytes));
+            const uint32_t dst0 = ring0 + st * kStageBytes;
+#pragma unroll
             for (int w = 0; w < kCW; ++w) {
-                const int v = ((w + k) % kCW) * G + cr;
-                if (s >= vw_size(op, v)) continue;
-                const uint8_t* src = op.w + (int64_t)(vw_start(op, v) + s) * op.unit_bytes;
-                const uint32_t dst = smem_u32(ring + st * kStageBytes + w * kSlotBytes);
+                // on the last stage only warps w' * G + c' < rem have a unit
+                if (last && ((w + k) % kCW) * G + cr >= op.rem) continue;
                 asm volatile(
                     "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], "
-                    "%2, [%3], %4;" ::"r"(dst),
-                    "l"(src), "r"((uint32_t)op.unit_bytes), "r"(fb), "l"(policy)
+                    "%2, [%3], %4;" ::"r"(dst0 + w * kSlotBytes),
+                    "l"(src[w] + (int64_t)s * ub), "r"(ub), "r"(fb), "l"(policy)
                     : "memory");
             }
         }
@@ -567,112 +465,14 @@ __device__ void producer(const Args& a, uint8_t* ring, uint64_t* full, uint64_t*
         // let the copies already issued land before the CTA retires
         const uint32_t lo = q > kStages ? q - kStages : 0;
         for (uint32_t p = lo; p < q; ++p) {
-            const uint32_t st = p % kStages;
             const uint64_t dl = globaltimer_ns() + kWaitNs;
-            while (!mbar_try(smem_u32(full + st), (p / kStages) & 1u) && globaltimer_ns() < dl) {
+            while (!mbar_try(smem_u32(full + p % kStages), (p / kStages) & 1u) && globaltimer_ns() < dl) {
             }
         }
     }
 }
 
-// Activation preparation for the fp8 path: per slot, every CTA takes a slice
-// of 8-column blocks; pass 1 publishes the per-token max |x|, pass 2 (after
-// all CTAs) writes the e4m3 parts in the order the consumers' B fragments
-// read them.
-__device__ void prepare(const Args& a, const Ctl& C, int lane) {
-    const int G = gridDim.x, c = blockIdx.x;
-    const int M = a.M;
-    for (int sl = 0; sl < a.n_slots; ++sl) {
-        const Slot& S = a.slot[sl];
-        bool ok = true;
-        if (lane == 0) {
-            if (S.dep0 >= 0) ok = wait_count(C.op_done + S.dep0, G * kCW, C.abort, C.err);
-            if (ok && S.dep1 >= 0) ok = wait_count(C.op_done + S.dep1, G * kCW, C.abort, C.err);
-        }
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
-        const int nb = S.ic / 8;
-        const int b0 = (int)((int64_t)nb * c / G), b1 = (int)((int64_t)nb * (c + 1) / G);
-        float mx[kF8Tok];
-        int bad = 0;
-#pragma unroll
-        for (int m = 0; m < kF8Tok; ++m) {
-            mx[m] = 0.0f;
-            if (m >= M) continue;
-            for (int b = b0 + lane; b < b1; b += 32) {
-                const uint4 q = *reinterpret_cast<const uint4*>(S.x + (int64_t)m * S.ldx + 8 * b);
-                const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float lo = fabsf(__uint_as_float(w4[i] << 16)), hi = fabsf(__uint_as_float(w4[i] & 0xffff0000u));
-                    bad |= !(lo <= 3.4028235e38f) | !(hi <= 3.4028235e38f);
-                    mx[m] = fmaxf(mx[m], fmaxf(lo, hi));
-                }
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], o));
-        }
-        bad = __any_sync(0xffffffffu, bad);
-        if (lane == 0) {
-            for (int m = 0; m < M && m < kF8Tok; ++m) atomicMax(C.slot_max + sl * kF8Tok + m, __float_as_uint(mx[m]));
-            if (bad) atomicOr(C.slot_flag + sl, 1);
-            __threadfence();
-            red_release_add(C.slot_cnt + 2 * sl, 1);
-            ok = wait_count(C.slot_cnt + 2 * sl, G, C.abort, C.err);
-        }
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
-        __threadfence();
-        int flag = __ldcg(C.slot_flag + sl);
-        float up[kF8Tok];
-#pragma unroll
-        for (int m = 0; m < kF8Tok; ++m) {
-            up[m] = 1.0f;
-            if (m >= M) continue;
-            const unsigned mb = __ldcg(C.slot_max + sl * kF8Tok + m);
-            if (mb == 0u) continue;                       // all zero: parts are zero for any scale
-            const int ex = token_exp(mb);
-            if (ex < -100 || ex > 100) flag = 1;          // (subnormal maxima included)
-            else up[m] = __uint_as_float((uint32_t)(127 - ex) << 23);
-        }
-        if (!flag) {
-            const int ntf = a.ntf;
-            uint8_t* parts = a.parts + S.parts_off;
-#pragma unroll 1
-            for (int m = 0; m < M && m < kF8Tok; ++m)
-                for (int b = b0 + lane; b < b1; b += 32) {
-                    const uint4 q = *reinterpret_cast<const uint4*>(S.x + (int64_t)m * S.ldx + 8 * b);
-                    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-                    float r[8];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        r[2 * i] = __uint_as_float(w4[i] << 16) * up[m];
-                        r[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u) * up[m];
-                    }
-                    // column 8b: unit kc, thread t of the chunk, block s within it
-                    const int col = 8 * b, kc = col >> 8, o = col & 255, t = o >> 6, s = (o & 63) >> 3;
-                    uint8_t* base = parts + (int64_t)kc * 2048 * ntf + (int64_t)s * 8 * ntf * 32 + t * 8;
-#pragma unroll
-                    for (int p = 0; p < kParts; ++p) {
-                        uint32_t lo = 0u, hi = 0u;
-                        const float sc = __uint_as_float((uint32_t)(127 + 4 * p) << 23);   // 2^(4p)
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const uint32_t e = f32_to_e4m3(r[i] * sc);
-                            r[i] -= e4m3_to_f32(e) / sc;           // exact: e has <= 4 bits of r's
-                            if (i < 4) lo |= e << (8 * i);
-                            else hi |= e << (8 * (i - 4));
-                        }
-                        const int n = kParts * m + p;
-                        *reinterpret_cast<uint2*>(base + (int64_t)n * 32) = make_uint2(lo, hi);
-                    }
-                }
-        }
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) red_release_add(C.slot_cnt + 2 * sl + 1, 1);
-    }
-}
-
-template <int NTF, int NTB>
+template <int NTB>
 __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uint64_t* empty, const Ctl& C,
                          volatile int* s_abort, const uint32_t* pair_fp3, const uint32_t* pair_nv,
                          const uint32_t* scale_tab, int warp, int lane) {
@@ -688,58 +488,36 @@ __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uin
         const int vw = ((warp + k) % kCW) * G + cr;
         const int u0 = vw_start(op, vw), mine = vw_size(op, vw);
         const int S = op.q + (cr < op.rem ? 1 : 0);
-        // inputs: earlier ops this op reads, and the prepared fp8 activations
-        bool f8 = false;
-        float4 sc = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-        if (mine > 0 && !dead) {
+        const bool produced = op.dep0 >= 0 || op.dep1 >= 0;
+        if (mine > 0 && !dead && produced) {
+            // earlier ops of the batch whose output this op reads
             bool ok = true;
             if (lane == 0) {
                 if (op.dep0 >= 0) ok = wait_count(C.op_done + op.dep0, T, C.abort, C.err);
                 if (ok && op.dep1 >= 0) ok = wait_count(C.op_done + op.dep1, T, C.abort, C.err);
-                if (ok && op.slot >= 0) ok = wait_count(C.slot_cnt + 2 * op.slot + 1, G, C.abort, C.err);
             }
             dead = !__shfl_sync(0xffffffffu, ok ? 1 : 0, 0);
-            if (!dead && op.slot >= 0 && __ldcg(C.slot_flag + op.slot) == 0) {
-                f8 = true;
-                float s4[kF8Tok];
-#pragma unroll
-                for (int m = 0; m < kF8Tok; ++m) {
-                    const unsigned mb = m < M ? __ldcg(C.slot_max + op.slot * kF8Tok + m) : 0u;
-                    s4[m] = mb ? __uint_as_float((uint32_t)(127 + token_exp(mb)) << 23) : 1.0f;
-                }
-                sc = make_float4(s4[0], s4[1], s4[2], s4[3]);
-            }
         }
         int kc = mine > 0 ? u0 % op.n_kc : 0, rg = mine > 0 ? u0 / op.n_kc : 0;
+        const int rg_first = rg;
         int seg0 = u0;
-        float accf[2][NTF][4];
-        float accb[2][NTB][4];
+        float acc[2][NTB][4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-#pragma unroll
-            for (int j = 0; j < NTF; ++j)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) accf[h][j][i] = 0.0f;
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int j = 0; j < NTB; ++j)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) accb[h][j][i] = 0.0f;
+                for (int i = 0; i < 4; ++i) acc[h][j][i] = 0.0f;
+        const uint16_t* xr[NTB];
+        bool xv[NTB];
+#pragma unroll
+        for (int j = 0; j < NTB; ++j) {
+            xv[j] = 8 * j + g < M;
+            xr[j] = op.x + (int64_t)(8 * j + g) * op.ldx;
         }
-        const uint8_t* parts_base = f8 ? a.parts + a.slot[op.slot].parts_off : nullptr;
         for (int s = 0; s < S; ++s, ++q) {
             const uint32_t st = q % kStages;
             const bool have = s < mine;
-            // B operands of the fp8 path first: their loads overlap the stage wait
-            uint2 bq[8][NTF];
-            if (f8 && have) {
-                const uint8_t* pb = parts_base + (int64_t)kc * 2048 * NTF + ((g * 4 + t) << 3);
-#pragma unroll
-                for (int ss = 0; ss < 8; ++ss)
-#pragma unroll
-                    for (int j = 0; j < NTF; ++j)
-                        bq[ss][j] = (8 * j + g < kParts * M) ? ldg_v2(pb + (ss * 8 * NTF + 8 * j) * 32)
-                                                             : make_uint2(0u, 0u);
-            }
             if (!dead) {
                 const bool ok = __all_sync(0xffffffffu, wait_phase(smem_u32(full + st), (q / kStages) & 1u, s_abort,
                                                                    C.abort, C.err));
@@ -756,58 +534,34 @@ __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uin
             if (lane == 0 && !dead) mbar_arrive(smem_u32(empty + st));
             if (!have || dead) continue;
 
-            if (f8) {
-                unit_spfp2_f8<NTF>(fw, bq, accf);
-            } else {
-                const uint16_t* xr[NTB];
-                bool xv[NTB];
-#pragma unroll
-                for (int j = 0; j < NTB; ++j) {
-                    xv[j] = 8 * j + g < M;
-                    xr[j] = op.x + (int64_t)(8 * j + g) * op.ldx;
-                }
-                const int64_t col = (int64_t)kc * 256 + t * 64;
-                if (op.fmt == SPARK_FMT_SPFP2) unit_bf16<SPARK_FMT_SPFP2, NTB>(fw, xr, xv, col, pair_fp3, scale_tab, accb);
-                else if (op.fmt == SPARK_FMT_FP3) unit_bf16<SPARK_FMT_FP3, NTB>(fw, xr, xv, col, pair_fp3, scale_tab, accb);
-                else unit_bf16<SPARK_FMT_NVFP4, NTB>(fw, xr, xv, col, pair_nv, scale_tab, accb);
-            }
+            const int64_t col = (int64_t)kc * 256 + t * 64;
+            if (op.fmt == SPARK_FMT_SPFP2)
+                unit_mma<SPARK_FMT_SPFP2, NTB>(fw, xr, xv, col, produced, pair_fp3, scale_tab, acc);
+            else if (op.fmt == SPARK_FMT_FP3)
+                unit_mma<SPARK_FMT_FP3, NTB>(fw, xr, xv, col, produced, pair_fp3, scale_tab, acc);
+            else
+                unit_mma<SPARK_FMT_NVFP4, NTB>(fw, xr, xv, col, produced, pair_nv, scale_tab, acc);
+
             const int u = u0 + s;
             if (kc == op.n_kc - 1 || s + 1 == mine) {
-                if (f8) {
-                    // columns 8j + 2t, 8j + 2t + 1 hold parts 2(t & 1), 2(t & 1) + 1
-                    // of token 2j + (t >> 1): scale by 2^-4p, add the lane pair
-                    const float s0 = (t & 1) ? 1.0f / 256.0f : 1.0f, s1 = (t & 1) ? 1.0f / 4096.0f : 1.0f / 16.0f;
-                    float vals[NTF][2];
+                float vals[2 * NTB][2];
 #pragma unroll
-                    for (int j = 0; j < NTF; ++j) {
-                        float vg = (accf[0][j][0] + accf[1][j][0]) * s0 + (accf[0][j][1] + accf[1][j][1]) * s1;
-                        float vh = (accf[0][j][2] + accf[1][j][2]) * s0 + (accf[0][j][3] + accf[1][j][3]) * s1;
-                        vals[j][0] = vg + __shfl_xor_sync(0xffffffffu, vg, 1);
-                        vals[j][1] = vh + __shfl_xor_sync(0xffffffffu, vh, 1);
+                for (int j = 0; j < NTB; ++j)
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        vals[2 * j + i][0] = acc[0][j][i] + acc[1][j][i];
+                        vals[2 * j + i][1] = acc[0][j][2 + i] + acc[1][j][2 + i];
                     }
-                    flush<true, NTF>(a, C, k, vw, rg, seg0, u + 1, u0, vals, sc, lane);
-                } else {
-                    float vals[2 * NTB][2];
+                if (seg0 == rg * op.n_kc && u + 1 == (rg + 1) * op.n_kc)
+                    write_rows<2 * NTB>(op, M, rg, vals, lane);
+                else
+                    flush_partial<2 * NTB>(a, C, k, vw, rg, rg == rg_first ? 0 : 1, vals, lane);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
                     for (int j = 0; j < NTB; ++j)
 #pragma unroll
-                        for (int i = 0; i < 2; ++i) {
-                            vals[2 * j + i][0] = accb[0][j][i] + accb[1][j][i];
-                            vals[2 * j + i][1] = accb[0][j][2 + i] + accb[1][j][2 + i];
-                        }
-                    flush<false, 2 * NTB>(a, C, k, vw, rg, seg0, u + 1, u0, vals, sc, lane);
-                }
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-#pragma unroll
-                    for (int j = 0; j < NTF; ++j)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) accf[h][j][i] = 0.0f;
-#pragma unroll
-                    for (int j = 0; j < NTB; ++j)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) accb[h][j][i] = 0.0f;
-                }
+                        for (int i = 0; i < 4; ++i) acc[h][j][i] = 0.0f;
                 seg0 = u + 1;
             }
             if (++kc == op.n_kc) {
@@ -815,16 +569,19 @@ __device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uin
                 ++rg;
             }
         }
-        // this warp is done with op k (outputs and partial reads included)
-        __syncwarp();
-        if (lane == 0) {
-            __threadfence();
-            red_release_add(C.op_done + k, 1);
+        // this warp is done with op k (outputs and partial reads included); the
+        // count is kept only for ops that something waits on
+        if (op.waited) {
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                red_release_add(C.op_done + k, 1);
+            }
         }
     }
 }
 
-template <int NTF, int NTB>
+template <int NTB>
 __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ Args a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem;
@@ -835,7 +592,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ 
     uint32_t* scale_tab = pair_nv + 256;
     __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const Ctl C = ctl_of(a.ws);
+    Ctl C;
+    C.err = reinterpret_cast<int*>(a.ws);
+    C.abort = reinterpret_cast<volatile int*>(a.ws + kCtlAbort);
+    C.op_done = reinterpret_cast<int*>(a.ws + kCtlOpDone);
     if (threadIdx.x == 0) {
         s_abort = 0;
         for (int i = 0; i < kStages; ++i) {
@@ -854,10 +614,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ 
     volatile int* sab = &s_abort;
     if (warp == kProdWarp) {
         if (lane == 0) producer(a, ring, full, empty, C, sab);
-    } else if (warp == kPrepWarp) {
-        prepare(a, C, lane);
     } else {
-        consumer<NTF, NTB>(a, ring, full, empty, C, sab, pair_fp3, pair_nv, scale_tab, warp, lane);
+        consumer<NTB>(a, ring, full, empty, C, sab, pair_fp3, pair_nv, scale_tab, warp, lane);
     }
     __syncthreads();
     // the last CTA out returns the control block to zero for the next launch
@@ -867,9 +625,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ 
         if (old == (int)gridDim.x - 1) {
             __threadfence();
             for (int k = 0; k < a.n_ops; ++k) C.op_done[k] = 0;
-            for (int i = 0; i < 2 * kMaxSlots; ++i) C.slot_cnt[i] = 0;
-            for (int i = 0; i < kMaxSlots; ++i) C.slot_flag[i] = 0;
-            for (int i = 0; i < kMaxSlots * kF8Tok; ++i) C.slot_max[i] = 0u;
             // an aborted launch can leave row-group counters raised
             if (*C.abort)
                 for (int i = 0; i < a.n_cnt; ++i) a.counters[i] = 0;
@@ -881,6 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ 
 }
 
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 2 * kStages * 8 + (64 + 256 + 256) * 4;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory above the per-CTA limit");
 
 int sm_count(int dev) {
     static int cache[64] = {};
@@ -891,7 +647,7 @@ int sm_count(int dev) {
 
 std::mutex g_mu;
 
-template <int NTF, int NTB>
+template <int NTB>
 int launch(const Args& a, int grid, cudaStream_t s) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -899,7 +655,7 @@ int launch(const Args& a, int grid, cudaStream_t s) {
         static bool done[64] = {};
         std::lock_guard<std::mutex> lk(g_mu);
         if (!done[dev]) {
-            cudaError_t e = cudaFuncSetAttribute(k_stream<NTF, NTB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaError_t e = cudaFuncSetAttribute(k_stream<NTB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)kSmemBytes);
             if (e != cudaSuccess) return set_error((int)e, "k_stream: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
             done[dev] = true;
@@ -915,7 +671,7 @@ int launch(const Args& a, int grid, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, k_stream<NTF, NTB>, a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_stream<NTB>, a);
     if (e != cudaSuccess) return set_error((int)e, "k_stream launch: %s", cudaGetErrorString(e));
     return SPARK_OK;
 }
@@ -925,7 +681,7 @@ int launch(const Args& a, int grid, cudaStream_t s) {
 // ---------------------------------------------------------------- host entry (used by gemv.cu)
 // Workspace layout shared with spark_linear: control block in [0, 4096), the
 // row-group counters at `counters_off` (int[max_counters], self-resetting),
-// then this kernel's partial sums and prepared activations from `scratch_off`.
+// then this kernel's partial sums from `scratch_off`.
 struct StreamPlan {
     stream::Args args;
     size_t scratch_bytes = 0;   // bytes needed from scratch_off
@@ -952,10 +708,7 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
     a = Args{};
     a.n_ops = n_ops;
     a.M = (int)M;
-    a.ntf = M <= 2 ? 1 : 2;
-    const bool f8 = M <= kF8Tok;
     int64_t cnt = 0;
-    int64_t parts_bytes = 0;
     for (int k = 0; k < n_ops; ++k) {
         const SparkChainOp& o = ops[k];
         SPARK_REQUIRE(o.kind == SPARK_CHAIN_LINEAR, SPARK_ERR_UNSUPPORTED,
@@ -1004,41 +757,26 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
         p.y_dtype = o.y_dtype;
         p.bias_dtype = o.bias ? o.bias_dtype : 0;
         p.silu = silu ? 1 : 0;
-        p.slot = -1;
-        if (fmt == SPARK_FMT_SPFP2 && f8) {
-            int sl = -1;
-            for (int j = 0; j < a.n_slots; ++j) {
-                const Slot& S = a.slot[j];
-                if (S.x == p.x && S.ldx == p.ldx && S.ic == (int)o.ic && S.dep0 == p.dep0 && S.dep1 == p.dep1) sl = j;
-            }
-            if (sl < 0 && a.n_slots < kMaxSlots) {
-                sl = a.n_slots++;
-                Slot& S = a.slot[sl];
-                S.x = p.x;
-                S.ldx = p.ldx;
-                S.ic = (int)o.ic;
-                S.dep0 = p.dep0;
-                S.dep1 = p.dep1;
-                S.parts_off = parts_bytes;
-                parts_bytes += (o.ic / 256) * 2048 * a.ntf;
-            }
-            p.slot = sl;     // -1 when the slots are used up: that op takes the bf16 path
-        }
     }
     a.n_cnt = (int)std::min<int64_t>(cnt, max_counters);
     SPARK_REQUIRE(cnt <= max_counters, SPARK_ERR_UNSUPPORTED,
                   "spark_linear_batch: %lld row groups in the batch, above %lld", (long long)cnt, (long long)max_counters);
     const int64_t T = (int64_t)G * kCW;
-    const int ring = n_ops < kPartRing ? n_ops : kPartRing;
     a.part_stride = T * 2 * M * 16;
-    const size_t part_bytes = (size_t)ring * a.part_stride * sizeof(float);
-    P->scratch_bytes = (part_bytes + 255) / 256 * 256 + (size_t)parts_bytes;
+    const size_t area = (size_t)a.part_stride * sizeof(float);
+    a.part_ring = (int)std::max<size_t>(1, std::min<size_t>((size_t)n_ops, kPartAreaBudget / area));
+    for (int k = 0; k < n_ops; ++k) {
+        Op& p = a.op[k];
+        if (k + a.part_ring < n_ops) p.waited = 1;
+        if (p.dep0 >= 0) a.op[p.dep0].waited = 1;
+        if (p.dep1 >= 0) a.op[p.dep1].waited = 1;
+    }
+    P->scratch_bytes = ((size_t)a.part_ring * area + 255) / 256 * 256;
     P->grid = G;
     a.ws = ws;
     if (ws) {
         a.counters = reinterpret_cast<int*>(ws + counters_off);
         a.partials = reinterpret_cast<float*>(ws + scratch_off);
-        a.parts = ws + scratch_off + (part_bytes + 255) / 256 * 256;
     }
     return SPARK_OK;
 }
@@ -1052,20 +790,17 @@ size_t stream_plan_scratch(const StreamPlan* P) { return P->scratch_bytes; }
 
 // scratch of a one-op batch (spark_linear on tiled weights, bf16 x)
 size_t stream_scratch_single(int64_t M, int64_t ic) {
+    (void)ic;
     int dev = 0;
     cudaGetDevice(&dev);
     const int64_t Mc = M < 1 ? 1 : (M > stream::kMaxTok ? stream::kMaxTok : M);
     const size_t part = (size_t)stream::sm_count(dev) * stream::kCW * 2 * Mc * 16 * sizeof(float);
-    const size_t parts = Mc <= stream::kF8Tok ? (size_t)(ic / 256) * 2048 * (Mc <= 2 ? 1 : 2) : 0;
-    return (part + 255) / 256 * 256 + parts;
+    return (part + 255) / 256 * 256;
 }
 
 int stream_launch(const StreamPlan& P, cudaStream_t s) {
     const stream::Args& a = P.args;
-    if (a.M <= 2) return stream::launch<1, 1>(a, P.grid, s);
-    if (a.M <= 4) return stream::launch<2, 1>(a, P.grid, s);
-    if (a.M <= 8) return stream::launch<1, 1>(a, P.grid, s);
-    return stream::launch<1, 2>(a, P.grid, s);
+    return a.M <= 8 ? stream::launch<1>(a, P.grid, s) : stream::launch<2>(a, P.grid, s);
 }
 
 }  // namespace spark
