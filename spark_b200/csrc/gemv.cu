@@ -748,6 +748,53 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv(const GemvArgs a) {
 }
 
 // ---------------------------------------------------------------- tiled layout
+// FP3 code words of one row's 64-column chunk.  Reference packing (six
+// words): code k at bit 3k (magnitude bits 0-1, sign bit 2, fp3_emu.py:107).
+// Tiled packing: two groups of three words; in group q, nibble i of word j
+// (j < 3) is code 32q + 8j + i as an e2m1 code (magnitude bits 0-1, sign bit
+// 3: FP3's magnitudes {0, .5, 1, 1.5} are e2m1's codes 0-3), and bit 2 of
+// nibble i of words 0, 1, 2 holds bit 0, 1, 2 of code 32q + 24 + i.
+__host__ __device__ inline uint32_t fp3_code(const uint32_t* ref, int k) {
+    const int b = 3 * k, w = b >> 5, o = b & 31;
+    uint32_t v = ref[w] >> o;
+    if (o > 29) v |= ref[w + 1] << (32 - o);
+    return v & 7u;
+}
+__host__ __device__ inline void fp3_pack_tiled(const uint32_t* ref, uint32_t* out) {
+    for (int q = 0; q < 2; ++q)
+        for (int j = 0; j < 3; ++j) {
+            uint32_t w = 0;
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t c = fp3_code(ref, 32 * q + 8 * j + i), x = fp3_code(ref, 32 * q + 24 + i);
+                w |= ((c & 3u) | ((x >> j) & 1u) << 2 | (c >> 2) << 3) << (4 * i);
+            }
+            out[3 * q + j] = w;
+        }
+}
+__device__ inline void fp3_unpack_tiled(const uint32_t* in, uint32_t* ref) {
+#pragma unroll
+    for (int w = 0; w < 6; ++w) ref[w] = 0u;
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t c;
+                if (j < 3) {
+                    const uint32_t n = in[3 * q + j] >> (4 * i);
+                    c = (n & 3u) | ((n >> 1) & 4u);
+                } else {
+                    c = ((in[3 * q] >> (4 * i + 2)) & 1u) | (((in[3 * q + 1] >> (4 * i + 2)) & 1u) << 1) |
+                        (((in[3 * q + 2] >> (4 * i + 2)) & 1u) << 2);
+                }
+                const int b = 3 * (32 * q + 8 * j + i);
+                ref[b >> 5] |= c << (b & 31);
+                if ((b & 31) > 29) ref[(b >> 5) + 1] |= c >> (32 - (b & 31));
+            }
+        }
+}
+
 // thread = (unit, lane): gather the lane's fragment words from the reference
 // layout and store them in fragment-major order
 template <int FMT>
@@ -785,11 +832,12 @@ __global__ void __launch_bounds__(256) k_tile(const uint8_t* __restrict__ wq, co
     }
     if constexpr (FMT == SPARK_FMT_SPFP2) {
         // Stream layout (the decoders of stream.cu): per 8-column block s of
-        // the chunk, word s = codes of row g (low half) | row g + 8 (high
-        // half), block column i at bits 4i and column 4 + i at bits 4i + 2;
-        // words 8-9: byte s % 4 of word 8 + s / 4 = e(row g) | e(row g + 8) << 4.
-        // The reference pair layout holds, per 16 columns, mantissa words
-        // m0, m1 (column j at bits 2j) and the exponent byte e0 | e1 << 4.
+        // the chunk, word s holds the 16 codes of rows g and g + 8 so that
+        // (word >> 2j) & 0x03030303 has, byte by byte, the codes of columns
+        // 2j and 2j + 1 of row g, then of row g + 8; words 8-9: byte s % 4 of
+        // word 8 + s / 4 = e(row g) | e(row g + 8) << 4.  The reference pair
+        // layout holds, per 16 columns, mantissa words m0, m1 (column j at
+        // bits 2j) and the exponent byte e0 | e1 << 4.
         const uint8_t* b = reinterpret_cast<const uint8_t*>(w);
         uint32_t out[10] = {};
 #pragma unroll
@@ -802,13 +850,20 @@ __global__ void __launch_bounds__(256) k_tile(const uint8_t* __restrict__ wq, co
                 const uint32_t e = h ? (q[4] >> 4) : (q[4] & 0xfu);
                 uint32_t p = 0;
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    p |= (((m >> (2 * i)) & 3u) << (4 * i)) | (((m >> (2 * (4 + i))) & 3u) << (4 * i + 2));
-                out[blk] |= p << (16 * half);
+                for (int i = 0; i < 8; ++i) p |= ((m >> (2 * i)) & 3u) << (2 * (i >> 1) + 8 * (i & 1) + 16 * half);
+                out[blk] |= p;
                 out[8 + (blk >> 2)] |= e << (8 * (blk & 3) + 4 * half);
             }
 #pragma unroll
         for (int i = 0; i < 10; ++i) w[i] = out[i];
+    }
+    if constexpr (FMT == SPARK_FMT_FP3) {
+        // per row: six code words re-packed for the e2m1 conversion, then the scale word
+        uint32_t out[6];
+        fp3_pack_tiled(w, out);
+        for (int i = 0; i < 6; ++i) w[i] = out[i];
+        fp3_pack_tiled(w + 7, out);
+        for (int i = 0; i < 6; ++i) w[7 + i] = out[i];
     }
     uint8_t* dst = tiled + u * unit_bytes_tiled<FMT>();
 #pragma unroll
@@ -976,6 +1031,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) k_gemv_tiled(const GemvArgs a)
 #pragma unroll
         for (int k = 0; k < FW; ++k) asm volatile("" ::"r"(fw[k]));
         issue(u0 + i + kDepthT, st);
+        if constexpr (FMT == SPARK_FMT_FP3) {
+            // tiled FP3 code words back to the reference packing
+            uint32_t ref[6];
+            fp3_unpack_tiled(fw, ref);
+#pragma unroll
+            for (int k = 0; k < 6; ++k) fw[k] = ref[k];
+            fp3_unpack_tiled(fw + 7, ref);
+#pragma unroll
+            for (int k = 0; k < 6; ++k) fw[7 + k] = ref[k];
+        }
 
         const uint32_t* c0 = fw;
         const uint32_t* c1 = fw + FW / 2;

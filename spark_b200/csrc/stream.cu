@@ -3,32 +3,43 @@
 //
 // y_k[M, oc_k] = x_k[M, ic_k] . decode(W_k)^T (+ bias_k) for every op k of a
 // batch, in ONE launch of one CTA per SM.  The work is HBM-bound at decode
-// batch sizes, so the design keeps the weight stream running from the first
-// op to the last:
-//   * a producer thread copies every op's weight units, op after op, into a
-//     5-stage shared-memory ring with bulk copies (evict-first in L2); an op
-//     boundary is only a different source address for the next stage;
-//   * 15 consumer warps each take one unit (16 rows x 256 columns) per stage,
-//     decode it in registers and feed mma.sync (bf16, fp32 accumulation); a
-//     row group split between warps is summed deterministically (partials +
-//     counter, the last arriver adds them in unit order);
-//   * ops may read earlier ops' outputs: a consumer waits on device-side
-//     completion counters (bounded waits) before it reads such an input, while
-//     the op's weights are already streaming.
+// batch sizes, so the design keeps every warp streaming weights from its
+// first unit to its last:
+//   * the batch's units (16 rows x 256 columns of one op) form one sequence,
+//     op after op, row group after row group, column chunk fastest; it is cut
+//     into G * kCW equal contiguous ranges, one per warp of the grid, so a warp
+//     sums whole row groups in registers and shares a row group with another
+//     warp only at the two ends of its range;
+//   * each warp feeds itself: lane 0 keeps kDepth bulk copies (evict-first in
+//     L2) of the warp's next units in flight into the warp's own shared-memory
+//     slots, so no warp ever waits for another one's progress;
+//   * the warp decodes a staged unit in registers and feeds mma.sync (bf16,
+//     fp32 accumulation); a row group shared between warps is summed
+//     deterministically (partials + counter, the last arriver adds them in
+//     unit order);
+//   * an op that reads an earlier op's output starts a new segment of the
+//     sequence (cut the same way): before it reads such an input a warp waits
+//     (bounded) until every warp has finished the producing segment, while its
+//     weights are already in flight.
 //
 // Every decoded weight is exact in bf16 (SPFP2 values are powers of two,
 // block_fp2_emu.py:36; FP3 / e2m1 codes have <= 2 significant bits and e4m3
 // scales <= 4, fp3_emu.py:47, nvfp4_emu.py:109-123), so mma.m16n8k16.bf16
 // reads the caller's bf16 x directly.
 //
-// Tiled layouts (spark_tile_weights): per unit, thread (g, t) of a warp owns
-// the 64-column chunk [64t, 64t + 64) of rows g and g + 8, stored as
-// lane-interleaved 16-byte vectors plus an 8-byte tail.  SPFP2: words 0-7
-// hold, per 8-column block s of the chunk, the 8 codes of row g (low half)
-// and row g + 8 (high half) with block column i at bits 4i and column 4 + i
-// at bits 4i + 2; words 8-9 hold the 16 block exponents, byte s % 4 of word
-// 8 + s / 4 = e(row g) | e(row g + 8) << 4.  FP3 / NVFP4: the reference
-// layout's code words of the chunk and its scale word, per row.
+// The main path runs every format on the f16 MMA: the decoded weights are
+// exact in f16 too (SPFP2: exponent field e + 5; FP3 / NVFP4 code values
+// times an e4m3 scale have at most 6 significant bits and lie within
+// [2^-10, 2688]), and f16 has single-instruction conversions from e5m2 and
+// e2m1 pairs: SPFP2 becomes e5m2 bytes by one byte permute per four weights,
+// FP3 (repacked at tile time) and NVFP4 are e2m1 codes.  The activations are
+// converted once per launch, per 256-column chunk and token, to f16 times a
+// power of two sigma (max |x| * sigma in [2^14, 2^15), so the conversion of a
+// bf16 value is exact down to max |x| * 2^-28); a unit's fresh accumulators
+// are scaled by 1 / sigma into the row sums.  The first warp to need a chunk
+// claims it (flag 0 -> 1), converts it and publishes it (2; 3 when it holds an
+// inf or NaN: the op then runs on the bf16 path, which keeps the
+// reference's inf / NaN pattern).
 #include <algorithm>
 #include <mutex>
 #include <new>
@@ -38,22 +49,21 @@
 namespace spark {
 namespace stream {
 
-constexpr int kCW = 15;                       // consumer warps
-constexpr int kProdWarp = kCW;                // producer (lane 0 issues the copies)
-constexpr int kThreads = (kCW + 1) * 32;      // 16 warps: 128 registers a thread
-constexpr int kStages = 5;
+constexpr int kCW = 16;                       // warps of a CTA; each streams its own units
+constexpr int kThreads = kCW * 32;            // 128 registers a thread
+constexpr int kDepth = 6;                     // units in flight per warp
 constexpr int kSlotBytes = 2304;              // largest tiled unit (NVFP4)
-constexpr int kStageBytes = kCW * kSlotBytes;
+constexpr int kWarpRing = kDepth * kSlotBytes;
 constexpr int kMaxOps = 48;
 constexpr int kMaxTok = 16;
-constexpr size_t kPartAreaBudget = (size_t)16 << 20;   // partial-sum areas of a batch: one per op up to this
+constexpr size_t kPartAreaBudget = (size_t)16 << 20;   // partial-sum areas of a batch: one per segment up to this
 constexpr uint64_t kWaitNs = 2000000000ull;   // bounded waits: 2 s
 
 // Control block inside the caller's workspace (bytes; the error word is at 0).
 constexpr size_t kCtlAbort = 4;
 constexpr size_t kCtlCtaDone = 8;
-constexpr size_t kCtlOpDone = 64;             // int[kMaxOps]
-static_assert(kCtlOpDone + 4 * kMaxOps <= 4096, "control block overflows its 4 KB");
+constexpr size_t kCtlSegDone = 64;            // int[kMaxOps]: warps done with each segment
+static_assert(kCtlSegDone + 4 * kMaxOps <= 4096, "control block overflows its 4 KB");
 
 struct Op {
     const uint8_t* w;        // tiled weight
@@ -61,21 +71,35 @@ struct Op {
     void* y;
     const void* bias;
     int64_t ldx, ldy;
-    int fmt, oc, n_kc, units;
-    int unit_bytes, cnt_off, dep0, dep1;
-    int y_dtype, bias_dtype, silu, n_rg;
-    int q, rem, waited, pad1;  // q, rem: units per virtual warp (see "work split"); waited: an op or a
-                               // partial-area reuse waits for this op's completion count
+    int fmt, oc, n_kc, ub;   // ub: the op's first unit in the batch's sequence
+    int units, unit_bytes, cnt_off, seg;
+    int dseg0, dseg1, y_dtype, bias_dtype;   // dseg: segments whose completion the op's input needs (-1: none)
+    int silu, f16, flag_off, chunk0;  // f16: the f16 path; flag_off: the op's chunk flags in the counters;
+                                      // chunk0: its first chunk in the batch's converted-activation arrays
+};
+
+// A segment: ops k0..k1-1, units [ub, ub + units) of the sequence, split over
+// T = G * kCW warps: warp v holds q + (v < rem) units from ub + v * q + min(v, rem).
+struct Seg {
+    int ub, units, q, rem;
+    int k0, k1, active, waited;   // active: warps with a non-empty range; waited: something waits for it
 };
 
 struct Args {
     Op op[kMaxOps];
-    int n_ops, M, n_cnt, part_ring;  // part_ring: partial-sum areas, reused every part_ring ops
+    Seg seg[kMaxOps];
+    int n_ops, n_seg, M, n_cnt;
+    int part_ring, n_cnt_all;  // part_ring: partial-sum areas, reused every part_ring segments;
+                               // n_cnt_all: counters including the chunk flags (reset at the end)
     uint8_t* ws;
     int* counters;
     float* partials;
-    int64_t part_stride;     // floats per ring area: T * 2 * M * 16
+    int64_t part_stride;     // floats per area: T * 2 * M * 16
+    float* xinv;             // [chunk][16]: 1 / sigma per token
+    uint16_t* xh;            // [chunk][M][256]: f16 activations times sigma
 };
+
+constexpr size_t kXhBudget = (size_t)8 << 20;   // converted activations of a batch's f16 ops
 
 // ---------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -98,14 +122,58 @@ __device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uin
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// D = A . B (+ C) on f16 operands, fp32 accumulation
+template <bool ACC>
+__device__ __forceinline__ void mma_f16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    if constexpr (ACC)
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%10,%10,%10};"
+            : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// the four e5m2 bytes of v as f16 pairs (bytes 0, 1) and (2, 3); exact
+__device__ __forceinline__ void e5m2x4_f16(uint32_t v, uint32_t& lo, uint32_t& hi) {
+    asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; cvt.rn.f16x2.e5m2x2 %0, l; cvt.rn.f16x2.e5m2x2 %1, h; }"
+        : "=r"(lo), "=r"(hi)
+        : "r"(v));
+}
+// the eight e2m1 codes of v (code 2j + i in byte j, i = 0 the low nibble) as
+// f16 pairs d[j] = (code 2j, code 2j + 1); exact
+__device__ __forceinline__ void e2m1x8_f16(uint32_t v, uint32_t* d) {
+    asm("{ .reg .b8 b0, b1, b2, b3; mov.b32 {b0, b1, b2, b3}, %4; cvt.rn.f16x2.e2m1x2 %0, b0; "
+        "cvt.rn.f16x2.e2m1x2 %1, b1; cvt.rn.f16x2.e2m1x2 %2, b2; cvt.rn.f16x2.e2m1x2 %3, b3; }"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(v));
+}
+// byte k of w (an e4m3 scale) as an f16 pair (s, s); exact
+__device__ __forceinline__ uint32_t e4m3_f16_dup(uint32_t w, int k) {
+    const uint32_t b = prmt(w, 0u, 0x4400u | (uint32_t)(k * 0x11));
+    uint32_t d;
+    asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; cvt.rn.f16x2.e4m3x2 %0, l; }" : "=r"(d) : "r"(b));
+    return d;
+}
+// FP3 step j (0..3) of a tiled code-word group w[0..2]: the eight codes as
+// e2m1 nibbles (see fp3_pack_tiled in gemv.cu)
+__device__ __forceinline__ uint32_t fp3_e2m1(const uint32_t* w, int j) {
+    if (j < 3) return w[j] & 0xbbbbbbbbu;
+    return ((w[0] >> 2) & 0x11111111u) | ((w[1] >> 1) & 0x22222222u) | ((w[2] << 1) & 0x88888888u);
+}
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
@@ -131,12 +199,20 @@ __device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
 }
 // activations that no op of the batch writes: read-only path; those that an
 // earlier op of the batch produced: L2 (coherent within the launch)
-__device__ __forceinline__ uint4 ld_x(const void* p, bool produced) {
+template <bool PROD>
+__device__ __forceinline__ uint4 ld_x(const void* p) {
     uint4 v;
-    if (produced)
+    if constexpr (PROD)
         asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     else
         asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// activations this launch converted (read after an acquire of their flag)
+__device__ __forceinline__ uint4 ld_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
 
@@ -175,19 +251,27 @@ __device__ __forceinline__ bool wait_count(const int* p, int target, volatile in
 }
 
 // ---------------------------------------------------------------- work split
-// Op k's units are split evenly over T = G * kCW virtual warps in unit
-// order: virtual warp v holds q + (v < rem) units starting at
-// v * q + min(v, rem) (q = U / T, rem = U % T, computed on the host).  CTA c
-// runs virtual warps v = w' * G + c' (c' = (c + k) % G, w' = (w + k) % kCW for
-// its consumer warp w), so every CTA gets an equal share (at most one unit
-// apart) and the roles rotate from op to op.  Row-group contributors are then a
-// contiguous range of virtual warps: sub-ranges are empty only when q == 0,
-// and then only for v >= rem, after every non-empty one.
-__device__ __forceinline__ int vw_start(const Op& op, int v) { return v * op.q + min(v, op.rem); }
-__device__ __forceinline__ int vw_size(const Op& op, int v) { return op.q + (v < op.rem ? 1 : 0); }
-__device__ __forceinline__ int vw_owner(const Op& op, int u) {
-    const int big = op.rem * (op.q + 1);
-    return u < big ? u / (op.q + 1) : op.rem + (u - big) / op.q;
+// Sub-ranges are empty only when q == 0, and then only for v >= rem: the
+// warps that share a row group are a contiguous range of v.
+__device__ __forceinline__ int vw_start(const Seg& sg, int v) { return v * sg.q + min(v, sg.rem); }
+__device__ __forceinline__ int vw_owner(const Seg& sg, int u) {
+    const int big = sg.rem * (sg.q + 1);
+    return u < big ? u / (sg.q + 1) : sg.rem + (u - big) / sg.q;
+}
+
+// The first segment s' >= s in which warp v has units: its range [gu, gend)
+// (positions in the batch's sequence).  False when there is none.
+__device__ __forceinline__ bool find_range(const Args& a, int v, int& s, int& gu, int& gend) {
+    for (; s < a.n_seg; ++s) {
+        const Seg& sg = a.seg[s];
+        const int n = sg.q + (v < sg.rem ? 1 : 0);
+        if (n > 0) {
+            gu = sg.ub + vw_start(sg, v);
+            gend = gu + n;
+            return true;
+        }
+    }
+    return false;
 }
 
 // ---------------------------------------------------------------- decoders
@@ -210,34 +294,34 @@ __device__ __forceinline__ uint32_t code_bf16(int fmt, uint32_t code) {
 
 // FP3 / NVFP4, step s (8 columns) of one row's chunk: four bf16x2 A registers,
 // the natural column pairs (2j, 2j + 1), each a table value times the block's
-// e4m3 scale (exact in bf16).
+// e4m3 scale (exact in bf16).  Both formats decode e2m1 codes (FP3's tiled
+// words become e2m1 nibbles), pair_tab[b] = the two codes of byte b.
 template <int FMT>
 __device__ __forceinline__ void decode_scaled(const uint32_t* c, uint32_t scale_word, int s, const uint32_t* pair_tab,
                                               const uint32_t* scale_tab, uint32_t* A) {
     const uint32_t s2 = scale_tab[(scale_word >> (8 * (s >> 1))) & 0xffu];
-    if constexpr (FMT == SPARK_FMT_FP3) {
-        const uint32_t v = window<6>(c, 24 * s);
+    const uint32_t v = FMT == SPARK_FMT_FP3 ? fp3_e2m1(c + 3 * (s >> 2), s & 3) : c[s];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) A[j] = bmul2(pair_tab[(v >> (6 * j)) & 63u], s2);
-    } else {
-        const uint32_t v = c[s];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) A[j] = bmul2(pair_tab[(v >> (8 * j)) & 0xffu], s2);
-    }
+    for (int j = 0; j < 4; ++j) A[j] = bmul2(pair_tab[(v >> (8 * j)) & 0xffu], s2);
 }
 
-// SPFP2, one row of block s: codes c0..c3 are the nibbles of sA (low 16
-// bits), c4..c7 those of sB; TH = [H, H | 0x80, 0, 0] and TL = [L, L, 0, 0]
-// are the byte tables of the block's exponent (bf16 of +-2^(e-10) has biased
-// exponent E = 117 + e: high byte sign | E >> 1, low byte (E & 1) << 7).
-// Out: P[0..3] = bf16 pairs of columns (0,1) (2,3) (4,5) (6,7).
-__device__ __forceinline__ void decode_spfp2_bf16(uint32_t sA, uint32_t sB, uint32_t TH, uint32_t TL, uint32_t* P) {
-    const uint32_t hA = prmt(TH, 0u, sA), lA = prmt(TL, 0u, sA);
-    const uint32_t hB = prmt(TH, 0u, sB), lB = prmt(TL, 0u, sB);
-    P[0] = prmt(lA, hA, 0x5140u);
-    P[1] = prmt(lA, hA, 0x7362u);
-    P[2] = prmt(lB, hB, 0x5140u);
-    P[3] = prmt(lB, hB, 0x7362u);
+// SPFP2, block s of rows g and g + 8 from the block's code word W: bf16 pairs
+// of columns (2j, 2j + 1).  TL = [L, L, 0, 0] and TH = [H, H | 0x80, 0, 0]
+// are the byte tables of a row's block exponent (bf16 of +-2^(e-10) has
+// biased exponent E = 117 + e: high byte sign | E >> 1, low byte
+// (E & 1) << 7); code c selects byte c of TL and byte c of TH (codes 2 and 3
+// are zero).  y = (W >> 2j) & 0x03030303 holds the codes (a, b, c, d) of
+// columns 2j, 2j + 1 of row g, then of row g + 8, one a byte; y * 0x11 +
+// 0x4040 is the byte-permute selector (a, 4 + a, b, 4 + b) of row g, the
+// high word of y * 0x110000, + 0x4040, the one of row g + 8.
+__device__ __forceinline__ void decode_spfp2_bf16(uint32_t W, uint32_t TLg, uint32_t THg, uint32_t TLh, uint32_t THh,
+                                                  uint32_t* A0, uint32_t* A1) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t y = (W >> (2 * j)) & 0x03030303u;
+        A0[j] = prmt(TLg, THg, y * 0x11u + 0x4040u);
+        A1[j] = prmt(TLh, THh, __umulhi(y, 0x110000u) + 0x4040u);
+    }
 }
 
 // Words of this thread's fragment from a staged unit (lane-interleaved
@@ -260,17 +344,19 @@ __device__ __forceinline__ void load_frag(const uint8_t* slot, int lane, uint32_
 }
 
 // One unit of any format: 8 steps of 8 columns, rows g and g + 8, NTB token
-// tiles of 8; acc[0] / acc[1] take the two MMAs of a step.
-template <int FMT, int NTB>
-__device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* const (&xr)[NTB], const bool (&xv)[NTB],
-                                         int64_t col, bool produced, const uint32_t* pair_tab,
-                                         const uint32_t* scale_tab, float (&acc)[2][NTB][4]) {
+// tiles of 8; acc[0] / acc[1] take the two MMAs of a step.  xr[j]: the row of
+// x this lane feeds to token tile j (lanes past the last token repeat it; the
+// columns they produce are never written).
+template <int FMT, int NTB, bool PROD>
+__device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* const (&xr)[NTB], int64_t col,
+                                         const uint32_t* pair_tab, const uint32_t* scale_tab,
+                                         float (&acc)[2][NTB][4]) {
     // one token tile: the unit's activations for all 8 steps are loaded first,
     // so their latency overlaps the decode
     uint4 xs[NTB == 1 ? 8 : 1];
     if constexpr (NTB == 1) {
 #pragma unroll
-        for (int s = 0; s < 8; ++s) xs[s] = xv[0] ? ld_x(xr[0] + col + 8 * s, produced) : make_uint4(0u, 0u, 0u, 0u);
+        for (int s = 0; s < 8; ++s) xs[s] = ld_x<PROD>(xr[0] + col + 8 * s);
     }
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
@@ -284,11 +370,8 @@ __device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* con
             const uint32_t Hh = (Yh >> 1) & 0x7f7f7f7fu, Lh = (Yh << 7) & 0x80808080u;
             const uint32_t k = (uint32_t)(s & 3);
             const uint32_t selH = 0x8800u | ((4u + k) << 4) | k, selL = 0x4400u | (k << 4) | k;
-            const uint32_t W = fw[s];
-            decode_spfp2_bf16(W & 0x3333u, (W >> 2) & 0x3333u, prmt(Hg, Hg | 0x80808080u, selH), prmt(Lg, 0u, selL),
-                              A0);
-            decode_spfp2_bf16((W >> 16) & 0x3333u, (W >> 18) & 0x3333u, prmt(Hh, Hh | 0x80808080u, selH),
-                              prmt(Lh, 0u, selL), A1);
+            decode_spfp2_bf16(fw[s], prmt(Lg, 0u, selL), prmt(Hg, Hg | 0x80808080u, selH), prmt(Lh, 0u, selL),
+                              prmt(Hh, Hh | 0x80808080u, selH), A0, A1);
         } else {
             constexpr int CW = FMT == SPARK_FMT_FP3 ? 6 : 8;
             decode_scaled<FMT>(fw, fw[CW], s, pair_tab, scale_tab, A0);
@@ -296,11 +379,74 @@ __device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* con
         }
 #pragma unroll
         for (int j = 0; j < NTB; ++j) {
-            uint4 x = make_uint4(0u, 0u, 0u, 0u);
+            uint4 x;
             if constexpr (NTB == 1) x = xs[s];
-            else if (xv[j]) x = ld_x(xr[j] + col + 8 * s, produced);
+            else x = ld_x<PROD>(xr[j] + col + 8 * s);
             mma_bf16(acc[0][j], A0[0], A1[0], A0[1], A1[1], x.x, x.y);
             mma_bf16(acc[1][j], A0[2], A1[2], A0[3], A1[3], x.z, x.w);
+        }
+    }
+}
+
+// f16 path, step s of rows g (A0) and g + 8 (A1): four f16 pairs each.
+// SPFP2: the e5m2 bytes of columns (0, 4, 1, 5) and (2, 6, 3, 7) (nibbles of
+// W & 0x3333 and W >> 2 & 0x3333; row g + 8 from W >> 16), T = [B, B | 0x80,
+// 0, 0] with B = (e + 5) << 2 the block's byte table; pairs (0, 4) (1, 5)
+// (2, 6) (3, 7), the order the activations are converted in.  FP3 / NVFP4:
+// e2m1 pairs (2j, 2j + 1) times the block's scale.
+template <int FMT>
+__device__ __forceinline__ void decode_f16(const uint32_t* fw, int s, uint32_t* A0, uint32_t* A1) {
+    if constexpr (FMT == SPARK_FMT_SPFP2) {
+        const uint32_t E = fw[8 + (s >> 2)];
+        const uint32_t Bg = (E & 0x0f0f0f0fu) * 4u + 0x14141414u, Bh = ((E >> 4) & 0x0f0f0f0fu) * 4u + 0x14141414u;
+        const uint32_t k = (uint32_t)(s & 3);
+        const uint32_t sel = 0x8800u | ((4u + k) << 4) | k;
+        const uint32_t Tg = prmt(Bg, Bg | 0x80808080u, sel), Th = prmt(Bh, Bh | 0x80808080u, sel);
+        const uint32_t W = fw[s];
+        e5m2x4_f16(prmt(Tg, 0u, W & 0x3333u), A0[0], A0[1]);
+        e5m2x4_f16(prmt(Tg, 0u, (W >> 2) & 0x3333u), A0[2], A0[3]);
+        e5m2x4_f16(prmt(Th, 0u, (W >> 16) & 0x3333u), A1[0], A1[1]);
+        e5m2x4_f16(prmt(Th, 0u, (W >> 18) & 0x3333u), A1[2], A1[3]);
+    } else {
+        constexpr int CW = FMT == SPARK_FMT_FP3 ? 6 : 8;
+        const uint32_t vg = FMT == SPARK_FMT_FP3 ? fp3_e2m1(fw + 3 * (s >> 2), s & 3) : fw[s];
+        const uint32_t vh = FMT == SPARK_FMT_FP3 ? fp3_e2m1(fw + CW + 1 + 3 * (s >> 2), s & 3) : fw[CW + 1 + s];
+        const uint32_t sg = e4m3_f16_dup(fw[CW], s >> 1), sh = e4m3_f16_dup(fw[2 * CW + 1], s >> 1);
+        e2m1x8_f16(vg, A0);
+        e2m1x8_f16(vh, A1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            A0[j] = hmul2(A0[j], sg);
+            A1[j] = hmul2(A1[j], sh);
+        }
+    }
+}
+
+// f16 path, one unit into fresh accumulators.  xr[j]: this lane's row of the
+// converted activations for token tile j, at the unit's chunk.
+template <int FMT, int NTB>
+__device__ __forceinline__ void unit_h(const uint32_t* fw, const uint16_t* const (&xr)[NTB], float (&acc)[2][NTB][4]) {
+    uint4 xs[NTB == 1 ? 8 : 1];
+    if constexpr (NTB == 1) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s) xs[s] = ld_v4(xr[0] + 8 * s);
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        uint32_t A0[4], A1[4];
+        decode_f16<FMT>(fw, s, A0, A1);
+#pragma unroll
+        for (int j = 0; j < NTB; ++j) {
+            uint4 x;
+            if constexpr (NTB == 1) x = xs[s];
+            else x = ld_v4(xr[j] + 8 * s);
+            if (s == 0) {
+                mma_f16<false>(acc[0][j], A0[0], A1[0], A0[1], A1[1], x.x, x.y);
+                mma_f16<false>(acc[1][j], A0[2], A1[2], A0[3], A1[3], x.z, x.w);
+            } else {
+                mma_f16<true>(acc[0][j], A0[0], A1[0], A0[1], A1[1], x.x, x.y);
+                mma_f16<true>(acc[1][j], A0[2], A1[2], A0[3], A1[3], x.z, x.w);
+            }
         }
     }
 }
@@ -315,47 +461,48 @@ __device__ __forceinline__ float silu_mul(float gv, float uv) { return gv / (1.0
 struct Ctl {
     int* err;
     volatile int* abort;
-    int* op_done;
+    int* seg_done;
 };
 
-// Row-group segments of op k are held as v[2j + i][r] = row g (r = 0) / g + 8
-// (r = 1) of token 8j + 2t + i.  write_rows writes a whole row group;
-// flush_partial publishes the partial of a segment, and the last contributor
-// sums the partials in unit order and writes the rows.
+// Row-group values are held as v[2j + i][r] = row g (r = 0) / g + 8 (r = 1)
+// of token 8j + 2t + i.  write_rows writes a whole row group; flush_partial
+// publishes the partial of a shared one, and the last warp to arrive sums the
+// partials in unit order and writes the rows.
 template <int NV>
 __device__ __forceinline__ void write_rows(const Op& op, int M, int rg, const float (&v)[NV][2], int lane) {
     const int g = lane >> 2, t = lane & 3;
-    {
-        const int64_t r0 = (int64_t)rg * 16 + g, r1 = r0 + 8;
-        const float b0 = r0 < op.oc ? bias_at(op, r0) : 0.0f, b1 = r1 < op.oc ? bias_at(op, r1) : 0.0f;
+    const int64_t r0 = (int64_t)rg * 16 + g, r1 = r0 + 8;
+    const float b0 = r0 < op.oc ? bias_at(op, r0) : 0.0f, b1 = r1 < op.oc ? bias_at(op, r1) : 0.0f;
 #pragma unroll
-        for (int idx = 0; idx < NV; ++idx) {
-            const int m = 8 * (idx >> 1) + 2 * t + (idx & 1);
-            if (m >= M) continue;
-            if (op.silu) {
-                // rows g (gate) and g + 8 (its up row) -> column 8 rg + g
-                store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + (int64_t)rg * 8 + g,
-                                 silu_mul(v[idx][0] + b0, v[idx][1] + b1));
-                continue;
-            }
-            if (r0 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r0, v[idx][0] + b0);
-            if (r1 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r1, v[idx][1] + b1);
+    for (int idx = 0; idx < NV; ++idx) {
+        const int m = 8 * (idx >> 1) + 2 * t + (idx & 1);
+        if (m >= M) continue;
+        if (op.silu) {
+            // rows g (gate) and g + 8 (its up row) -> column 8 rg + g
+            store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + (int64_t)rg * 8 + g,
+                             silu_mul(v[idx][0] + b0, v[idx][1] + b1));
+            continue;
         }
+        if (r0 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r0, v[idx][0] + b0);
+        if (r1 < op.oc) store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r1, v[idx][1] + b1);
     }
 }
 
+// slot: 0 for the row group holding the start of this warp's range in the
+// segment, 1 for the one holding its end.
 template <int NV>
-__device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int k, int vw, int rg, int slot,
+__device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int s, int k, int vw, int rg, int slot,
                                            const float (&v)[NV][2], int lane) {
     const Op& op = a.op[k];
+    const Seg& sg = a.seg[s];
     const int g = lane >> 2, t = lane & 3;
     const int M = a.M;
-    float* area = a.partials + (int64_t)(k % a.part_ring) * a.part_stride;
-    // areas are reused every part_ring ops: the op that last used this one
-    // must be finished (every warp past it, its partials read)
-    if (k >= a.part_ring) {
+    float* area = a.partials + (int64_t)(s % a.part_ring) * a.part_stride;
+    // areas are reused every part_ring segments: the segment that last used
+    // this one must be finished (every warp past it, its partials read)
+    if (s >= a.part_ring) {
         bool ok = true;
-        if (lane == 0) ok = wait_count(C.op_done + (k - a.part_ring), gridDim.x * kCW, C.abort, C.err);
+        if (lane == 0) ok = wait_count(C.seg_done + (s - a.part_ring), a.seg[s - a.part_ring].active, C.abort, C.err);
         if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
     }
     float* mine = area + ((int64_t)vw * 2 + slot) * M * 16;
@@ -367,19 +514,18 @@ __device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int k, i
             __stcg(mine + m * 16 + g + 8, v[idx][1]);
         }
     }
+    __threadfence();
     __syncwarp();
-    const int first = rg * op.n_kc;
-    const int v_lo = vw_owner(op, first), v_hi = vw_owner(op, first + op.n_kc - 1);
+    const int first = op.ub + rg * op.n_kc - sg.ub;        // the row group's units in segment order
+    const int v_lo = vw_owner(sg, first), v_hi = vw_owner(sg, first + op.n_kc - 1);
     int old = 0;
-    if (lane == 0) {
-        __threadfence_block();
-        old = atom_acq_rel_add(a.counters + op.cnt_off + rg, 1);
-    }
+    if (lane == 0) old = atom_acq_rel_add(a.counters + op.cnt_off + rg, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old != v_hi - v_lo) return;
+    __threadfence();
     // the first contributor holds this row group in its second slot when its
-    // sub-range began in an earlier row group
-    const int lo_slot = vw_start(op, v_lo) < first ? 1 : 0;
+    // range began before the row group
+    const int lo_slot = vw_start(sg, v_lo) < first ? 1 : 0;
     const int row = lane & 15;
     const int64_t r = (int64_t)rg * 16 + row;
     const float b = op.silu ? (row < 8 ? bias_at(op, r) : 0.0f) : (r < op.oc ? bias_at(op, r) : 0.0f);
@@ -414,168 +560,390 @@ __device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int k, i
     if (lane == 0) a.counters[op.cnt_off + rg] = 0;
 }
 
-// ---------------------------------------------------------------- roles
-__device__ void producer(const Args& a, uint8_t* ring, uint64_t* full, uint64_t* empty, const Ctl& C,
-                         volatile int* s_abort) {
-    const int G = gridDim.x, c = blockIdx.x;
-    uint64_t policy;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-    uint32_t q = 0;
-    bool stop = false;
-    const uint32_t ring0 = smem_u32(ring);
-    for (int k = 0; k < a.n_ops && !stop; ++k) {
-        const Op& op = a.op[k];
-        const int cr = (c + k) % G;
-        const int S = op.q + (cr < op.rem ? 1 : 0);
-        const uint32_t ub = (uint32_t)op.unit_bytes;
-        // per consumer warp: its first unit's address; warps with v < rem hold
-        // one unit more (the last stage's), the others q
-        const uint8_t* src[kCW];
-        int n_long = 0;
+// ---------------------------------------------------------------- converted activations
+__device__ __forceinline__ void st_release(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t f16x2_rn(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
+// Convert chunk c (256 columns) of op k's activations, one warp: lane l
+// takes columns 8l..8l+7 (step l & 7 of the 64-column slice l >> 3) of every
+// token, in the order the op's decoder pairs them (SPFP2: 0, 4, 1, 5, 2, 6,
+// 3, 7; FP3 / NVFP4: natural).  Then publish the chunk.
+template <bool PROD>
+__device__ __noinline__ void prep_chunk(const Args& a, int k, int c, int lane) {
+    const Op& op = a.op[k];
+    const int M = a.M;
+    const int gc = op.chunk0 + c;
+    bool bad = false;
+    for (int m = 0; m < M; ++m) {
+        const uint4 v = ld_x<PROD>(op.x + (int64_t)m * op.ldx + (int64_t)c * 256 + 8 * lane);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        float f[8];
+        float mx = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kCW; ++w) {
-            const int v = ((w + k) % kCW) * G + cr;
-            src[w] = op.w + (int64_t)vw_start(op, v) * ub;
-            n_long += v < op.rem ? 1 : 0;
+        for (int i = 0; i < 4; ++i) {
+            f[2 * i] = __uint_as_float(w[i] << 16);
+            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
         }
-        for (int s = 0; s < S; ++s, ++q) {
-            const uint32_t st = q % kStages;
-            if (!wait_phase(smem_u32(empty + st), ((q / kStages) & 1u) ^ 1u, s_abort, C.abort, C.err) || *C.abort) {
-                *s_abort = 1;
-                stop = true;
-                break;
-            }
-            const bool last = s == op.q;
-            const uint32_t fb = smem_u32(full + st);
-            mbar_expect_tx(fb, (uint32_t)((last ? n_long : kCW) * op.unit_bytes));
-            const uint32_t dst0 = ring0 + st * kStageBytes;
 #pragma unroll
-            for (int w = 0; w < kCW; ++w) {
-                // on the last stage only warps w' * G + c' < rem have a unit
-                if (last && ((w + k) % kCW) * G + cr >= op.rem) continue;
-                asm volatile(
-                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], "
-                    "%2, [%3], %4;" ::"r"(dst0 + w * kSlotBytes),
-                    "l"(src[w] + (int64_t)s * ub), "r"(ub), "r"(fb), "l"(policy)
-                    : "memory");
-            }
+        for (int i = 0; i < 8; ++i) {
+            bad |= !isfinite(f[i]);
+            mx = fmaxf(mx, fabsf(f[i]));
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        // sigma = 2^(14 - E) for max |x| = 1.f * 2^E (E clamped below at -112)
+        const int e = max((int)((__float_as_uint(mx) >> 23) & 0xffu), 15);
+        const float sig = mx > 0.0f ? __uint_as_float((uint32_t)(268 - e) << 23) : 1.0f;
+        const float inv = mx > 0.0f ? __uint_as_float((uint32_t)(e - 14) << 23) : 1.0f;
+        if (lane == 0) a.xinv[(int64_t)gc * 16 + m] = inv;
+        uint4 o;
+        if (op.fmt == SPARK_FMT_SPFP2)
+            o = make_uint4(f16x2_rn(f[0] * sig, f[4] * sig), f16x2_rn(f[1] * sig, f[5] * sig),
+                           f16x2_rn(f[2] * sig, f[6] * sig), f16x2_rn(f[3] * sig, f[7] * sig));
+        else
+            o = make_uint4(f16x2_rn(f[0] * sig, f[1] * sig), f16x2_rn(f[2] * sig, f[3] * sig),
+                           f16x2_rn(f[4] * sig, f[5] * sig), f16x2_rn(f[6] * sig, f[7] * sig));
+        *reinterpret_cast<uint4*>(a.xh + ((int64_t)gc * M + m) * 256 + 8 * lane) = o;
     }
-    if (stop) {
-        // let the copies already issued land before the CTA retires
-        const uint32_t lo = q > kStages ? q - kStages : 0;
-        for (uint32_t p = lo; p < q; ++p) {
-            const uint64_t dl = globaltimer_ns() + kWaitNs;
-            while (!mbar_try(smem_u32(full + p % kStages), (p / kStages) & 1u) && globaltimer_ns() < dl) {
+    if (lane >= M && lane < 16) a.xinv[(int64_t)gc * 16 + lane] = 1.0f;
+    bad = __any_sync(0xffffffffu, bad);
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) st_release(a.counters + op.flag_off + c, bad ? 3 : 2);
+}
+
+// Make every chunk of op k's converted activations ready: claim and prepare the
+// unclaimed ones, then wait (bounded) for the rest.  bad: a chunk holds an
+// inf or NaN.  False on abort.
+template <bool PROD>
+__device__ bool ensure_chunks(const Args& a, const Ctl& C, int k, int vw, int lane, bool& bad) {
+    const Op& op = a.op[k];
+    int* flags = a.counters + op.flag_off;
+    const int n = op.n_kc;
+    // claim free chunks one at a time, looking from a warp-dependent chunk on,
+    // so the warps that reach an op together prepare its chunks in parallel
+    const int start = vw % n;
+    while (true) {
+        int found = -1;
+        for (int b0 = 0; b0 < n && found < 0; b0 += 32) {
+            int c = start + b0 + lane;
+            c -= c >= n ? n : 0;
+            c -= c >= n ? n : 0;
+            const bool free = b0 + lane < n && ld_acquire(flags + c) == 0;
+            const unsigned m = __ballot_sync(0xffffffffu, free);
+            if (m) found = __shfl_sync(0xffffffffu, c, __ffs(m) - 1);
+        }
+        if (found < 0) break;
+        int won = 0;
+        if (lane == 0) won = atomicCAS(flags + found, 0, 1) == 0;
+        if (__shfl_sync(0xffffffffu, won, 0)) prep_chunk<PROD>(a, k, found, lane);
+    }
+    bool any_bad = false, ok = true;
+    for (int b0 = 0; b0 < n && ok; b0 += 32) {
+        const int c = b0 + lane;
+        int f = 2;
+        if (c < n) {
+            f = ld_acquire(flags + c);
+            if (f < 2) {
+                const uint64_t dl = globaltimer_ns() + kWaitNs;
+                while ((f = ld_acquire(flags + c)) < 2) {
+                    if (*C.abort) {
+                        ok = false;
+                        break;
+                    }
+                    if (globaltimer_ns() > dl) {
+                        report_device_error(C.err, 1);
+                        *C.abort = 1;
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
             }
+        }
+        any_bad |= f == 3;
+        ok = __all_sync(0xffffffffu, ok);
+    }
+    bad = __any_sync(0xffffffffu, any_bad);
+    __threadfence();
+    return ok;
+}
+
+// ---------------------------------------------------------------- the warp's copy stream
+// The warp's next unit to copy: a run of `left` units of op k from address
+// src (one op inside range [.., gend) of segment s; run_end: the run's end in
+// the sequence).  Warp-uniform; lane 0 issues the copies.
+struct Feed {
+    const uint8_t* src;
+    int left, ubytes;
+    int s, run_end, gend, k;
+    bool live;
+    uint32_t slot;           // next slot to fill
+    uint32_t n;              // copies issued
+};
+
+// Start the run of op k at sequence position gu.
+__device__ __forceinline__ void feed_run(const Args& a, Feed& F, int gu) {
+    while (F.k + 1 < a.n_ops && gu >= a.op[F.k + 1].ub) ++F.k;
+    const Op& op = a.op[F.k];
+    F.ubytes = op.unit_bytes;
+    F.src = op.w + (int64_t)(gu - op.ub) * op.unit_bytes;
+    F.run_end = min(F.gend, op.ub + op.units);
+    F.left = F.run_end - gu;
+}
+
+__device__ __forceinline__ void feed_next(const Args& a, Feed& F, int vw) {
+    int gu = F.run_end;
+    if (gu == F.gend) {
+        ++F.s;
+        F.live = find_range(a, vw, F.s, gu, F.gend);
+        if (!F.live) return;
+    }
+    feed_run(a, F, gu);
+}
+
+__device__ __forceinline__ void feed_issue(const Args& a, Feed& F, int vw, uint32_t ring, uint32_t bars, int lane,
+                                           uint64_t policy) {
+    if (lane == 0) {
+        const uint32_t fb = bars + 8 * F.slot;
+        mbar_expect_tx(fb, (uint32_t)F.ubytes);
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+            "%4;" ::"r"(ring + F.slot * kSlotBytes),
+            "l"(F.src), "r"(F.ubytes), "r"(fb), "l"(policy)
+            : "memory");
+    }
+    F.src += F.ubytes;
+    F.slot = F.slot + 1 == kDepth ? 0 : F.slot + 1;
+    ++F.n;
+    if (--F.left == 0) feed_next(a, F, vw);
+}
+
+// The consumer side of the same sequence.
+struct Walk {
+    uint32_t slot, parity;   // next slot to read and its phase parity
+    uint32_t n;              // units read
+    bool dead;
+};
+
+// Process units [gu, end) of op k (all inside one range of segment s, which
+// ends at gend).  seg0: the first unit of the row group's part being summed.
+template <int FMT, int NTB, bool PROD, bool H = false>
+__device__ __forceinline__ void run_units(const Args& a, const Ctl& C, Feed& F, Walk& Wk, int s, int k, int gu,
+                                          int end, int gend, int vw, int k_first, int rg_first, const uint8_t* ring_p,
+                                          uint32_t ring, uint32_t bars, volatile int* s_abort, const uint32_t* pair_tab,
+                                          const uint32_t* scale_tab, int lane, uint64_t policy) {
+    const Op& op = a.op[k];
+    const int g = lane >> 2, t = lane & 3;
+    const int M = a.M;
+    const int n_kc = op.n_kc;
+    // x rows this lane feeds (token 8j + g; lanes past the last token repeat
+    // it): the caller's bf16 rows, or on the f16 path the converted chunks
+    const uint16_t* xr[NTB];
+    const float* xi = nullptr;          // f16 path: 1 / sigma of tokens 2t, 2t + 1 (+ 8j) per chunk
+    int64_t kc_stride = 256;            // elements from one chunk to the next in xr
+#pragma unroll
+    for (int j = 0; j < NTB; ++j) {
+        const int m = min(8 * j + g, M - 1);
+        if constexpr (H) xr[j] = a.xh + ((int64_t)op.chunk0 * M + m) * 256 + t * 64;
+        else xr[j] = op.x + (int64_t)m * op.ldx + t * 64;
+    }
+    if constexpr (H) {
+        xi = a.xinv + (int64_t)op.chunk0 * 16 + 2 * t;
+        kc_stride = 256 * M;
+    }
+    const int lu0 = gu - op.ub;
+    int rg = lu0 / n_kc, kc = lu0 - rg * n_kc;
+    int seg0 = gu;
+    float acc[2][NTB][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < NTB; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[h][j][i] = 0.0f;
+    constexpr int FW = FMT == SPARK_FMT_SPFP2 ? 10 : (FMT == SPARK_FMT_FP3 ? 14 : 18);
+    for (; gu < end; ++gu) {
+        const bool ok = __all_sync(0xffffffffu, wait_phase(bars + 8 * Wk.slot, Wk.parity, s_abort, C.abort, C.err));
+        if (!ok) {
+            Wk.dead = true;
+            return;
+        }
+        uint32_t fw[FW];
+        load_frag<FW>(ring_p + Wk.slot * kSlotBytes, lane, fw);
+        __syncwarp();
+        // the slot's bytes are in registers: refill it with the unit kDepth ahead
+        if (F.live) {
+            if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            feed_issue(a, F, vw, ring, bars, lane, policy);
+        }
+        ++Wk.n;
+        if (++Wk.slot == kDepth) {
+            Wk.slot = 0;
+            Wk.parity ^= 1u;
+        }
+
+        if constexpr (H) {
+            const uint16_t* xq[NTB];
+#pragma unroll
+            for (int j = 0; j < NTB; ++j) xq[j] = xr[j] + (int64_t)kc * kc_stride;
+            float u[2][NTB][4];
+            unit_h<FMT, NTB>(fw, xq, u);
+#pragma unroll
+            for (int j = 0; j < NTB; ++j) {
+                const float2 r = *reinterpret_cast<const float2*>(xi + kc * 16 + 8 * j);
+                acc[0][j][0] += (u[0][j][0] + u[1][j][0]) * r.x;
+                acc[0][j][1] += (u[0][j][1] + u[1][j][1]) * r.y;
+                acc[0][j][2] += (u[0][j][2] + u[1][j][2]) * r.x;
+                acc[0][j][3] += (u[0][j][3] + u[1][j][3]) * r.y;
+            }
+        } else {
+            const uint16_t* xq[NTB];
+#pragma unroll
+            for (int j = 0; j < NTB; ++j) xq[j] = xr[j];
+            unit_mma<FMT, NTB, PROD>(fw, xq, (int64_t)kc * 256, pair_tab, scale_tab, acc);
+        }
+
+        if (kc == n_kc - 1 || gu + 1 == gend) {
+            float vals[2 * NTB][2];
+#pragma unroll
+            for (int j = 0; j < NTB; ++j)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    vals[2 * j + i][0] = acc[0][j][i] + acc[1][j][i];
+                    vals[2 * j + i][1] = acc[0][j][2 + i] + acc[1][j][2 + i];
+                }
+            if (kc == n_kc - 1 && seg0 == op.ub + rg * n_kc)
+                write_rows<2 * NTB>(op, M, rg, vals, lane);
+            else
+                flush_partial<2 * NTB>(a, C, s, k, vw, rg, (k == k_first && rg == rg_first) ? 0 : 1, vals, lane);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int j = 0; j < NTB; ++j)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[h][j][i] = 0.0f;
+            seg0 = gu + 1;
+        }
+        if (++kc == n_kc) {
+            kc = 0;
+            ++rg;
         }
     }
 }
 
+template <int NTB, bool PROD, bool H>
+__device__ __forceinline__ void run_op(const Args& a, const Ctl& C, Feed& F, Walk& Wk, int s, int k, int gu, int end,
+                                       int gend, int vw, int k_first, int rg_first, const uint8_t* ring_p, uint32_t ring,
+                                       uint32_t bars, volatile int* s_abort, const uint32_t* pair_nv,
+                                       const uint32_t* scale_tab, int lane, uint64_t policy) {
+    const int fmt = a.op[k].fmt;
+    if (fmt == SPARK_FMT_SPFP2)
+        run_units<SPARK_FMT_SPFP2, NTB, PROD, H>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring,
+                                                 bars, s_abort, pair_nv, scale_tab, lane, policy);
+    else if (fmt == SPARK_FMT_FP3)
+        run_units<SPARK_FMT_FP3, NTB, PROD, H>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring,
+                                               bars, s_abort, pair_nv, scale_tab, lane, policy);
+    else
+        run_units<SPARK_FMT_NVFP4, NTB, PROD, H>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring,
+                                                 bars, s_abort, pair_nv, scale_tab, lane, policy);
+}
+
 template <int NTB>
-__device__ void consumer(const Args& a, const uint8_t* ring, uint64_t* full, uint64_t* empty, const Ctl& C,
-                         volatile int* s_abort, const uint32_t* pair_fp3, const uint32_t* pair_nv,
-                         const uint32_t* scale_tab, int warp, int lane) {
-    const int G = gridDim.x, c = blockIdx.x;
-    const int T = G * kCW;
-    const int g = lane >> 2, t = lane & 3;
-    const int M = a.M;
-    uint32_t q = 0;
-    bool dead = false;
-    for (int k = 0; k < a.n_ops; ++k) {
-        const Op& op = a.op[k];
-        const int cr = (c + k) % G;
-        const int vw = ((warp + k) % kCW) * G + cr;
-        const int u0 = vw_start(op, vw), mine = vw_size(op, vw);
-        const int S = op.q + (cr < op.rem ? 1 : 0);
-        const bool produced = op.dep0 >= 0 || op.dep1 >= 0;
-        if (mine > 0 && !dead && produced) {
-            // earlier ops of the batch whose output this op reads
-            bool ok = true;
-            if (lane == 0) {
-                if (op.dep0 >= 0) ok = wait_count(C.op_done + op.dep0, T, C.abort, C.err);
-                if (ok && op.dep1 >= 0) ok = wait_count(C.op_done + op.dep1, T, C.abort, C.err);
-            }
-            dead = !__shfl_sync(0xffffffffu, ok ? 1 : 0, 0);
-        }
-        int kc = mine > 0 ? u0 % op.n_kc : 0, rg = mine > 0 ? u0 / op.n_kc : 0;
-        const int rg_first = rg;
-        int seg0 = u0;
-        float acc[2][NTB][4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int j = 0; j < NTB; ++j)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) acc[h][j][i] = 0.0f;
-        const uint16_t* xr[NTB];
-        bool xv[NTB];
-#pragma unroll
-        for (int j = 0; j < NTB; ++j) {
-            xv[j] = 8 * j + g < M;
-            xr[j] = op.x + (int64_t)(8 * j + g) * op.ldx;
-        }
-        for (int s = 0; s < S; ++s, ++q) {
-            const uint32_t st = q % kStages;
-            const bool have = s < mine;
-            if (!dead) {
-                const bool ok = __all_sync(0xffffffffu, wait_phase(smem_u32(full + st), (q / kStages) & 1u, s_abort,
-                                                                   C.abort, C.err));
-                if (!ok) dead = true;
-            }
-            uint32_t fw[18];
-            if (have && !dead) {
-                const uint8_t* slot = ring + st * kStageBytes + warp * kSlotBytes;
-                if (op.fmt == SPARK_FMT_SPFP2) load_frag<10>(slot, lane, fw);
-                else if (op.fmt == SPARK_FMT_FP3) load_frag<14>(slot, lane, fw);
-                else load_frag<18>(slot, lane, fw);
-            }
-            __syncwarp();
-            if (lane == 0 && !dead) mbar_arrive(smem_u32(empty + st));
-            if (!have || dead) continue;
+__device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, uint32_t ring, uint32_t bars,
+                          volatile int* s_abort, const uint32_t* pair_nv, const uint32_t* scale_tab, int vw, int lane) {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    Feed F;
+    F.s = 0;
+    F.k = 0;
+    F.slot = 0;
+    F.n = 0;
+    {
+        int gu = 0;
+        F.live = find_range(a, vw, F.s, gu, F.gend);
+        if (!F.live) return;
+        feed_run(a, F, gu);
+    }
+    // prime the ring
+    for (int i = 0; i < kDepth && F.live; ++i) feed_issue(a, F, vw, ring, bars, lane, policy);
 
-            const int64_t col = (int64_t)kc * 256 + t * 64;
-            if (op.fmt == SPARK_FMT_SPFP2)
-                unit_mma<SPARK_FMT_SPFP2, NTB>(fw, xr, xv, col, produced, pair_fp3, scale_tab, acc);
-            else if (op.fmt == SPARK_FMT_FP3)
-                unit_mma<SPARK_FMT_FP3, NTB>(fw, xr, xv, col, produced, pair_fp3, scale_tab, acc);
+    Walk Wk;
+    Wk.slot = 0;
+    Wk.parity = 0;
+    Wk.n = 0;
+    Wk.dead = false;
+    int s = 0, gu = 0, gend = 0, k = 0;
+    while (!Wk.dead && find_range(a, vw, s, gu, gend)) {
+        while (k + 1 < a.n_ops && gu >= a.op[k + 1].ub) ++k;
+        const int k_first = k;
+        const int rg_first = (gu - a.op[k].ub) / a.op[k].n_kc;
+        while (gu < gend && !Wk.dead) {
+            const Op& op = a.op[k];
+            const int end = min(gend, op.ub + op.units);
+            const bool prod = op.dseg0 >= 0 || op.dseg1 >= 0;
+            if (prod) {
+                // earlier segments whose output this op reads
+                bool ok = true;
+                if (lane == 0) {
+                    if (op.dseg0 >= 0) ok = wait_count(C.seg_done + op.dseg0, a.seg[op.dseg0].active, C.abort, C.err);
+                    if (ok && op.dseg1 >= 0)
+                        ok = wait_count(C.seg_done + op.dseg1, a.seg[op.dseg1].active, C.abort, C.err);
+                }
+                if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+                    Wk.dead = true;
+                    break;
+                }
+            }
+            bool h = false;
+            if (op.f16) {
+                bool bad = false;
+                const bool ok = prod ? ensure_chunks<true>(a, C, k, vw, lane, bad)
+                                     : ensure_chunks<false>(a, C, k, vw, lane, bad);
+                if (!ok) {
+                    Wk.dead = true;
+                    break;
+                }
+                h = !bad;
+            }
+            if (h)
+                run_op<NTB, false, true>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring, bars,
+                                         s_abort, pair_nv, scale_tab, lane, policy);
+            else if (prod)
+                run_op<NTB, true, false>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring, bars,
+                                         s_abort, pair_nv, scale_tab, lane, policy);
             else
-                unit_mma<SPARK_FMT_NVFP4, NTB>(fw, xr, xv, col, produced, pair_nv, scale_tab, acc);
-
-            const int u = u0 + s;
-            if (kc == op.n_kc - 1 || s + 1 == mine) {
-                float vals[2 * NTB][2];
-#pragma unroll
-                for (int j = 0; j < NTB; ++j)
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        vals[2 * j + i][0] = acc[0][j][i] + acc[1][j][i];
-                        vals[2 * j + i][1] = acc[0][j][2 + i] + acc[1][j][2 + i];
-                    }
-                if (seg0 == rg * op.n_kc && u + 1 == (rg + 1) * op.n_kc)
-                    write_rows<2 * NTB>(op, M, rg, vals, lane);
-                else
-                    flush_partial<2 * NTB>(a, C, k, vw, rg, rg == rg_first ? 0 : 1, vals, lane);
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-#pragma unroll
-                    for (int j = 0; j < NTB; ++j)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) acc[h][j][i] = 0.0f;
-                seg0 = u + 1;
-            }
-            if (++kc == op.n_kc) {
-                kc = 0;
-                ++rg;
-            }
+                run_op<NTB, false, false>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring, bars,
+                                          s_abort, pair_nv, scale_tab, lane, policy);
+            gu = end;
+            if (gu < gend) ++k;
         }
-        // this warp is done with op k (outputs and partial reads included); the
-        // count is kept only for ops that something waits on
-        if (op.waited) {
+        if (Wk.dead) break;
+        // this warp is done with segment s (outputs and partial reads
+        // included); the count is kept only for segments something waits on
+        if (a.seg[s].waited) {
+            __threadfence();
             __syncwarp();
-            if (lane == 0) {
-                __threadfence_block();
-                red_release_add(C.op_done + k, 1);
+            if (lane == 0) red_release_add(C.seg_done + s, 1);
+        }
+        ++s;
+    }
+    if (Wk.dead) {
+        // let the copies in flight land before the CTA retires
+        uint32_t sl = Wk.slot, par = Wk.parity;
+        for (uint32_t i = Wk.n; i < F.n; ++i) {
+            const uint64_t dl = globaltimer_ns() + kWaitNs;
+            while (!mbar_try(bars + 8 * sl, par) && globaltimer_ns() < dl) {
+            }
+            if (++sl == kDepth) {
+                sl = 0;
+                par ^= 1u;
             }
         }
     }
@@ -585,49 +953,49 @@ template <int NTB>
 __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ Args a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-    uint64_t* empty = full + kStages;
-    uint32_t* pair_fp3 = reinterpret_cast<uint32_t*>(empty + kStages);
-    uint32_t* pair_nv = pair_fp3 + 64;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kCW * kWarpRing);
+    uint32_t* pair_nv = reinterpret_cast<uint32_t*>(full + kCW * kDepth);
     uint32_t* scale_tab = pair_nv + 256;
     __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     Ctl C;
     C.err = reinterpret_cast<int*>(a.ws);
     C.abort = reinterpret_cast<volatile int*>(a.ws + kCtlAbort);
-    C.op_done = reinterpret_cast<int*>(a.ws + kCtlOpDone);
+    C.seg_done = reinterpret_cast<int*>(a.ws + kCtlSegDone);
     if (threadIdx.x == 0) {
         s_abort = 0;
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(smem_u32(full + i), 1);
-            mbar_init(smem_u32(empty + i), kCW);
-        }
+        for (int i = 0; i < kCW * kDepth; ++i) mbar_init(smem_u32(full + i), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
         const uint32_t sb = __float_as_uint(e4m3_to_f32((uint32_t)i)) >> 16;   // e4m3 values are exact in bf16
         scale_tab[i] = sb | (sb << 16);
         pair_nv[i] = code_bf16(SPARK_FMT_NVFP4, (uint32_t)i & 15u) | (code_bf16(SPARK_FMT_NVFP4, (uint32_t)i >> 4) << 16);
-        if (i < 64) pair_fp3[i] = code_bf16(SPARK_FMT_FP3, (uint32_t)i & 7u) | (code_bf16(SPARK_FMT_FP3, (uint32_t)i >> 3) << 16);
     }
     __syncthreads();
-    volatile int* sab = &s_abort;
-    if (warp == kProdWarp) {
-        if (lane == 0) producer(a, ring, full, empty, C, sab);
-    } else {
-        consumer<NTB>(a, ring, full, empty, C, sab, pair_fp3, pair_nv, scale_tab, warp, lane);
-    }
+    // virtual warp: the warps of a CTA take ranges spread over the sequence,
+    // so an SM mixes formats (SPFP2 decodes on the integer pipe, FP3 / NVFP4
+    // on shared-memory tables and the bf16 multiplier)
+    const int vw = warp * (int)gridDim.x + blockIdx.x;
+    warp_main<NTB>(a, C, ring + warp * kWarpRing, smem_u32(ring + warp * kWarpRing), smem_u32(full + warp * kDepth),
+                   &s_abort, pair_nv, scale_tab, vw, lane);
     __syncthreads();
     // the last CTA out returns the control block to zero for the next launch
+    __shared__ int s_last;
     if (threadIdx.x == 0) {
         __threadfence();
-        const int old = atomicAdd(reinterpret_cast<int*>(a.ws + kCtlCtaDone), 1);
-        if (old == (int)gridDim.x - 1) {
-            __threadfence();
-            for (int k = 0; k < a.n_ops; ++k) C.op_done[k] = 0;
-            // an aborted launch can leave row-group counters raised
-            if (*C.abort)
-                for (int i = 0; i < a.n_cnt; ++i) a.counters[i] = 0;
+        s_last = atomicAdd(reinterpret_cast<int*>(a.ws + kCtlCtaDone), 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        const bool aborted = *C.abort != 0;
+        for (int i = threadIdx.x; i < a.n_seg; i += blockDim.x) C.seg_done[i] = 0;
+        // an aborted launch can leave row-group counters raised; the chunk
+        // flags after them are cleared every launch
+        for (int i = (aborted ? 0 : a.n_cnt) + threadIdx.x; i < a.n_cnt_all; i += blockDim.x) a.counters[i] = 0;
+        __syncthreads();
+        if (threadIdx.x == 0) {
             *C.abort = 0;
             __threadfence();
             *reinterpret_cast<volatile int*>(a.ws + kCtlCtaDone) = 0;
@@ -635,7 +1003,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ 
     }
 }
 
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 2 * kStages * 8 + (64 + 256 + 256) * 4;
+constexpr size_t kSmemBytes = (size_t)kCW * kWarpRing + (size_t)kCW * kDepth * 8 + (256 + 256) * 4;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory above the per-CTA limit");
 
 int sm_count(int dev) {
@@ -704,11 +1072,13 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
     cudaGetDevice(&dev);
     const int G = sm_count(dev);
     SPARK_REQUIRE(G > 0, SPARK_ERR_DEVICE, "spark_linear_batch: no device");
+    const int64_t T = (int64_t)G * kCW;
     Args& a = P->args;
     a = Args{};
     a.n_ops = n_ops;
     a.M = (int)M;
-    int64_t cnt = 0;
+    int64_t cnt = 0, ub = 0;
+    int seg_k0 = 0;
     for (int k = 0; k < n_ops; ++k) {
         const SparkChainOp& o = ops[k];
         SPARK_REQUIRE(o.kind == SPARK_CHAIN_LINEAR, SPARK_ERR_UNSUPPORTED,
@@ -732,6 +1102,13 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
         for (int d = 0; d < 2; ++d)
             SPARK_REQUIRE(o.dep[d] >= -1 && o.dep[d] < k, SPARK_ERR_INVALID,
                           "spark_linear_batch: op %d: dep %d must name an earlier op", k, o.dep[d]);
+        // an op that reads the output of an op of the current segment opens a new one
+        if (o.dep[0] >= seg_k0 || o.dep[1] >= seg_k0) {
+            Seg& sg = a.seg[a.n_seg++];
+            sg.k0 = seg_k0;
+            sg.k1 = k;
+            seg_k0 = k;
+        }
         Op& p = a.op[k];
         p.w = o.wq;
         p.x = static_cast<const uint16_t*>(o.x);
@@ -742,41 +1119,70 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
         p.fmt = fmt;
         p.oc = (int)o.oc;
         p.n_kc = (int)(o.ic / 256);
-        p.n_rg = (int)((o.oc + 15) / 16);
-        const int64_t units = (int64_t)p.n_rg * p.n_kc;
-        SPARK_REQUIRE(units < (1ll << 30) && o.oc < (1ll << 30), SPARK_ERR_UNSUPPORTED,
+        const int64_t n_rg = (o.oc + 15) / 16;
+        const int64_t units = n_rg * p.n_kc;
+        SPARK_REQUIRE(units < (1ll << 30) && o.oc < (1ll << 30) && ub + units < (1ll << 31), SPARK_ERR_UNSUPPORTED,
                       "spark_linear_batch: op %d too large", k);
         p.units = (int)units;
-        p.q = (int)(units / ((int64_t)G * kCW));
-        p.rem = (int)(units % ((int64_t)G * kCW));
+        p.ub = (int)ub;
+        ub += units;
         p.unit_bytes = unit_bytes_of(fmt);
         p.cnt_off = (int)cnt;
-        cnt += p.n_rg;
-        p.dep0 = o.dep[0];
-        p.dep1 = o.dep[1];
+        cnt += n_rg;
+        p.seg = a.n_seg;
+        p.dseg0 = o.dep[0] >= 0 ? a.op[o.dep[0]].seg : -1;
+        p.dseg1 = o.dep[1] >= 0 ? a.op[o.dep[1]].seg : -1;
         p.y_dtype = o.y_dtype;
         p.bias_dtype = o.bias ? o.bias_dtype : 0;
         p.silu = silu ? 1 : 0;
     }
+    {
+        Seg& sg = a.seg[a.n_seg++];
+        sg.k0 = seg_k0;
+        sg.k1 = n_ops;
+    }
     a.n_cnt = (int)std::min<int64_t>(cnt, max_counters);
     SPARK_REQUIRE(cnt <= max_counters, SPARK_ERR_UNSUPPORTED,
                   "spark_linear_batch: %lld row groups in the batch, above %lld", (long long)cnt, (long long)max_counters);
-    const int64_t T = (int64_t)G * kCW;
-    a.part_stride = T * 2 * M * 16;
-    const size_t area = (size_t)a.part_stride * sizeof(float);
-    a.part_ring = (int)std::max<size_t>(1, std::min<size_t>((size_t)n_ops, kPartAreaBudget / area));
+    // ops take the f16 path while their converted activations fit the budget
+    // and their chunk flags fit after the row-group counters
+    int64_t chunks = 0;
     for (int k = 0; k < n_ops; ++k) {
         Op& p = a.op[k];
-        if (k + a.part_ring < n_ops) p.waited = 1;
-        if (p.dep0 >= 0) a.op[p.dep0].waited = 1;
-        if (p.dep1 >= 0) a.op[p.dep1].waited = 1;
+        if ((size_t)(chunks + p.n_kc) * 512 * M > kXhBudget || cnt + chunks + p.n_kc > max_counters) continue;
+        p.f16 = 1;
+        p.chunk0 = (int)chunks;
+        p.flag_off = (int)(cnt + chunks);
+        chunks += p.n_kc;
     }
-    P->scratch_bytes = ((size_t)a.part_ring * area + 255) / 256 * 256;
+    a.n_cnt_all = (int)(cnt + chunks);
+    a.part_stride = T * 2 * M * 16;
+    const size_t area = (size_t)a.part_stride * sizeof(float);
+    a.part_ring = (int)std::max<size_t>(1, std::min<size_t>((size_t)a.n_seg, kPartAreaBudget / area));
+    for (int s = 0; s < a.n_seg; ++s) {
+        Seg& sg = a.seg[s];
+        sg.ub = a.op[sg.k0].ub;
+        sg.units = a.op[sg.k1 - 1].ub + a.op[sg.k1 - 1].units - sg.ub;
+        sg.q = (int)(sg.units / T);
+        sg.rem = (int)(sg.units % T);
+        sg.active = sg.q > 0 ? (int)T : sg.rem;
+        if (s + a.part_ring < a.n_seg) sg.waited = 1;
+    }
+    for (int k = 0; k < n_ops; ++k) {
+        if (a.op[k].dseg0 >= 0) a.seg[a.op[k].dseg0].waited = 1;
+        if (a.op[k].dseg1 >= 0) a.seg[a.op[k].dseg1].waited = 1;
+    }
+    // scratch: partial-sum areas, then 1 / sigma [chunks][16], then the converted activations
+    const size_t inv_off = ((size_t)a.part_ring * area + 255) / 256 * 256;
+    const size_t xh_off = inv_off + ((size_t)chunks * 16 * sizeof(float) + 255) / 256 * 256;
+    P->scratch_bytes = xh_off + (size_t)chunks * 512 * M;
     P->grid = G;
     a.ws = ws;
     if (ws) {
         a.counters = reinterpret_cast<int*>(ws + counters_off);
         a.partials = reinterpret_cast<float*>(ws + scratch_off);
+        a.xinv = reinterpret_cast<float*>(ws + scratch_off + inv_off);
+        a.xh = reinterpret_cast<uint16_t*>(ws + scratch_off + xh_off);
     }
     return SPARK_OK;
 }
@@ -788,14 +1194,18 @@ int stream_plan_alloc(StreamPlan** P) {
 void stream_plan_free(StreamPlan* P) { delete P; }
 size_t stream_plan_scratch(const StreamPlan* P) { return P->scratch_bytes; }
 
-// scratch of a one-op batch (spark_linear on tiled weights, bf16 x)
+// scratch of a one-op batch (spark_linear on tiled weights, bf16 x): the
+// partial-sum area and the f16 path's converted activations
 size_t stream_scratch_single(int64_t M, int64_t ic) {
-    (void)ic;
     int dev = 0;
     cudaGetDevice(&dev);
     const int64_t Mc = M < 1 ? 1 : (M > stream::kMaxTok ? stream::kMaxTok : M);
     const size_t part = (size_t)stream::sm_count(dev) * stream::kCW * 2 * Mc * 16 * sizeof(float);
-    return (part + 255) / 256 * 256;
+    size_t bytes = (part + 255) / 256 * 256;
+    const int64_t chunks = ic / 256;
+    if ((size_t)chunks * 512 * Mc <= stream::kXhBudget)
+        bytes += ((size_t)chunks * 16 * sizeof(float) + 255) / 256 * 256 + (size_t)chunks * 512 * Mc;
+    return bytes;
 }
 
 int stream_launch(const StreamPlan& P, cudaStream_t s) {
