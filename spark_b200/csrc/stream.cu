@@ -451,6 +451,29 @@ __device__ __forceinline__ void unit_h(const uint32_t* fw, const uint16_t* const
     }
 }
 
+// f16 path, one token tile: xs holds this unit's activations (loaded during
+// the unit before); each step's register is refilled with the next unit's
+// (nxt, when the op has one) as soon as its MMAs have read it, so the loads
+// overlap a whole unit of decoding.
+template <int FMT>
+__device__ __forceinline__ void unit_h1(const uint32_t* fw, uint4 (&xs)[8], const uint16_t* nxt,
+                                        float (&acc)[2][1][4]) {
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        uint32_t A0[4], A1[4];
+        decode_f16<FMT>(fw, s, A0, A1);
+        const uint4 x = xs[s];
+        if (s == 0) {
+            mma_f16<false>(acc[0][0], A0[0], A1[0], A0[1], A1[1], x.x, x.y);
+            mma_f16<false>(acc[1][0], A0[2], A1[2], A0[3], A1[3], x.z, x.w);
+        } else {
+            mma_f16<true>(acc[0][0], A0[0], A1[0], A0[1], A1[1], x.x, x.y);
+            mma_f16<true>(acc[1][0], A0[2], A1[2], A0[3], A1[3], x.z, x.w);
+        }
+        if (nxt) xs[s] = ld_v4(nxt + 8 * s);
+    }
+}
+
 // ---------------------------------------------------------------- epilogue
 __device__ __forceinline__ float bias_at(const Op& op, int64_t row) {
     return op.bias ? load_as_float(op.bias, op.bias_dtype, row) : 0.0f;
@@ -514,7 +537,9 @@ __device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int s, i
             __stcg(mine + m * 16 + g + 8, v[idx][1]);
         }
     }
-    __threadfence();
+    // the warp barrier orders every lane's partial before lane 0's release.
+    // (No GPU-scope fence here: lane 0 has bulk copies in flight, and a fence
+    // would wait for them.)
     __syncwarp();
     const int first = op.ub + rg * op.n_kc - sg.ub;        // the row group's units in segment order
     const int v_lo = vw_owner(sg, first), v_hi = vw_owner(sg, first + op.n_kc - 1);
@@ -522,7 +547,7 @@ __device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int s, i
     if (lane == 0) old = atom_acq_rel_add(a.counters + op.cnt_off + rg, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old != v_hi - v_lo) return;
-    __threadfence();
+    __syncwarp();                   // lane 0's acquire before every lane's reads
     // the first contributor holds this row group in its second slot when its
     // range began before the row group
     const int lo_slot = vw_start(sg, v_lo) < first ? 1 : 0;
@@ -612,9 +637,7 @@ __device__ __noinline__ void prep_chunk(const Args& a, int k, int c, int lane) {
         *reinterpret_cast<uint4*>(a.xh + ((int64_t)gc * M + m) * 256 + 8 * lane) = o;
     }
     if (lane >= M && lane < 16) a.xinv[(int64_t)gc * 16 + lane] = 1.0f;
-    bad = __any_sync(0xffffffffu, bad);
-    __threadfence();
-    __syncwarp();
+    bad = __any_sync(0xffffffffu, bad);   // also orders every lane's stores before lane 0's release
     if (lane == 0) st_release(a.counters + op.flag_off + c, bad ? 3 : 2);
 }
 
@@ -670,8 +693,7 @@ __device__ bool ensure_chunks(const Args& a, const Ctl& C, int k, int vw, int la
         any_bad |= f == 3;
         ok = __all_sync(0xffffffffu, ok);
     }
-    bad = __any_sync(0xffffffffu, any_bad);
-    __threadfence();
+    bad = __any_sync(0xffffffffu, any_bad);   // every flag's acquire before any lane's reads
     return ok;
 }
 
@@ -769,6 +791,15 @@ __device__ __forceinline__ void run_units(const Args& a, const Ctl& C, Feed& F, 
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[h][j][i] = 0.0f;
     constexpr int FW = FMT == SPARK_FMT_SPFP2 ? 10 : (FMT == SPARK_FMT_FP3 ? 14 : 18);
+    // f16 path, one token tile: the first unit's activations and scales
+    uint4 xs[H && NTB == 1 ? 8 : 1];
+    float2 rr = make_float2(0.0f, 0.0f);
+    if constexpr (H && NTB == 1) {
+        const uint16_t* x0 = xr[0] + (int64_t)kc * kc_stride;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) xs[q] = ld_v4(x0 + 8 * q);
+        rr = *reinterpret_cast<const float2*>(xi + kc * 16);
+    }
     for (; gu < end; ++gu) {
         const bool ok = __all_sync(0xffffffffu, wait_phase(bars + 8 * Wk.slot, Wk.parity, s_abort, C.abort, C.err));
         if (!ok) {
@@ -789,7 +820,18 @@ __device__ __forceinline__ void run_units(const Args& a, const Ctl& C, Feed& F, 
             Wk.parity ^= 1u;
         }
 
-        if constexpr (H) {
+        if constexpr (H && NTB == 1) {
+            const bool more = gu + 1 < end;
+            const int kn = kc + 1 == n_kc ? 0 : kc + 1;
+            float u[2][1][4];
+            unit_h1<FMT>(fw, xs, more ? xr[0] + (int64_t)kn * kc_stride : nullptr, u);
+            const float2 r = rr;
+            if (more) rr = *reinterpret_cast<const float2*>(xi + kn * 16);
+            acc[0][0][0] += (u[0][0][0] + u[1][0][0]) * r.x;
+            acc[0][0][1] += (u[0][0][1] + u[1][0][1]) * r.y;
+            acc[0][0][2] += (u[0][0][2] + u[1][0][2]) * r.x;
+            acc[0][0][3] += (u[0][0][3] + u[1][0][3]) * r.y;
+        } else if constexpr (H) {
             const uint16_t* xq[NTB];
 #pragma unroll
             for (int j = 0; j < NTB; ++j) xq[j] = xr[j] + (int64_t)kc * kc_stride;
@@ -928,7 +970,6 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
         // this warp is done with segment s (outputs and partial reads
         // included); the count is kept only for segments something waits on
         if (a.seg[s].waited) {
-            __threadfence();
             __syncwarp();
             if (lane == 0) red_release_add(C.seg_done + s, 1);
         }
