@@ -91,6 +91,7 @@ struct Args {
     int n_ops, n_seg, M, n_cnt;
     int part_ring, n_cnt_all;  // part_ring: partial-sum areas, reused every part_ring segments;
                                // n_cnt_all: counters including the chunk flags (reset at the end)
+    int n_chunks, pad1;        // chunks of the f16 ops' converted activations
     uint8_t* ws;
     int* counters;
     float* partials;
@@ -902,6 +903,18 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
                           volatile int* s_abort, const uint32_t* pair_nv, const uint32_t* scale_tab, int vw, int lane) {
     uint64_t policy;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    // chunks of ops whose activations come from outside the batch are
+    // converted at launch start, chunk i by virtual warp i; they are claimed
+    // like the others, so a warp that reaches an op first converts whatever
+    // is still unclaimed itself
+    for (int i = vw; NTB == 1 && i < a.n_chunks; i += (int)gridDim.x * kCW) {
+        int k = 0;
+        while (k < a.n_ops && !(a.op[k].f16 && i >= a.op[k].chunk0 && i < a.op[k].chunk0 + a.op[k].n_kc)) ++k;
+        if (k == a.n_ops || a.op[k].dseg0 >= 0 || a.op[k].dseg1 >= 0) continue;
+        int won = 0;
+        if (lane == 0) won = atomicCAS(a.counters + a.op[k].flag_off + (i - a.op[k].chunk0), 0, 1) == 0;
+        if (__shfl_sync(0xffffffffu, won, 0)) prep_chunk<false>(a, k, i - a.op[k].chunk0, lane);
+    }
     Feed F;
     F.s = 0;
     F.k = 0;
@@ -944,20 +957,23 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
                 }
             }
             bool h = false;
-            if (op.f16) {
-                bool bad = false;
-                const bool ok = prod ? ensure_chunks<true>(a, C, k, vw, lane, bad)
-                                     : ensure_chunks<false>(a, C, k, vw, lane, bad);
-                if (!ok) {
-                    Wk.dead = true;
-                    break;
+            if constexpr (NTB == 1) {      // the f16 path runs up to 8 tokens
+                if (op.f16) {
+                    bool bad = false;
+                    const bool ok = prod ? ensure_chunks<true>(a, C, k, vw, lane, bad)
+                                         : ensure_chunks<false>(a, C, k, vw, lane, bad);
+                    if (!ok) {
+                        Wk.dead = true;
+                        break;
+                    }
+                    h = !bad;
                 }
-                h = !bad;
+                if (h)
+                    run_op<1, false, true>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring, bars,
+                                           s_abort, pair_nv, scale_tab, lane, policy);
             }
-            if (h)
-                run_op<NTB, false, true>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring, bars,
-                                         s_abort, pair_nv, scale_tab, lane, policy);
-            else if (prod)
+            if (h) {
+            } else if (prod)
                 run_op<NTB, true, false>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring, bars,
                                          s_abort, pair_nv, scale_tab, lane, policy);
             else
@@ -1185,10 +1201,12 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
     a.n_cnt = (int)std::min<int64_t>(cnt, max_counters);
     SPARK_REQUIRE(cnt <= max_counters, SPARK_ERR_UNSUPPORTED,
                   "spark_linear_batch: %lld row groups in the batch, above %lld", (long long)cnt, (long long)max_counters);
-    // ops take the f16 path while their converted activations fit the budget
-    // and their chunk flags fit after the row-group counters
+    // up to 8 tokens, ops take the f16 path while their converted activations
+    // fit the budget and their chunk flags fit after the row-group counters
+    // (above 8 tokens the per-unit rescaling of two token tiles costs more than
+    // the cheaper decode saves)
     int64_t chunks = 0;
-    for (int k = 0; k < n_ops; ++k) {
+    for (int k = 0; k < n_ops && M <= 8; ++k) {
         Op& p = a.op[k];
         if ((size_t)(chunks + p.n_kc) * 512 * M > kXhBudget || cnt + chunks + p.n_kc > max_counters) continue;
         p.f16 = 1;
@@ -1197,6 +1215,7 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
         chunks += p.n_kc;
     }
     a.n_cnt_all = (int)(cnt + chunks);
+    a.n_chunks = (int)chunks;
     a.part_stride = T * 2 * M * 16;
     const size_t area = (size_t)a.part_stride * sizeof(float);
     a.part_ring = (int)std::max<size_t>(1, std::min<size_t>((size_t)a.n_seg, kPartAreaBudget / area));
@@ -1244,7 +1263,7 @@ size_t stream_scratch_single(int64_t M, int64_t ic) {
     const size_t part = (size_t)stream::sm_count(dev) * stream::kCW * 2 * Mc * 16 * sizeof(float);
     size_t bytes = (part + 255) / 256 * 256;
     const int64_t chunks = ic / 256;
-    if ((size_t)chunks * 512 * Mc <= stream::kXhBudget)
+    if (Mc <= 8 && (size_t)chunks * 512 * Mc <= stream::kXhBudget)
         bytes += ((size_t)chunks * 16 * sizeof(float) + 255) / 256 * 256 + (size_t)chunks * 512 * Mc;
     return bytes;
 }
