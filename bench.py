@@ -527,8 +527,9 @@ def run_gpu(args, rank, world, local):
 
 
 def load_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if present."""
-    p = os.path.join(ROOT, "profiles", "gemv_spfp2_m1.json")
+    """Per-launch DRAM bytes (read + write) of the dominant kernel, k_stream over the headline
+    step, from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "stream_step_m1.json")
     try:
         with open(p) as f:
             return json.load(f).get("dram_bytes_per_launch")

@@ -194,7 +194,10 @@ SPARK_API int spark_linear_noalloc(int fmt, const uint8_t* wq, const uint8_t* sc
                                    int64_t M, int64_t oc, int64_t ic, int64_t ldx, const void* bias, int bias_dtype,
                                    void* y, int y_dtype, int64_t ldy, void* stream);
 
-/* A chain of dependent decode-step ops in ONE persistent launch: dequant
+/* EXPERIMENTAL (measured slower than the launches it replaces: 0.83 vs 0.65 ms
+ * for a 14-op MLP chain at M = 1, each op paying the tcgen05 decode path's
+ * critical path; spark_linear_batch on tiled weights is the fast batched form).
+ * A chain of dependent decode-step ops in ONE persistent launch: dequant
  * linears (SPFP2 / FP3 / NVFP4 reference layouts, bf16 x, M <= 16 tokens) and
  * SiLU(gate) * up.  It replaces a sequence of spark_linear / spark_silu_mul
  * calls (a layer's q/k/v -> o -> gate/up -> SiLU -> down, as the reference
@@ -229,8 +232,13 @@ SPARK_API int spark_linear_chain(const SparkChainOp* ops, int n_ops, int64_t M, 
                                  size_t workspace_bytes, void* stream);
 
 /* A batch of decode-sized dequant linears (1 to 48 ops, M <= 16 tokens, bf16
- * activations) in ONE persistent launch: the weights of every op stream from
- * HBM through one shared-memory ring per SM without a gap at op boundaries.
+ * activations) in ONE persistent launch: the batch's units (16 rows x 256
+ * columns) form one sequence cut into equal contiguous ranges, one per warp
+ * of the grid, and each warp streams its range from HBM through its own
+ * shared-memory ring, so the weight stream has no gap at op boundaries.  Up
+ * to 8 tokens the weights are decoded to f16 and the activations converted
+ * once per launch to f16 with a power-of-two scale per 256-column chunk;
+ * above 8 tokens, or when a chunk holds an inf or NaN, the op runs on bf16.
  * No counterpart in the reference (it runs one linear per call,
  * 01_core/spark_v3_kernel.cu:172-214); it replaces a sequence of spark_linear
  * calls, e.g. the projections of a decoder layer.  Each op is a SparkChainOp
