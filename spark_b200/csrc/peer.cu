@@ -4,7 +4,7 @@
 // Each rank's down projection writes its partial [M, H] sum into a buffer
 // that every rank can address (the allocation mapped into the other ranks'
 // processes through legacy CUDA IPC handles: plain peer memory over NVLink,
-// no multicast object).  spark_peer_allreduce then gives every
+// no NVLink-SHARP object).  spark_peer_allreduce then gives every
 // rank the full sum without NCCL:
 //   1. CTA b of rank r publishes "partial ready" to CTA b of every rank
 //      (a release store of a per-CTA epoch into each rank's flag array at
@@ -124,7 +124,7 @@ extern "C" {
 int spark_peer_flags_count(int world) { return kPeerCtas * world; }
 
 // Sharing a device buffer with the other ranks of one node (legacy CUDA IPC:
-// a plain peer mapping, no multicast object).  The handle names the whole
+// a plain peer mapping, no NVLink-SHARP object).  The handle names the whole
 // allocation that holds `ptr` (a caching allocator hands out pieces of larger
 // blocks), so the offset of `ptr` inside it travels along.
 int spark_ipc_handle(const void* ptr, void* handle, int64_t* offset) {
