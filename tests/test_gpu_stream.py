@@ -196,3 +196,61 @@ def test_batch_rejects_bad_ops():
     ym = torch.empty(17, 256, dtype=torch.float32, device="cuda")
     with pytest.raises(SparkError, match="M must be"):
         ops().linear_batch([ops().BatchOp("spfp2", wt, xm, ym)])
+
+
+@pytest.mark.parametrize("M", [1, 8, 16])
+def test_batch_long_chain_reuses_partial_areas(M):
+    """Nine dependent ops (nine segments) at M = 1 / 8 / 16: at 8 and 16 tokens
+    the partial-sum areas are fewer than the segments and are reused after a
+    completion wait.  Checked against the same sequence of separate calls."""
+    H = 2560
+    g = torch.Generator().manual_seed(50 + M)
+    fmts = ["spfp2", "fp3", "nvfp4"]
+    layers = []
+    for i in range(9):
+        W = (torch.randn(H, H, generator=g) * 0.02).cuda()
+        fmt = fmts[i % 3]
+        if fmt == "spfp2":
+            wq, s = ops().spfp2_pack(W)[0], None
+        elif fmt == "fp3":
+            wq, s = ops().fp3_pack(W)
+        else:
+            wq, s = ops().nvfp4_pack(W)
+        layers.append((fmt, ops().tile_weights(fmt, wq, s, H, H)))
+    x = torch.randn(M, H, generator=g).bfloat16().cuda()
+    bufs = [x] + [torch.empty(M, H, dtype=torch.bfloat16, device="cuda") for _ in layers]
+    batch = [ops().BatchOp(fmt, wt, bufs[i], bufs[i + 1], deps=[i - 1] if i else ())
+             for i, (fmt, wt) in enumerate(layers)]
+    for _ in range(2):
+        ops().linear_batch(batch)
+    torch.cuda.synchronize()
+    y = x
+    for i, (fmt, wt) in enumerate(layers):
+        y = ops().linear(fmt, wt, None, y, H, H, out_dtype=torch.bfloat16, tiled=True)
+        assert torch.equal(bufs[i + 1], y), (M, i)
+    ops().check_device_errors()
+
+
+def test_batch_mixed_paths():
+    """One batch where one op's activations hold an inf (that op runs the bf16
+    path) and the others are finite (f16 path): the same inf / NaN pattern as
+    the op's own call, finite values within TOL of fp64."""
+    specs = [("spfp2", 1024, 2560), ("fp3", 512, 2560), ("nvfp4", 768, 4096)]
+    g = torch.Generator().manual_seed(61)
+    batch, singles, refs = [], [], []
+    for i, (fmt, oc, ic) in enumerate(specs):
+        wq, s, wt, dec = make(fmt, oc, ic, seed=200 + i)
+        x = torch.randn(2, ic, generator=g).bfloat16().cuda()
+        if i == 1:
+            x[0, 11] = float("inf")
+        y = torch.empty(2, oc, dtype=torch.float32, device="cuda")
+        batch.append(ops().BatchOp(fmt, wt, x, y))
+        singles.append(ops().linear(fmt, wt, None, x, oc, ic, out_dtype=torch.float32, tiled=True))
+        refs.append(ref(x, dec))
+    ops().linear_batch(batch)
+    torch.cuda.synchronize()
+    for op, one, y64 in zip(batch, singles, refs):
+        assert torch.equal(torch.isnan(op.y), torch.isnan(one)) and torch.equal(torch.isinf(op.y), torch.isinf(one))
+        fin = torch.isfinite(one).cpu().numpy()
+        assert np.abs(op.y.cpu().numpy()[fin] - y64[fin]).max() <= TOL
+    ops().check_device_errors()
