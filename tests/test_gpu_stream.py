@@ -4,9 +4,10 @@ oracle-decoded weights.
 
 Tolerance: max |y - y_ref| <= 5e-4 for fp32 output; for
 activations scaled away from 1 the bound scales with max |y_ref| (relative
-1e-5, the fp32 accumulation's own error at these sizes).  SPFP2 up to 4 tokens
-runs the fp8 tensor path (activations split into e4m3 parts), above that and
-for non-finite activations the bf16 path; FP3 / NVFP4 always the bf16 path.
+1e-5, the fp32 accumulation's own error at these sizes).  Up to 8 tokens every
+format runs the f16 path (weights decoded to f16, activations converted once
+per launch with a power-of-two scale per 256-column chunk); above 8 tokens and
+for ops whose activations hold an inf or NaN, the bf16 path.
 """
 from __future__ import annotations
 
@@ -78,9 +79,9 @@ def test_bias_and_output_dtypes(fmt):
 
 
 def test_spfp2_activation_range():
-    """fp8 path: the per-token power-of-two scale and four e4m3 parts keep the
-    result at fp32-accumulation accuracy whatever the activations' magnitude,
-    also with one large outlier per token."""
+    """f16 path: the per-chunk power-of-two scale keeps the result at
+    fp32-accumulation accuracy whatever the activations' magnitude, also with
+    one large outlier per token."""
     oc, ic = 512, 2560
     wq, s, wt, dec = make("spfp2", oc, ic, seed=9)
     g = torch.Generator().manual_seed(10)
