@@ -15,8 +15,8 @@
 //     slots, so no warp ever waits for another one's progress;
 //   * the warp decodes a staged unit in registers and feeds mma.sync (bf16,
 //     fp32 accumulation); a row group shared between warps is summed
-//     deterministically (partials + counter, the last arriver adds them in
-//     unit order);
+//     deterministically (partials + counter; the warp whose range ends in
+//     the row group adds them in unit order);
 //   * an op that reads an earlier op's output starts a new segment of the
 //     sequence (cut the same way): before it reads such an input a warp waits
 //     (bounded) until every warp has finished the producing segment, while its
@@ -192,11 +192,6 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 }
 __device__ __forceinline__ void red_release_add(int* p, int v) {
     asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
-    int old;
-    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
 }
 // activations that no op of the batch writes: read-only path; those that an
 // earlier op of the batch produced: L2 (coherent within the launch)
@@ -490,8 +485,11 @@ struct Ctl {
 
 // Row-group values are held as v[2j + i][r] = row g (r = 0) / g + 8 (r = 1)
 // of token 8j + 2t + i.  write_rows writes a whole row group; flush_partial
-// publishes the partial of a shared one, and the last warp to arrive sums the
-// partials in unit order and writes the rows.
+// publishes the partial of a shared one.  The first contributor (the warp
+// whose range ends in the row group, or begins at its first unit) sums the
+// partials in unit order and writes the rows: it reaches the row group last
+// (the others meet it at the start of their ranges), so it rarely waits, and
+// the others publish without waiting for a round trip.
 template <int NV>
 __device__ __forceinline__ void write_rows(const Op& op, int M, int rg, const float (&v)[NV][2], int lane) {
     const int g = lane >> 2, t = lane & 3;
@@ -544,11 +542,15 @@ __device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int s, i
     __syncwarp();
     const int first = op.ub + rg * op.n_kc - sg.ub;        // the row group's units in segment order
     const int v_lo = vw_owner(sg, first), v_hi = vw_owner(sg, first + op.n_kc - 1);
-    int old = 0;
-    if (lane == 0) old = atom_acq_rel_add(a.counters + op.cnt_off + rg, 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != v_hi - v_lo) return;
-    __syncwarp();                   // lane 0's acquire before every lane's reads
+    int* cnt = a.counters + op.cnt_off + rg;
+    if (vw != v_lo) {
+        if (lane == 0) red_release_add(cnt, 1);
+        return;
+    }
+    // the others never wait on this warp, so the wait ends; bounded all the same
+    bool ok = true;
+    if (lane == 0) ok = wait_count(cnt, v_hi - v_lo, C.abort, C.err);
+    if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;   // lane 0's acquire before every lane's reads
     // the first contributor holds this row group in its second slot when its
     // range began before the row group
     const int lo_slot = vw_start(sg, v_lo) < first ? 1 : 0;
@@ -583,7 +585,7 @@ __device__ __noinline__ void flush_partial(const Args& a, const Ctl& C, int s, i
             store_from_float(op.y, op.y_dtype, (int64_t)m * op.ldy + r, sum + b);
         }
     }
-    if (lane == 0) a.counters[op.cnt_off + rg] = 0;
+    if (lane == 0) *cnt = 0;
 }
 
 // ---------------------------------------------------------------- converted activations
@@ -1206,7 +1208,9 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
     // (above 8 tokens the per-unit rescaling of two token tiles costs more than
     // the cheaper decode saves)
     int64_t chunks = 0;
-    for (int k = 0; k < n_ops && M <= 8; ++k) {
+    // (a one-op batch keeps the bf16 path: the conversion's latency at launch
+    // start costs more than it saves over the few units each warp then has)
+    for (int k = 0; k < n_ops && M <= 8 && n_ops > 1; ++k) {
         Op& p = a.op[k];
         if ((size_t)(chunks + p.n_kc) * 512 * M > kXhBudget || cnt + chunks + p.n_kc > max_counters) continue;
         p.f16 = 1;
