@@ -905,6 +905,24 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
                           volatile int* s_abort, const uint32_t* pair_nv, const uint32_t* scale_tab, int vw, int lane) {
     uint64_t policy;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    Feed F;
+    F.s = 0;
+    F.k = 0;
+    F.slot = 0;
+    F.n = 0;
+    {
+        int gu = 0;
+        F.live = find_range(a, vw, F.s, gu, F.gend);
+        if (F.live) feed_run(a, F, gu);
+    }
+    const bool has_units = F.live;     // (priming clears F.live when the range fits in the ring)
+    // prime the ring.  Weights only: with a programmatic launch this runs
+    // while the previous kernel of the stream may still be finishing, and no
+    // kernel that triggers this launch early writes weights.
+    for (int i = 0; i < kDepth && F.live; ++i) feed_issue(a, F, vw, ring, bars, lane, policy);
+    // activations, the workspace and the outputs only after the previous grid
+    // (a no-op without a programmatic launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // chunks of ops whose activations come from outside the batch are
     // converted at launch start, chunk i by virtual warp i; they are claimed
     // like the others, so a warp that reaches an op first converts whatever
@@ -917,19 +935,7 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
         if (lane == 0) won = atomicCAS(a.counters + a.op[k].flag_off + (i - a.op[k].chunk0), 0, 1) == 0;
         if (__shfl_sync(0xffffffffu, won, 0)) prep_chunk<false>(a, k, i - a.op[k].chunk0, lane);
     }
-    Feed F;
-    F.s = 0;
-    F.k = 0;
-    F.slot = 0;
-    F.n = 0;
-    {
-        int gu = 0;
-        F.live = find_range(a, vw, F.s, gu, F.gend);
-        if (!F.live) return;
-        feed_run(a, F, gu);
-    }
-    // prime the ring
-    for (int i = 0; i < kDepth && F.live; ++i) feed_issue(a, F, vw, ring, bars, lane, policy);
+    if (!has_units) return;
 
     Walk Wk;
     Wk.slot = 0;
@@ -1021,9 +1027,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ 
     C.err = reinterpret_cast<int*>(a.ws);
     C.abort = reinterpret_cast<volatile int*>(a.ws + kCtlAbort);
     C.seg_done = reinterpret_cast<int*>(a.ws + kCtlSegDone);
-    if (threadIdx.x == 0) {
-        s_abort = 0;
-        for (int i = 0; i < kCW * kDepth; ++i) mbar_init(smem_u32(full + i), 1);
+    // the next launch of the stream may start its prologue now (it waits for
+    // this grid before it touches anything but its weights)
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;");
+    if (threadIdx.x == 0) s_abort = 0;
+    if (lane == 0) {
+        for (int i = 0; i < kDepth; ++i) mbar_init(smem_u32(full + warp * kDepth + i), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
@@ -1074,8 +1083,11 @@ int sm_count(int dev) {
 
 std::mutex g_mu;
 
+// cooperative: the batch has several segments, whose waits need every CTA
+// resident; otherwise a programmatic launch, which may overlap the previous
+// kernel's tail
 template <int NTB>
-int launch(const Args& a, int grid, cudaStream_t s) {
+int launch(const Args& a, int grid, cudaStream_t s, bool cooperative) {
     int dev = 0;
     cudaGetDevice(&dev);
     {
@@ -1094,8 +1106,13 @@ int launch(const Args& a, int grid, cudaStream_t s) {
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
+    if (cooperative) {
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+    } else {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+    }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, k_stream<NTB>, a);
@@ -1274,7 +1291,8 @@ size_t stream_scratch_single(int64_t M, int64_t ic) {
 
 int stream_launch(const StreamPlan& P, cudaStream_t s) {
     const stream::Args& a = P.args;
-    return a.M <= 8 ? stream::launch<1>(a, P.grid, s) : stream::launch<2>(a, P.grid, s);
+    const bool coop = a.n_seg > 1;
+    return a.M <= 8 ? stream::launch<1>(a, P.grid, s, coop) : stream::launch<2>(a, P.grid, s, coop);
 }
 
 }  // namespace spark
