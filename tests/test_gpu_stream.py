@@ -255,3 +255,21 @@ def test_batch_mixed_paths():
         fin = torch.isfinite(one).cpu().numpy()
         assert np.abs(op.y.cpu().numpy()[fin] - y64[fin]).max() <= TOL
     ops().check_device_errors()
+
+
+def test_weights_rewritten_in_place_before_the_call():
+    """Tile new weights into the SAME buffer and call the linear right after,
+    with nothing in between on the stream: the call must see the new weights
+    (its weight prefetch runs before it waits for the previous kernel)."""
+    from spark_b200 import ops as O2, _lib
+    oc, ic = 1024, 2560
+    wq_a, _, wt, dec_a = make("spfp2", oc, ic, seed=71)
+    wq_b, _, _, dec_b = make("spfp2", oc, ic, seed=72)
+    x = torch.randn(1, ic).bfloat16().cuda()
+    y = torch.empty(1, oc, dtype=torch.float32, device="cuda")
+    f = O2.FORMATS["spfp2"]
+    for wq, dec in ((wq_b, dec_b), (wq_a, dec_a), (wq_b, dec_b)):
+        _lib.call("spark_tile_weights", f, O2._p(O2._bytes(wq)), None, oc, ic, O2._p(wt), O2._stream(wt))
+        O2.linear("spfp2", wt, None, x, oc, ic, out=y, tiled=True)
+        torch.cuda.synchronize()
+        assert np.abs(y.cpu().numpy() - ref(x, dec)).max() <= TOL
