@@ -22,7 +22,9 @@ step time is the max over ranks.  The same line carries `tp_mlp`: BASELINE
 config 4 (a 32-layer SPFP2 MLP stack at 64 tokens) tensor-parallel over the N
 ranks (gate/up column-split, down row-split, one NCCL all-reduce of fp32
 partials per layer), with a parity check of a 2-layer slice against an fp64
-evaluation of the unsharded weights.  `--impl reference` times the
+evaluation of the unsharded weights, and `tp_decode`: the same stack at 8
+decode tokens, NCCL form against one launch per layer with the all-reduce
+inside the kernel (spark_linear_batch_ar).  `--impl reference` times the
 reference's CPU path (decode + fp32 matmul per call, ported to C in oracle/)
 on the host cores.
 """
@@ -462,6 +464,7 @@ def run_gpu(args, rank, world, local):
 
     # ---------------- BASELINE config 4, tensor-parallel over the ranks of this run
     tp = tp_mlp_measure(args, rank, world, local)
+    tp_dec = tp_decode_measure(args, rank, world, local)
     clk.__exit__(None, None, None)
     pre_flops = sum(2.0 * PREFILL_M * oc * ic for _, _, oc, ic in SHAPES)
     pre_tflops = world * pre_flops * pre_steps / (ms_pre * 1e-3) / 1e12
@@ -509,6 +512,7 @@ def run_gpu(args, rank, world, local):
                           "note": "the same calls dispatched from Python every step"}},
         "clocks": clk.summary(),
         "tp_mlp": tp,
+        "tp_decode": tp_dec,
         "prefill": {
             "workload": f"BASELINE config 3: M={PREFILL_M} bf16 tokens through the 7 linears of one layer "
                         "(SPFP2 gate/up/down, FP3 q/k/v, NVFP4 out_proj) as 4 row-merged launches (q|k|v, "
@@ -677,12 +681,13 @@ def run_reference(args, rank, world):
 TP_LAYERS, TP_H, TP_I, TP_M = 32, 4096, 12288, 64
 
 
-def _tp_stack(rank, world, device, peer=None, keep_full=0):
-    """The config-4 stack as TPMLP layers of this rank, and (keep_full > 0) the
-    first keep_full layers' unsharded weights decoded from their SPFP2 packing
-    (the GPU unpack, bit-exact against the reference emulator) in fp64."""
+def _tp_stack(rank, world, device, peer=None, keep_full=0, fused=None):
+    """The config-4 stack as TPMLP layers of this rank (TPMLPFused layers sharing
+    the BatchAllReduce `fused`, when given), and (keep_full > 0) the first
+    keep_full layers' unsharded weights decoded from their SPFP2 packing (the
+    GPU unpack, bit-exact against the reference emulator) in fp64."""
     from spark_b200 import ops
-    from spark_b200.tp import TPMLP
+    from spark_b200.tp import TPMLP, TPMLPFused
     g = torch.Generator(device=device)
     layers, full = [], []
     for li in range(TP_LAYERS):
@@ -690,7 +695,8 @@ def _tp_stack(rank, world, device, peer=None, keep_full=0):
         gate = torch.randn(TP_I, TP_H, device=device, generator=g) * 0.015
         up = torch.randn(TP_I, TP_H, device=device, generator=g) * 0.015
         down = torch.randn(TP_H, TP_I, device=device, generator=g) * 0.015
-        layers.append(TPMLP(gate, up, down, rank, world, peer=peer))
+        layers.append(TPMLPFused(gate, up, down, rank, world, ar=fused) if fused is not None else
+                      TPMLP(gate, up, down, rank, world, peer=peer))
         if li < keep_full:
             full.append(tuple(ops.spfp2_unpack(ops.spfp2_pack(w)[0], w.numel()).view(w.shape).double()
                               for w in (gate, up, down)))
@@ -835,6 +841,69 @@ def tp_mlp_measure(args, rank, world, local):
                                   "row-parallel + " + ("one-shot peer all-reduce (spark_peer_allreduce)"
                                                        if peer is not None else "NCCL all-reduce")
                                   + " of fp32 partials", "graph": bool(args.tp_graph)},
+    }
+
+
+TP_DEC_M = 8      # decode tokens of the in-kernel all-reduce comparison
+
+
+def tp_decode_measure(args, rank, world, local):
+    """The config-4 stack's layers at decode size (TP_DEC_M bf16 tokens),
+    tensor-parallel over the ranks two ways: TPMLP (per layer a gate|up
+    launch, a SiLU launch, a down launch and an NCCL all-reduce of the fp32
+    partials) and TPMLPFused (ONE launch per layer: gate|up with the SiLU
+    epilogue, then the down projection, whose partials are summed over the
+    ranks inside the same kernel over peer memory).  Both replay as CUDA
+    graphs.  Parity: rank 0's output of the fused layers 0-1 against
+    _tp_reference of the unsharded weights, with tp_mlp's bound."""
+    import math
+    from spark_b200 import ops
+    from spark_b200.tp import BatchAllReduce
+    device = torch.device("cuda", local)
+    g = torch.Generator(device=device).manual_seed(5)
+    x0 = torch.randn(TP_DEC_M, TP_H, device=device, generator=g).bfloat16()
+    stream = torch.cuda.Stream(device)
+    k = max(50, args.steps // 5)
+    ar = BatchAllReduce(TP_H, TP_DEC_M)
+    out, parity = {}, None
+    for kind in ("fused", "nccl"):
+        layers, full = _tp_stack(rank, world, device, keep_full=2 if rank == 0 and kind == "fused" else 0,
+                                 fused=ar if kind == "fused" else None)
+        if kind == "fused":
+            with torch.cuda.stream(stream):
+                y2 = layers[1](layers[0](x0))
+            torch.cuda.synchronize()
+            if rank == 0:
+                ref = _tp_reference(x0, full)
+                err = float((y2.double() - ref).abs().max().item())
+                ymax = float(ref.abs().max().item())
+                tol = 2.0 ** (math.floor(math.log2(max(ymax, 2.0 ** -20))) - 6)
+                parity = {"layers": 2, "max_abs": err, "bound": tol, "ok": bool(err <= tol), "max_abs_ref": ymax}
+            del full, y2
+        ms, finite = _time_stack(layers, x0, stream, args.warmup, k, world)
+        out[kind] = {"ms_per_step": round(ms, 4), "finite": finite,
+                     "gpu_launches_per_step": TP_LAYERS * (1 if kind == "fused" else 3)}
+        ops.check_device_errors()
+        barrier(world)
+        del layers
+        torch.cuda.empty_cache()
+    ar.check()
+    ar.close()
+    packed_total = TP_LAYERS * 3 * (TP_I * TP_H // 16 * 5)
+    peak, peak_kind = peaks()
+    for kind, d in out.items():
+        per_gpu = packed_total / world / (d["ms_per_step"] * 1e-3) / 1e9
+        d["tokens_per_s"] = round(TP_DEC_M / (d["ms_per_step"] * 1e-3), 1)
+        d["roofline"] = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s per GPU",
+                         "frac": round(per_gpu / peak, 4), "peak_source": peak_kind}
+    return {
+        "workload": f"the config-4 stack (32 x SPFP2 gate/up [12288,4096], down [4096,12288]) at {TP_DEC_M} "
+                    f"decode tokens, tp{world}", "tp": world, "steps": k,
+        "fused": {**out["fused"], "path": "TPMLPFused: one spark_linear_batch_ar launch per layer, the down "
+                                          "projection's all-reduce inside the kernel (peer stores + flags)"},
+        "nccl": {**out["nccl"], "path": "TPMLP: row-merged gate|up, SiLU, down launches + NCCL all-reduce"},
+        "speedup_fused_vs_nccl": round(out["nccl"]["ms_per_step"] / out["fused"]["ms_per_step"], 3),
+        "parity": parity,
     }
 
 

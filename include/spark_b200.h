@@ -252,10 +252,46 @@ SPARK_API int spark_linear_chain(const SparkChainOp* ops, int n_ops, int64_t M, 
  * workspace: spark_linear_batch_workspace_size(ops, n_ops, M) bytes, 256-byte
  * aligned, zero-filled before its first use (it may be shared with
  * spark_linear calls on the same stream); launches that share it must not
- * overlap on the GPU.  The launch is cooperative (one CTA per SM). */
+ * overlap on the GPU.  One CTA per SM: a cooperative launch when the batch
+ * has dependencies, otherwise a programmatic one (it prefetches its first
+ * weights while the previous kernel of the stream finishes). */
 SPARK_API size_t spark_linear_batch_workspace_size(const SparkChainOp* ops, int n_ops, int64_t M);
 SPARK_API int spark_linear_batch(const SparkChainOp* ops, int n_ops, int64_t M, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* spark_linear_batch with the all-reduce of one op fused into its epilogue:
+ * op ar->op is a row-parallel linear (this rank holds a slice of its input
+ * features, its output is a partial sum), e.g. the down projection of a
+ * tensor-parallel MLP.  Inside the same launch, each warp that finished row
+ * groups of the op stores their fp32 partials into every rank's receive
+ * buffer over peer memory and publishes them (release flags, system scope),
+ * then waits (bounded, 2 s) for every rank's partials of those row groups,
+ * sums them in rank order 0..W-1 and writes y (+ bias): every rank gets the
+ * same bits, with no separate all-reduce launch.
+ * Replaces the NCCL all-reduce after the row-parallel projection.
+ *   recv[r]:  rank r's receive buffer, spark_batch_ar_recv_floats(world, M, oc)
+ *             fp32 (mapped into this process, e.g. spark_ipc_open);
+ *   flags[r]: rank r's flag array, spark_batch_ar_flags_count(world, oc) ints,
+ *             zero before the first call (the last int counts this rank's calls).
+ * Every rank makes the same sequence of calls (CUDA graphs included) with the
+ * same op shapes; the op may not use SPARK_EPILOGUE_SILU and no other op of
+ * the batch may read its output (SPARK_ERR_UNSUPPORTED); M <= 16; 1 to
+ * SPARK_MAX_PEERS ranks (the two size helpers return 0 outside).  A peer that does not arrive in
+ * 2 s sets the workspace error word (spark_workspace_check).  workspace:
+ * spark_linear_batch_ar_workspace_size(ops, n_ops, M, ar) bytes (ar's buffers
+ * may be null for that query). */
+typedef struct {
+    int op;
+    int world, rank;
+    float* const* recv;
+    int* const* flags;
+} SparkBatchAllReduce;
+SPARK_API size_t spark_linear_batch_ar_workspace_size(const SparkChainOp* ops, int n_ops, int64_t M,
+                                                      const SparkBatchAllReduce* ar);
+SPARK_API int64_t spark_batch_ar_recv_floats(int world, int64_t M, int64_t oc);
+SPARK_API int64_t spark_batch_ar_flags_count(int world, int64_t oc);
+SPARK_API int spark_linear_batch_ar(const SparkChainOp* ops, int n_ops, int64_t M, const SparkBatchAllReduce* ar,
+                                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* Fragment-major copy of a packed weight for spark_linear(fmt | SPARK_LAYOUT_TILED):
  * the same bytes (codes and, for FP3/NVFP4, scales) permuted so every thread of the

@@ -39,6 +39,12 @@ class SparkChainOp(ctypes.Structure):
                 ("y", ctypes.c_void_p), ("y_dtype", ctypes.c_int), ("ldy", ctypes.c_int64), ("dep", ctypes.c_int * 2)]
 
 
+class SparkBatchAllReduce(ctypes.Structure):
+    """struct SparkBatchAllReduce of include/spark_b200.h."""
+    _fields_ = [("op", ctypes.c_int), ("world", ctypes.c_int), ("rank", ctypes.c_int),
+                ("recv", ctypes.c_void_p), ("flags", ctypes.c_void_p)]
+
+
 class SparkError(RuntimeError):
     """A C-ABI call returned a non-zero status."""
 
@@ -81,6 +87,10 @@ _SIGNATURES = {
                                    _i64, _p]),
     "spark_linear_batch_workspace_size": (_sz, [_p, _i, _i64]),
     "spark_linear_batch": (_i, [_p, _i, _i64, _p, _sz, _p]),
+    "spark_linear_batch_ar_workspace_size": (_sz, [_p, _i, _i64, _p]),
+    "spark_batch_ar_recv_floats": (_i64, [_i, _i64, _i64]),
+    "spark_batch_ar_flags_count": (_i64, [_i, _i64]),
+    "spark_linear_batch_ar": (_i, [_p, _i, _i64, _p, _p, _sz, _p]),
     "spark_linear_chain_workspace_size": (_sz, [_i]),
     "spark_linear_chain": (_i, [_p, _i, _i64, _p, _sz, _p]),
     "spark_linear_noalloc": (_i, [_i, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p]),

@@ -1381,6 +1381,7 @@ size_t stream_plan_scratch(const StreamPlan* P);
 int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size_t counters_off,
                 int64_t max_counters, size_t scratch_off, StreamPlan* P);
 int stream_launch(const StreamPlan& P, cudaStream_t s);
+int stream_plan_set_ar(StreamPlan* P, const SparkBatchAllReduce* ar);
 size_t stream_scratch_single(int64_t M, int64_t ic);
 size_t tc_partials_bytes(int dev, int64_t M);
 bool tc_linear_ok(int fmt, const void* wq, const void* scales, const void* x, int x_dtype, int64_t ic,
@@ -1646,6 +1647,75 @@ int spark_linear_batch(const SparkChainOp* ops, int n_ops, int64_t M, void* work
     rc = stream_plan(ops, n_ops, M, static_cast<uint8_t*>(workspace), L.counters, kMaxRowGroups, L.partials, P);
     if (rc == SPARK_OK && L.partials + stream_plan_scratch(P) > workspace_bytes)
         rc = set_error(SPARK_ERR_WORKSPACE, "spark_linear_batch: workspace of %zu bytes needed (got %zu)",
+                       L.partials + stream_plan_scratch(P), workspace_bytes);
+    if (rc == SPARK_OK) rc = stream_launch(*P, reinterpret_cast<cudaStream_t>(stream));
+    stream_plan_free(P);
+    return rc;
+}
+
+int64_t spark_batch_ar_recv_floats(int world, int64_t M, int64_t oc) {
+    if (world < 1 || world > SPARK_MAX_PEERS || M < 1 || M > 16 || oc < 1) return 0;
+    return (int64_t)2 * world * ((oc + 15) / 16) * M * 16;
+}
+
+int64_t spark_batch_ar_flags_count(int world, int64_t oc) {
+    if (world < 1 || world > SPARK_MAX_PEERS || oc < 1) return 0;
+    return (int64_t)world * ((oc + 15) / 16) + 1;
+}
+
+}  // extern "C"
+
+// The host-side checks of the all-reduce arguments that need no device.
+static int check_batch_ar(const SparkChainOp* ops, int n_ops, const SparkBatchAllReduce* ar) {
+    SPARK_REQUIRE(ar, SPARK_ERR_INVALID, "spark_linear_batch_ar: null all-reduce arguments");
+    SPARK_REQUIRE(ar->world >= 1 && ar->world <= SPARK_MAX_PEERS && ar->rank >= 0 && ar->rank < ar->world,
+                  SPARK_ERR_INVALID, "spark_linear_batch_ar: rank %d of %d (1 to %d ranks)", ar->rank, ar->world,
+                  SPARK_MAX_PEERS);
+    SPARK_REQUIRE(ops && ar->op >= 0 && ar->op < n_ops, SPARK_ERR_INVALID,
+                  "spark_linear_batch_ar: op %d not in the batch", ar->op);
+    // the summed output is written after the op's units complete, so no op
+    // of the same launch can wait for it
+    for (int k = 0; k < n_ops; ++k)
+        SPARK_REQUIRE(ops[k].dep[0] != ar->op && ops[k].dep[1] != ar->op, SPARK_ERR_UNSUPPORTED,
+                      "spark_linear_batch_ar: op %d reads the all-reduced op %d; run it in a later launch", k,
+                      ar->op);
+    return SPARK_OK;
+}
+
+extern "C" {
+
+size_t spark_linear_batch_ar_workspace_size(const SparkChainOp* ops, int n_ops, int64_t M,
+                                            const SparkBatchAllReduce* ar) {
+    if (check_batch_ar(ops, n_ops, ar) != SPARK_OK) return 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const WsLayout L = ws_layout(0, max_warps(dev));
+    StreamPlan* P = nullptr;
+    if (stream_plan_alloc(&P)) return 0;
+    size_t need = 0;
+    if (stream_plan(ops, n_ops, M, nullptr, L.counters, kMaxRowGroups, L.partials, P) == SPARK_OK &&
+        stream_plan_set_ar(P, ar) == SPARK_OK)
+        need = (L.partials + stream_plan_scratch(P) + 255) / 256 * 256;
+    stream_plan_free(P);
+    return need;
+}
+
+int spark_linear_batch_ar(const SparkChainOp* ops, int n_ops, int64_t M, const SparkBatchAllReduce* ar,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const WsLayout L = ws_layout(0, max_warps(dev));
+    SPARK_REQUIRE(workspace && aligned(workspace, 256), SPARK_ERR_WORKSPACE,
+                  "spark_linear_batch_ar: a 256-byte aligned workspace is required");
+    int rc = check_batch_ar(ops, n_ops, ar);
+    if (rc) return rc;
+    StreamPlan* P = nullptr;
+    rc = stream_plan_alloc(&P);
+    if (rc) return rc;
+    rc = stream_plan(ops, n_ops, M, static_cast<uint8_t*>(workspace), L.counters, kMaxRowGroups, L.partials, P);
+    if (rc == SPARK_OK) rc = stream_plan_set_ar(P, ar);
+    if (rc == SPARK_OK && L.partials + stream_plan_scratch(P) > workspace_bytes)
+        rc = set_error(SPARK_ERR_WORKSPACE, "spark_linear_batch_ar: workspace of %zu bytes needed (got %zu)",
                        L.partials + stream_plan_scratch(P), workspace_bytes);
     if (rc == SPARK_OK) rc = stream_launch(*P, reinterpret_cast<cudaStream_t>(stream));
     stream_plan_free(P);

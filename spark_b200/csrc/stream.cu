@@ -76,6 +76,7 @@ struct Op {
     int dseg0, dseg1, y_dtype, bias_dtype;   // dseg: segments whose completion the op's input needs (-1: none)
     int silu, f16, flag_off, chunk0;  // f16: the f16 path; flag_off: the op's chunk flags in the counters;
                                       // chunk0: its first chunk in the batch's converted-activation arrays
+    int pad3, pad4, pad5, pad6;
 };
 
 // A segment: ops k0..k1-1, units [ub, ub + units) of the sequence, split over
@@ -98,6 +99,17 @@ struct Args {
     int64_t part_stride;     // floats per area: T * 2 * M * 16
     float* xinv;             // [chunk][16]: 1 / sigma per token
     uint16_t* xh;            // [chunk][M][256]: f16 activations times sigma
+    // the fused all-reduce of one op (ar_world = 0: none): every rank's
+    // receive buffer [2][world][ar_nrg][M][16] fp32 and flag array
+    // [world][ar_nrg] (+ this rank's call count), as this process maps them
+    float* ar_recv[SPARK_MAX_PEERS];
+    int* ar_flags[SPARK_MAX_PEERS];
+    int ar_world, ar_rank, ar_nrg, ar_op;
+    float* ar_local;         // the op's rank-local sums [M][ar_nrg * 16] (the op's y during the launch)
+    void* ar_y;              // the op's real output, bias and dtypes
+    const void* ar_bias;
+    int64_t ar_ldy;
+    int ar_oc, ar_y_dtype, ar_bias_dtype, pad2;
 };
 
 constexpr size_t kXhBudget = (size_t)8 << 20;   // converted activations of a batch's f16 ops
@@ -483,6 +495,117 @@ struct Ctl {
     int* seg_done;
 };
 
+// ---------------------------------------------------------------- fused all-reduce
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait (one thread) until a flag another GPU writes reaches `target`.
+__device__ bool wait_peer(const int* p, int target, const Ctl& C) {
+    if (ld_acquire_sys(p) >= target) return true;
+    const uint64_t dl = globaltimer_ns() + kWaitNs;
+    while (true) {
+        __nanosleep(64);
+        if (ld_acquire_sys(p) >= target) return true;
+        if (*C.abort) return false;
+        if (globaltimer_ns() > dl) {
+            report_device_error(C.err, 5);
+            *C.abort = 1;
+            return false;
+        }
+    }
+}
+
+// All-reduce of one finished row group over the ranks, in two halves.
+// ar_publish: this lane's values val[e] (token mm[e], row rr[e] of the group,
+// valid ok[e]) into every rank's receive slot for (this rank, rg), then a
+// release flag per rank.  ar_collect: once every rank's flag for rg is up,
+// val[e] becomes the sum over ranks 0..W-1 in that order (this rank's own term
+// from registers: the same bits the others read).  Slots alternate by call
+// parity; a rank reuses a slot two calls later only after every rank has
+// published (and so finished reading) the call in between.
+__device__ __forceinline__ int ar_epoch(const Args& a) {
+    // this call's number: the calls this rank made before it, + 1
+    return *reinterpret_cast<volatile int*>(a.ar_flags[a.ar_rank] + a.ar_world * a.ar_nrg) + 1;
+}
+template <int NE>
+__device__ void ar_publish(const Args& a, int rg, const int (&mm)[NE], const int (&rr)[NE], const float (&val)[NE],
+                           const bool (&ok)[NE], int lane) {
+    const int W = a.ar_world, R = a.ar_rank, nrg = a.ar_nrg, M = a.M;
+    const int epoch = ar_epoch(a);
+    const int64_t stride = (int64_t)nrg * M * 16;                             // one rank's slots
+    const int64_t off = ((int64_t)(epoch & 1) * W * nrg + rg) * M * 16;       // (parity, rank 0, rg)
+    for (int p = 0; p < W; ++p) {
+        float* dst = a.ar_recv[p] + off + R * stride;
+#pragma unroll
+        for (int e = 0; e < NE; ++e)
+            if (ok[e]) __stcg(dst + mm[e] * 16 + rr[e], val[e]);
+    }
+    __syncwarp();                     // every lane's stores before the releases
+    if (lane < W) st_release_sys(a.ar_flags[lane] + R * nrg + rg, epoch);
+}
+template <int NE>
+__device__ bool ar_collect(const Args& a, const Ctl& C, int rg, const int (&mm)[NE], const int (&rr)[NE],
+                           float (&val)[NE], const bool (&ok)[NE], int lane) {
+    const int W = a.ar_world, R = a.ar_rank, nrg = a.ar_nrg, M = a.M;
+    const int epoch = ar_epoch(a);
+    const int64_t stride = (int64_t)nrg * M * 16;
+    const int64_t off = ((int64_t)(epoch & 1) * W * nrg + rg) * M * 16;
+    bool good = true;
+    if (lane < W && lane != R) good = wait_peer(a.ar_flags[R] + lane * nrg + rg, epoch, C);
+    if (!__all_sync(0xffffffffu, good)) return false;
+    const float* base = a.ar_recv[R] + off;
+#pragma unroll
+    for (int e = 0; e < NE; ++e) {
+        if (!ok[e]) continue;
+        float sum = 0.0f;
+        for (int r = 0; r < W; ++r) sum += r == R ? val[e] : __ldcg(base + r * stride + mm[e] * 16 + rr[e]);
+        val[e] = sum;
+    }
+    return true;
+}
+
+// The exchange of the all-reduced op, after this warp's units of it: the op
+// itself wrote this rank's sums (fp32, no bias) to the local buffer ar_local
+// ([M][ar_nrg * 16]); the row groups r_lo..r_hi are the ones this warp
+// finished (their first unit lies in its range).  All are published first,
+// then each is summed over the ranks and written to the op's real output.
+__device__ __noinline__ void ar_pass(const Args& a, const Ctl& C, int r_lo, int r_hi, int lane) {
+    const int M = a.M, ld = a.ar_nrg * 16;
+    __syncwarp();                     // this warp's own row writes before its reads
+    const int row = lane & 15;
+    constexpr int NE = 8;
+    for (int pass = 0; pass < 2; ++pass)
+        for (int rg = r_lo; rg <= r_hi; ++rg) {
+            int mm[NE], rr[NE];
+            float val[NE];
+            bool ok[NE];
+#pragma unroll
+            for (int i = 0; i < NE; ++i) {
+                mm[i] = (lane >> 4) + 2 * i;
+                rr[i] = row;
+                ok[i] = mm[i] < M;
+                val[i] = ok[i] ? __ldcg(a.ar_local + (int64_t)mm[i] * ld + rg * 16 + row) : 0.0f;
+            }
+            if (pass == 0) {
+                ar_publish<NE>(a, rg, mm, rr, val, ok, lane);
+                continue;
+            }
+            if (!ar_collect<NE>(a, C, rg, mm, rr, val, ok, lane)) return;
+            const int64_t r = (int64_t)rg * 16 + row;
+#pragma unroll
+            for (int i = 0; i < NE; ++i) {
+                if (!ok[i] || r >= a.ar_oc) continue;
+                const float b = a.ar_bias ? load_as_float(a.ar_bias, a.ar_bias_dtype, r) : 0.0f;
+                store_from_float(a.ar_y, a.ar_y_dtype, (int64_t)mm[i] * a.ar_ldy + r, val[i] + b);
+            }
+        }
+}
+
 // Row-group values are held as v[2j + i][r] = row g (r = 0) / g + 8 (r = 1)
 // of token 8j + 2t + i.  write_rows writes a whole row group; flush_partial
 // publishes the partial of a shared one.  The first contributor (the warp
@@ -864,6 +987,8 @@ __device__ __forceinline__ void run_units(const Args& a, const Ctl& C, Feed& F, 
                     vals[2 * j + i][0] = acc[0][j][i] + acc[1][j][i];
                     vals[2 * j + i][1] = acc[0][j][2 + i] + acc[1][j][2 + i];
                 }
+            // an all-reduced op's row groups all go through flush_partial (a warp
+            // that holds a whole row group is its own finisher there)
             if (kc == n_kc - 1 && seg0 == op.ub + rg * n_kc)
                 write_rows<2 * NTB>(op, M, rg, vals, lane);
             else
@@ -987,6 +1112,11 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
             else
                 run_op<NTB, false, false>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring, bars,
                                           s_abort, pair_nv, scale_tab, lane, policy);
+            if (k == a.ar_op && a.ar_world > 0 && !Wk.dead) {
+                // the row groups whose first unit lies in [gu, end)
+                const int r_lo = (gu - op.ub + op.n_kc - 1) / op.n_kc, r_hi = (end - 1 - op.ub) / op.n_kc;
+                if (r_lo <= r_hi) ar_pass(a, C, r_lo, r_hi, lane);
+            }
             gu = end;
             if (gu < gend) ++k;
         }
@@ -1064,6 +1194,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ 
         for (int i = (aborted ? 0 : a.n_cnt) + threadIdx.x; i < a.n_cnt_all; i += blockDim.x) a.counters[i] = 0;
         __syncthreads();
         if (threadIdx.x == 0) {
+            // this rank's count of fused all-reduce calls (the next call's number - 1)
+            if (a.ar_world > 0) a.ar_flags[a.ar_rank][a.ar_world * a.ar_nrg] += 1;
             *C.abort = 0;
             __threadfence();
             *reinterpret_cast<volatile int*>(a.ws + kCtlCtaDone) = 0;
@@ -1129,6 +1261,7 @@ int launch(const Args& a, int grid, cudaStream_t s, bool cooperative) {
 struct StreamPlan {
     stream::Args args;
     size_t scratch_bytes = 0;   // bytes needed from scratch_off
+    uint8_t* scratch = nullptr; // ws + scratch_off (null for a size query)
     int grid = 0;
 };
 
@@ -1259,12 +1392,58 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
     P->scratch_bytes = xh_off + (size_t)chunks * 512 * M;
     P->grid = G;
     a.ws = ws;
+    P->scratch = ws ? ws + scratch_off : nullptr;
     if (ws) {
         a.counters = reinterpret_cast<int*>(ws + counters_off);
         a.partials = reinterpret_cast<float*>(ws + scratch_off);
         a.xinv = reinterpret_cast<float*>(ws + scratch_off + inv_off);
         a.xh = reinterpret_cast<uint16_t*>(ws + scratch_off + xh_off);
     }
+    return SPARK_OK;
+}
+
+// The fused all-reduce of one op of a planned batch (spark_linear_batch_ar):
+// the op writes this rank's sums (fp32, no bias) to a scratch buffer, which
+// the kernel then exchanges; its real output, bias and dtypes move to Args.
+// ar may hold null buffers for a size query.
+int stream_plan_set_ar(StreamPlan* P, const SparkBatchAllReduce* ar) {
+    using namespace stream;
+    Args& a = P->args;
+    SPARK_REQUIRE(ar, SPARK_ERR_INVALID, "spark_linear_batch_ar: null all-reduce arguments");
+    SPARK_REQUIRE(ar->world >= 1 && ar->world <= SPARK_MAX_PEERS && ar->rank >= 0 && ar->rank < ar->world,
+                  SPARK_ERR_INVALID, "spark_linear_batch_ar: rank %d of %d (1 to %d ranks)", ar->rank, ar->world,
+                  SPARK_MAX_PEERS);
+    SPARK_REQUIRE(ar->op >= 0 && ar->op < a.n_ops, SPARK_ERR_INVALID, "spark_linear_batch_ar: op %d not in the batch",
+                  ar->op);
+    Op& op = a.op[ar->op];
+    SPARK_REQUIRE(!op.silu, SPARK_ERR_UNSUPPORTED, "spark_linear_batch_ar: the all-reduced op cannot fuse SiLU");
+    const int nrg = (op.oc + 15) / 16;
+    const size_t local_off = (P->scratch_bytes + 255) / 256 * 256;
+    P->scratch_bytes = local_off + (size_t)a.M * nrg * 16 * sizeof(float);
+    if (!P->scratch) return SPARK_OK;
+    SPARK_REQUIRE(ar->recv && ar->flags, SPARK_ERR_INVALID, "spark_linear_batch_ar: null all-reduce buffers");
+    for (int r = 0; r < ar->world; ++r)
+        SPARK_REQUIRE(ar->recv[r] && ar->flags[r] && aligned(ar->recv[r], 16) && aligned(ar->flags[r], 4),
+                      SPARK_ERR_INVALID, "spark_linear_batch_ar: rank %d's buffers missing or misaligned", r);
+    for (int r = 0; r < ar->world; ++r) {
+        a.ar_recv[r] = ar->recv[r];
+        a.ar_flags[r] = ar->flags[r];
+    }
+    a.ar_world = ar->world;
+    a.ar_rank = ar->rank;
+    a.ar_nrg = nrg;
+    a.ar_op = ar->op;
+    a.ar_local = reinterpret_cast<float*>(P->scratch + local_off);
+    a.ar_y = op.y;
+    a.ar_bias = op.bias;
+    a.ar_ldy = op.ldy;
+    a.ar_oc = op.oc;
+    a.ar_y_dtype = op.y_dtype;
+    a.ar_bias_dtype = op.bias_dtype;
+    op.y = a.ar_local;
+    op.bias = nullptr;
+    op.ldy = (int64_t)nrg * 16;
+    op.y_dtype = SPARK_DTYPE_F32;
     return SPARK_OK;
 }
 

@@ -68,6 +68,37 @@ def _ipc_unmap(handle: bytes) -> None:
         del _IPC_MAPS[handle]
 
 
+def _share(tensors: list[torch.Tensor], rank: int, world: int, group=None) -> tuple[list[list[int]], list[bytes]]:
+    """Exchange the CUDA IPC handles of this rank's `tensors` over the group and
+    map every other rank's: returns, per tensor, the device address of every
+    rank's copy (this rank's own pointer at index `rank`) and the handles
+    opened (to _ipc_unmap on close)."""
+    import ctypes
+    from . import _lib
+
+    def handle(t):
+        h = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_int64(0)
+        _lib.call("spark_ipc_handle", ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off))
+        return bytes(h), off.value
+
+    mine = [handle(t) for t in tensors]
+    every = [mine]
+    if world > 1:
+        every = [None] * world
+        dist.all_gather_object(every, mine, group=group)
+    ptrs: list[list[int]] = [[] for _ in tensors]
+    opened: list[bytes] = []
+    for r, theirs in enumerate(every):
+        for i, (h, off) in enumerate(theirs):
+            if r == rank:
+                ptrs[i].append(tensors[i].data_ptr())
+                continue
+            ptrs[i].append(_ipc_map(h) + off)
+            opened.append(h)
+    return ptrs, opened
+
+
 class PeerAllReduce:
     """One-shot all-reduce of per-rank partial sums over peer memory
     (spark_peer_allreduce): the NCCL all-reduce after the row-parallel down
@@ -100,28 +131,7 @@ class PeerAllReduce:
         self.epochs = torch.zeros(L.spark_peer_flags_count(1), dtype=torch.int32, device=dev)
         self.err = torch.zeros(64, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
-
-        def handle(t):
-            h = (ctypes.c_uint8 * 64)()
-            off = ctypes.c_int64(0)
-            _lib.call("spark_ipc_handle", ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off))
-            return bytes(h), off.value
-
-        mine = (handle(self.local), handle(self.flags))
-        every = [mine]
-        if self.world > 1:
-            every = [None] * self.world
-            dist.all_gather_object(every, mine, group=group)
-        self._opened = []
-        bufs, flags = [], []
-        for r, ((hb, ob), (hf, of)) in enumerate(every):
-            if r == self.rank:
-                bufs.append(self.local.data_ptr())
-                flags.append(self.flags.data_ptr())
-                continue
-            bufs.append(_ipc_map(hb) + ob)
-            flags.append(_ipc_map(hf) + of)
-            self._opened += [hb, hf]
+        (bufs, flags), self._opened = _share([self.local, self.flags], self.rank, self.world, group)
         half = n_pad * self.local.element_size()
         P = ctypes.c_void_p * self.world
         self._bufs = [P(*[b + k * half for b in bufs]) for k in (0, 1)]
@@ -204,6 +214,102 @@ class TPMLP(torch.nn.Module):
         y = d(h, out=torch.empty(h.shape[0], d.out_features, dtype=torch.float32, device=x.device))
         dist.all_reduce(y, group=self.group)
         return y.to(x.dtype)
+
+
+class BatchAllReduce:
+    """The shared buffers of spark_linear_batch_ar: the all-reduce of one op of
+    a batched decode launch (width `oc`, up to `max_tokens` tokens) done
+    inside that launch over peer memory.
+
+    Every rank owns a receive buffer (2 launch parities x ranks x row groups x
+    tokens x 16 fp32) and a flag array (one flag per rank and row group, then
+    the launch counter); their CUDA IPC handles are exchanged once through the
+    process group.  The launch counter lives on the device, so calls can be
+    captured in a CUDA graph and replayed any number of times.  Every rank
+    must make the same sequence of calls, each with the same batch shapes."""
+
+    def __init__(self, oc: int, max_tokens: int = 16, group=None):
+        from . import _lib
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 8:
+            raise ValueError("BatchAllReduce: at most 8 ranks")
+        if not 1 <= max_tokens <= 16:
+            raise ValueError("BatchAllReduce: 1 to 16 tokens")
+        self.oc, self.max_tokens, self._group = oc, max_tokens, group
+        dev = torch.device("cuda", torch.cuda.current_device())
+        L = _lib.lib()
+        self.recv = torch.zeros(L.spark_batch_ar_recv_floats(self.world, max_tokens, oc), dtype=torch.float32,
+                                device=dev)
+        self.flags = torch.zeros(L.spark_batch_ar_flags_count(self.world, oc), dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        (self._recv, self._flags), self._opened = _share([self.recv, self.flags], self.rank, self.world, group)
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def __call__(self, batch: list, op: int, stream=None) -> None:
+        """Run `batch` (ops.BatchOp list) in one launch; op `op`'s y receives the
+        sum over the ranks (fp32, rank order 0..W-1) plus its bias."""
+        from . import ops
+        y, M = batch[op].y, batch[op].x.shape[0]
+        if batch[op].silu or y.shape[1] != self.oc or M > self.max_tokens:
+            raise ValueError(f"BatchAllReduce: op {op} must be a plain linear of width {self.oc} "
+                             f"on at most {self.max_tokens} tokens")
+        ops.linear_batch_allreduce(batch, op, self.world, self.rank, self._recv, self._flags, stream=stream)
+
+    def check(self) -> None:
+        """Raise if a launch gave up waiting for a peer (synchronises)."""
+        from . import ops
+        ops.check_device_errors()
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers (every rank calls it; see PeerAllReduce.close)."""
+        torch.cuda.synchronize()
+        if self.world > 1 and dist.is_initialized():
+            dist.barrier(group=self._group)
+        for h in self._opened:
+            _ipc_unmap(h)
+        self._opened = []
+
+
+class TPMLPFused(torch.nn.Module):
+    """TPMLP in ONE kernel launch: gate|up with the SiLU epilogue, then the
+    row-parallel down projection, whose ranks' fp32 partials are summed inside
+    the same launch over peer memory (BatchAllReduce): no NCCL call and no
+    separate all-reduce kernel.  Decode sizes: bf16 x [M, H], M <= max_tokens."""
+
+    def __init__(self, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor, rank: int = 0, world: int = 1,
+                 group=None, max_tokens: int = 16, fmt: str = "spfp2", ar: BatchAllReduce | None = None):
+        """ar: a BatchAllReduce of width hidden shared with other layers (the
+        calls run one after another on a stream); by default the layer owns one."""
+        super().__init__()
+        from . import ops
+        from .inference_v3 import V3GateUpSiLU, V3PackedLinear
+
+        def packed(w):
+            w = w.contiguous()
+            if fmt == "spfp2":
+                return V3PackedLinear(fmt, ops.spfp2_pack(w)[0], w.shape[0], w.shape[1])
+            c, sc = ops.nvfp4_pack(w) if fmt == "nvfp4" else ops.fp3_pack(w)
+            return V3PackedLinear(fmt, c, w.shape[0], w.shape[1], scales=sc)
+
+        g, u, d = shard_rows(gate, rank, world), shard_rows(up, rank, world), shard_cols(down, rank, world)
+        self.gate_up = V3GateUpSiLU(packed(g), packed(u))
+        self.down = packed(d)
+        self.hidden, self.inter = down.shape[0], g.shape[0]
+        if ar is not None and (ar.oc != self.hidden or ar.world != world):
+            raise ValueError("TPMLPFused: the shared BatchAllReduce has another width or rank count")
+        self.ar = ar if ar is not None else BatchAllReduce(self.hidden, max_tokens, group)
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        from . import ops
+        M = x.shape[0]
+        h = torch.empty(M, self.inter, dtype=torch.bfloat16, device=x.device)
+        y = out if out is not None else torch.empty(M, self.hidden, dtype=x.dtype, device=x.device)
+        gu, dn = self.gate_up.merged, self.down
+        self.ar([ops.BatchOp(gu.fmt, gu.w_tiled, x, h, bias=gu.bias, silu=True),
+                 ops.BatchOp(dn.fmt, dn.w_tiled, h, y, bias=dn.bias, deps=[0])], 1)
+        return y
 
 
 def pack_layers_split(weights: list[torch.Tensor], pack: Callable[[torch.Tensor], torch.Tensor], rank: int,

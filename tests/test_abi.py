@@ -53,3 +53,33 @@ def test_linear_argument_validation():
     assert run(fmt=2) == _lib.ERR_INVALID          # FP3 without scales
     assert run(xd=5) == _lib.ERR_INVALID
     assert run(M=0) == _lib.OK                      # nothing to do
+
+
+def test_batch_allreduce_argument_validation():
+    """spark_linear_batch_ar rejects bad all-reduce arguments on the host,
+    before it plans the launch (no device needed)."""
+    P = ctypes.c_void_p
+    ops = (_lib.SparkChainOp * 2)()
+    for k in range(2):
+        c = ops[k]
+        c.kind, c.fmt, c.wq, c.x, c.ic, c.ldx = _lib.CHAIN_LINEAR, _lib.FMT_SPFP2 | _lib.LAYOUT_TILED, 256, 256, 512, 512
+        c.oc, c.y, c.y_dtype, c.ldy = 256, 256, _lib.DTYPE_BF16, 256
+        c.dep[0] = c.dep[1] = -1
+    ops[1].dep[0] = 0
+    L = _lib.lib()
+
+    def run(op, world, rank):
+        ar = _lib.SparkBatchAllReduce(op, world, rank, None, None)
+        rc = L.spark_linear_batch_ar(ctypes.cast(ops, P), 2, 1, ctypes.byref(ar), P(256), 1 << 20, None)
+        ws = L.spark_linear_batch_ar_workspace_size(ctypes.cast(ops, P), 2, 1, ctypes.byref(ar))
+        return rc, ws
+
+    assert run(1, 9, 0) == (_lib.ERR_INVALID, 0)             # more ranks than peers
+    assert run(1, 2, 2) == (_lib.ERR_INVALID, 0)             # rank out of range
+    assert run(2, 2, 0) == (_lib.ERR_INVALID, 0)             # op not in the batch
+    assert run(0, 2, 0) == (_lib.ERR_UNSUPPORTED, 0)         # a later op reads the summed output
+    assert "later launch" in _lib.last_error()
+    assert L.spark_linear_batch_ar(ctypes.cast(ops, P), 2, 1, None, P(256), 1 << 20, None) == _lib.ERR_INVALID
+    assert L.spark_batch_ar_recv_floats(2, 16, 2560) == 2 * 2 * 160 * 16 * 16
+    assert L.spark_batch_ar_flags_count(2, 2560) == 2 * 160 + 1
+    assert L.spark_batch_ar_recv_floats(0, 16, 2560) == 0 and L.spark_batch_ar_flags_count(9, 16) == 0
