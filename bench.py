@@ -918,6 +918,17 @@ def run_tp_mlp(args, rank, world, local):
         print(json.dumps(line), flush=True)
 
 
+def run_tp_decode(args, rank, world, local):
+    """--tp-decode: the decode-size tensor-parallel comparison alone, its own JSON line."""
+    clk = Clocks(local)
+    clk.__enter__()
+    line = tp_decode_measure(args, rank, world, local)
+    clk.__exit__(None, None, None)
+    line["clocks"] = clk.summary()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 QAT_TOKENS, QAT_H, QAT_I = 8 * 4096, 2560, 9728     # BASELINE config 5 (QAT variant)
 
 
@@ -1106,6 +1117,8 @@ def main():
                     help="profile mode: tiled-layout GEMV, tcgen05 kernel, or reference-layout GEMV")
     ap.add_argument("--copies", type=int, default=0, help="profile mode: weight copies to rotate over")
     ap.add_argument("--tp-mlp", action="store_true", help="run the config-4 tensor-parallel MLP stack instead")
+    ap.add_argument("--tp-decode", action="store_true",
+                    help="run the decode-size tensor-parallel stack (fused vs NCCL all-reduce) instead")
     ap.add_argument("--qat", action="store_true", help="run the config-5 QAT fake-quant measurement instead")
     ap.add_argument("--prefetch", action="store_true", help="profile: each launch prefetches the next copy into L2")
     ap.add_argument("--tp-graph", type=int, default=1, help="tp-mlp: replay each step as a CUDA graph")
@@ -1133,6 +1146,8 @@ def main():
     try:
         if args.tp_mlp:
             run_tp_mlp(args, rank, world, local)
+        elif args.tp_decode:
+            run_tp_decode(args, rank, world, local)
         else:
             run_gpu(args, rank, world, local)
     finally:

@@ -74,13 +74,18 @@ struct Op {
     int fmt, oc, n_kc, ub;   // ub: the op's first unit in the batch's sequence
     int units, unit_bytes, cnt_off, seg;
     int dseg0, dseg1, y_dtype, bias_dtype;   // dseg: segments whose completion the op's input needs (-1: none)
-    int silu, f16, flag_off, chunk0;  // f16: the f16 path; flag_off: the op's chunk flags in the counters;
+    int silu, f16, flag_off, chunk0;  // f16: the f16 path; flag_off: the op's chunk flags in the counters
+                                      // (kFlagStride ints apart);
                                       // chunk0: its first chunk in the batch's converted-activation arrays
-    int pad3, pad4, pad5, pad6;
+    int feed, feed_rgs, feed_cnt, fed;   // feed: 1 + the op whose activation chunks this op's rows complete
+                                         // (0: none), feed_rgs row groups per chunk, counters at feed_cnt
+                                         // (kFlagStride apart); fed: this op's chunks come from its producer
 };
 
 // A segment: ops k0..k1-1, units [ub, ub + units) of the sequence, split over
 // T = G * kCW warps: warp v holds q + (v < rem) units from ub + v * q + min(v, rem).
+constexpr int kFlagStride = 32;       // ints between two chunk flags (one 128-byte line each)
+
 struct Seg {
     int ub, units, q, rem;
     int k0, k1, active, waited;   // active: warps with a non-empty range; waited: something waits for it
@@ -246,8 +251,10 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
 __device__ __forceinline__ bool wait_count(const int* p, int target, volatile int* abort, int* err) {
     if (ld_acquire(p) >= target) return true;
     const uint64_t dl = globaltimer_ns() + kWaitNs;
+    unsigned ns = 64;
     while (true) {
-        __nanosleep(64);
+        __nanosleep(ns);
+        ns = min(2 * ns, 1024u);
         if (ld_acquire(p) >= target) return true;
         if (*abort) return false;
         if (globaltimer_ns() > dl) {
@@ -508,8 +515,10 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
 __device__ bool wait_peer(const int* p, int target, const Ctl& C) {
     if (ld_acquire_sys(p) >= target) return true;
     const uint64_t dl = globaltimer_ns() + kWaitNs;
+    unsigned ns = 32;
     while (true) {
-        __nanosleep(64);
+        __nanosleep(ns);
+        ns = min(2 * ns, 256u);
         if (ld_acquire_sys(p) >= target) return true;
         if (*C.abort) return false;
         if (globaltimer_ns() > dl) {
@@ -604,6 +613,30 @@ __device__ __noinline__ void ar_pass(const Args& a, const Ctl& C, int r_lo, int 
                 store_from_float(a.ar_y, a.ar_y_dtype, (int64_t)mm[i] * a.ar_ldy + r, val[i] + b);
             }
         }
+}
+
+template <bool PROD>
+__device__ __noinline__ void prep_chunk(const Args& a, int k, int c, int lane);
+// Op k feeds a later op's converted activations.  After its units of op k,
+// a warp counts the row groups it wrote (r_lo..r_hi, those whose first unit
+// lies in its range) toward their chunks; the warp that completes a chunk
+// converts it, so the consumer waits only for the chunks it reads, not for
+// the whole producing segment.  (The warp barrier orders every lane's rows
+// before lane 0's release; the completing warp's acquire orders the other
+// writers' rows before its reads.)
+__device__ __noinline__ void feed_pass(const Args& a, int k, int r_lo, int r_hi, int lane) {
+    const Op& op = a.op[k];
+    __syncwarp();
+    for (int c = r_lo / op.feed_rgs; c <= r_hi / op.feed_rgs; ++c) {
+        const int n = min(r_hi, (c + 1) * op.feed_rgs - 1) - max(r_lo, c * op.feed_rgs) + 1;
+        int* cnt = a.counters + op.feed_cnt + c * kFlagStride;
+        int old = 0;
+        if (lane == 0) {
+            asm volatile("atom.release.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(cnt), "r"(n) : "memory");
+            if (old + n == op.feed_rgs) (void)ld_acquire(cnt);
+        }
+        if (__shfl_sync(0xffffffffu, old, 0) + n == op.feed_rgs) prep_chunk<true>(a, op.feed - 1, c, lane);
+    }
 }
 
 // Row-group values are held as v[2j + i][r] = row g (r = 0) / g + 8 (r = 1)
@@ -731,8 +764,11 @@ __device__ __noinline__ void prep_chunk(const Args& a, int k, int c, int lane) {
     const int M = a.M;
     const int gc = op.chunk0 + c;
     bool bad = false;
+    // the next token's load in flight while one is converted
+    uint4 nx = ld_x<PROD>(op.x + (int64_t)c * 256 + 8 * lane);
     for (int m = 0; m < M; ++m) {
-        const uint4 v = ld_x<PROD>(op.x + (int64_t)m * op.ldx + (int64_t)c * 256 + 8 * lane);
+        const uint4 v = nx;
+        if (m + 1 < M) nx = ld_x<PROD>(op.x + (int64_t)(m + 1) * op.ldx + (int64_t)c * 256 + 8 * lane);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         float f[8];
         float mx = 0.0f;
@@ -764,44 +800,50 @@ __device__ __noinline__ void prep_chunk(const Args& a, int k, int c, int lane) {
     }
     if (lane >= M && lane < 16) a.xinv[(int64_t)gc * 16 + lane] = 1.0f;
     bad = __any_sync(0xffffffffu, bad);   // also orders every lane's stores before lane 0's release
-    if (lane == 0) st_release(a.counters + op.flag_off + c, bad ? 3 : 2);
+    if (lane == 0) st_release(a.counters + op.flag_off + c * kFlagStride, bad ? 3 : 2);
 }
 
-// Make every chunk of op k's converted activations ready: claim and prepare the
-// unclaimed ones, then wait (bounded) for the rest.  bad: a chunk holds an
-// inf or NaN.  False on abort.
+// Make the chunks of op k's converted activations that units [u0, u1) of the
+// op read ready: claim and prepare the unclaimed ones, then wait (bounded,
+// with a growing sleep) for the rest.  Units are row-group major, chunk
+// fastest, so the range reads a run of chunks that may wrap.  Only the
+// chunks a warp reads are polled: thousands of warps polling every chunk
+// flag of an op turn its cache lines into an L2 hot spot that slows the
+// weight stream.  bad: one of them holds an inf or NaN (the warp then takes
+// the bf16 path for this op).  False on abort.
 template <bool PROD>
-__device__ bool ensure_chunks(const Args& a, const Ctl& C, int k, int vw, int lane, bool& bad) {
+__device__ bool ensure_chunks(const Args& a, const Ctl& C, int k, int u0, int u1, int lane, bool& bad) {
     const Op& op = a.op[k];
     int* flags = a.counters + op.flag_off;
     const int n = op.n_kc;
-    // claim free chunks one at a time, looking from a warp-dependent chunk on,
-    // so the warps that reach an op together prepare its chunks in parallel
-    const int start = vw % n;
-    while (true) {
+    const int L = min(u1 - u0, n), c0 = u0 % n;
+    while (!op.fed) {
         int found = -1;
-        for (int b0 = 0; b0 < n && found < 0; b0 += 32) {
-            int c = start + b0 + lane;
+        for (int b0 = 0; b0 < L && found < 0; b0 += 32) {
+            int c = c0 + b0 + lane;
             c -= c >= n ? n : 0;
             c -= c >= n ? n : 0;
-            const bool free = b0 + lane < n && ld_acquire(flags + c) == 0;
+            const bool free = b0 + lane < L && ld_acquire(flags + c * kFlagStride) == 0;
             const unsigned m = __ballot_sync(0xffffffffu, free);
             if (m) found = __shfl_sync(0xffffffffu, c, __ffs(m) - 1);
         }
         if (found < 0) break;
         int won = 0;
-        if (lane == 0) won = atomicCAS(flags + found, 0, 1) == 0;
+        if (lane == 0) won = atomicCAS(flags + found * kFlagStride, 0, 1) == 0;
         if (__shfl_sync(0xffffffffu, won, 0)) prep_chunk<PROD>(a, k, found, lane);
     }
     bool any_bad = false, ok = true;
-    for (int b0 = 0; b0 < n && ok; b0 += 32) {
-        const int c = b0 + lane;
+    for (int b0 = 0; b0 < L && ok; b0 += 32) {
+        int c = c0 + b0 + lane;
+        c -= c >= n ? n : 0;
+        c -= c >= n ? n : 0;
         int f = 2;
-        if (c < n) {
-            f = ld_acquire(flags + c);
+        if (b0 + lane < L) {
+            f = ld_acquire(flags + c * kFlagStride);
             if (f < 2) {
                 const uint64_t dl = globaltimer_ns() + kWaitNs;
-                while ((f = ld_acquire(flags + c)) < 2) {
+                unsigned ns = 64;
+                while ((f = ld_acquire(flags + c * kFlagStride)) < 2) {
                     if (*C.abort) {
                         ok = false;
                         break;
@@ -812,7 +854,8 @@ __device__ bool ensure_chunks(const Args& a, const Ctl& C, int k, int vw, int la
                         ok = false;
                         break;
                     }
-                    __nanosleep(64);
+                    __nanosleep(ns);
+                    ns = min(2 * ns, 1024u);
                 }
             }
         }
@@ -1057,7 +1100,7 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
         while (k < a.n_ops && !(a.op[k].f16 && i >= a.op[k].chunk0 && i < a.op[k].chunk0 + a.op[k].n_kc)) ++k;
         if (k == a.n_ops || a.op[k].dseg0 >= 0 || a.op[k].dseg1 >= 0) continue;
         int won = 0;
-        if (lane == 0) won = atomicCAS(a.counters + a.op[k].flag_off + (i - a.op[k].chunk0), 0, 1) == 0;
+        if (lane == 0) won = atomicCAS(a.counters + a.op[k].flag_off + (i - a.op[k].chunk0) * kFlagStride, 0, 1) == 0;
         if (__shfl_sync(0xffffffffu, won, 0)) prep_chunk<false>(a, k, i - a.op[k].chunk0, lane);
     }
     if (!has_units) return;
@@ -1076,7 +1119,7 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
             const Op& op = a.op[k];
             const int end = min(gend, op.ub + op.units);
             const bool prod = op.dseg0 >= 0 || op.dseg1 >= 0;
-            if (prod) {
+            if (prod && !op.fed) {
                 // earlier segments whose output this op reads
                 bool ok = true;
                 if (lane == 0) {
@@ -1093,8 +1136,8 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
             if constexpr (NTB == 1) {      // the f16 path runs up to 8 tokens
                 if (op.f16) {
                     bool bad = false;
-                    const bool ok = prod ? ensure_chunks<true>(a, C, k, vw, lane, bad)
-                                         : ensure_chunks<false>(a, C, k, vw, lane, bad);
+                    const bool ok = prod ? ensure_chunks<true>(a, C, k, gu - op.ub, end - op.ub, lane, bad)
+                                         : ensure_chunks<false>(a, C, k, gu - op.ub, end - op.ub, lane, bad);
                     if (!ok) {
                         Wk.dead = true;
                         break;
@@ -1112,10 +1155,15 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
             else
                 run_op<NTB, false, false>(a, C, F, Wk, s, k, gu, end, gend, vw, k_first, rg_first, ring_p, ring, bars,
                                           s_abort, pair_nv, scale_tab, lane, policy);
-            if (k == a.ar_op && a.ar_world > 0 && !Wk.dead) {
-                // the row groups whose first unit lies in [gu, end)
+            if (((k == a.ar_op && a.ar_world > 0) || op.feed) && !Wk.dead) {
+                // the row groups whose first unit lies in [gu, end): this warp wrote them
                 const int r_lo = (gu - op.ub + op.n_kc - 1) / op.n_kc, r_hi = (end - 1 - op.ub) / op.n_kc;
-                if (r_lo <= r_hi) ar_pass(a, C, r_lo, r_hi, lane);
+                if (r_lo <= r_hi) {
+                    if (op.feed)
+                        feed_pass(a, k, r_lo, r_hi, lane);
+                    else
+                        ar_pass(a, C, r_lo, r_hi, lane);
+                }
             }
             gu = end;
             if (gu < gend) ++k;
@@ -1358,17 +1406,40 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
     // (above 8 tokens the per-unit rescaling of two token tiles costs more than
     // the cheaper decode saves)
     int64_t chunks = 0;
+    // each chunk flag on its own 128-byte line: every warp that reaches an op
+    // claims and polls the flags of the chunks it reads, and flags sharing a
+    // line would serialise those atomics and loads in one L2 slice
+    const int64_t fbase = (cnt + kFlagStride - 1) / kFlagStride * kFlagStride;
     // (a one-op batch keeps the bf16 path: the conversion's latency at launch
     // start costs more than it saves over the few units each warp then has)
     for (int k = 0; k < n_ops && M <= 8 && n_ops > 1; ++k) {
         Op& p = a.op[k];
-        if ((size_t)(chunks + p.n_kc) * 512 * M > kXhBudget || cnt + chunks + p.n_kc > max_counters) continue;
+        if ((size_t)(chunks + p.n_kc) * 512 * M > kXhBudget || fbase + (chunks + p.n_kc) * kFlagStride > max_counters)
+            continue;
         p.f16 = 1;
         p.chunk0 = (int)chunks;
-        p.flag_off = (int)(cnt + chunks);
+        p.flag_off = (int)(fbase + chunks * kFlagStride);
         chunks += p.n_kc;
     }
-    a.n_cnt_all = (int)(cnt + chunks);
+    // a consumer whose one input is an earlier op's whole bf16 output gets its
+    // chunks converted by that producer as their row groups complete
+    int64_t feeds = fbase + chunks * kFlagStride;
+    for (int k = 0; k < n_ops; ++k) {
+        Op& c = a.op[k];
+        const SparkChainOp& o = ops[k];
+        if (!c.f16 || o.dep[0] < 0 || o.dep[1] >= 0) continue;
+        Op& pr = a.op[o.dep[0]];
+        const int width = pr.silu ? pr.oc / 2 : pr.oc;
+        if (pr.feed || pr.y != o.x || pr.ldy != c.ldx || pr.y_dtype != SPARK_DTYPE_BF16 || width != c.n_kc * 256 ||
+            feeds + (int64_t)c.n_kc * kFlagStride > max_counters)
+            continue;
+        pr.feed = k + 1;
+        pr.feed_rgs = pr.silu ? 32 : 16;
+        pr.feed_cnt = (int)feeds;
+        c.fed = 1;
+        feeds += (int64_t)c.n_kc * kFlagStride;
+    }
+    a.n_cnt_all = (int)(chunks ? feeds : cnt);
     a.n_chunks = (int)chunks;
     a.part_stride = T * 2 * M * 16;
     const size_t area = (size_t)a.part_stride * sizeof(float);
