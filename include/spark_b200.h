@@ -259,37 +259,37 @@ SPARK_API size_t spark_linear_batch_workspace_size(const SparkChainOp* ops, int 
 SPARK_API int spark_linear_batch(const SparkChainOp* ops, int n_ops, int64_t M, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
-/* spark_linear_batch with the all-reduce of one op fused into its epilogue:
- * op ar->op is a row-parallel linear (this rank holds a slice of its input
+/* spark_linear_batch with the all-reduce of one op inside the launch: op
+ * ar->op is a row-parallel linear (this rank holds a slice of its input
  * features, its output is a partial sum), e.g. the down projection of a
- * tensor-parallel MLP.  Inside the same launch, each warp that finished row
- * groups of the op stores their fp32 partials into every rank's receive
- * buffer over peer memory and publishes them (release flags, system scope),
- * then waits (bounded, 2 s) for every rank's partials of those row groups,
- * sums them in rank order 0..W-1 and writes y (+ bias): every rank gets the
- * same bits, with no separate all-reduce launch.
- * Replaces the NCCL all-reduce after the row-parallel projection.
- *   recv[r]:  rank r's receive buffer, spark_batch_ar_recv_floats(world, M, oc)
- *             fp32 (mapped into this process, e.g. spark_ipc_open);
- *   flags[r]: rank r's flag array, spark_batch_ar_flags_count(world, oc) ints,
- *             zero before the first call (the last int counts this rank's calls).
+ * tensor-parallel MLP.  Each warp that finished row groups of the op stores
+ * their fp32 partials into every rank's receive buffer over peer memory, as
+ * 8-byte words tagged with the call number (single 64-bit stores: no fence
+ * and no flag), then waits (bounded, 2 s) until every rank's words of those
+ * row groups carry this call's number, sums them in rank order 0..W-1 and
+ * writes y (+ bias): every rank gets the same bits, with no separate
+ * all-reduce launch.  Replaces the NCCL all-reduce after the row-parallel
+ * projection.
+ *   recv[r]:  rank r's receive buffer of spark_batch_ar_recv_bytes(world,
+ *             M, oc) bytes, 16-byte aligned, zero before the first call
+ *             (mapped into this process, e.g. spark_ipc_open);
+ *   counter:  this rank's call counter, one int, zero before the first call.
  * Every rank makes the same sequence of calls (CUDA graphs included) with the
  * same op shapes; the op may not use SPARK_EPILOGUE_SILU and no other op of
  * the batch may read its output (SPARK_ERR_UNSUPPORTED); M <= 16; 1 to
- * SPARK_MAX_PEERS ranks (the two size helpers return 0 outside).  A peer that does not arrive in
- * 2 s sets the workspace error word (spark_workspace_check).  workspace:
- * spark_linear_batch_ar_workspace_size(ops, n_ops, M, ar) bytes (ar's buffers
- * may be null for that query). */
+ * SPARK_MAX_PEERS ranks (spark_batch_ar_recv_bytes returns 0 outside).  A
+ * peer that does not arrive in 2 s sets the workspace error word
+ * (spark_workspace_check).  workspace: spark_linear_batch_ar_workspace_size(
+ * ops, n_ops, M, ar) bytes (ar's buffers may be null for that query). */
 typedef struct {
     int op;
     int world, rank;
-    float* const* recv;
-    int* const* flags;
+    void* const* recv;
+    int* counter;
 } SparkBatchAllReduce;
 SPARK_API size_t spark_linear_batch_ar_workspace_size(const SparkChainOp* ops, int n_ops, int64_t M,
                                                       const SparkBatchAllReduce* ar);
-SPARK_API int64_t spark_batch_ar_recv_floats(int world, int64_t M, int64_t oc);
-SPARK_API int64_t spark_batch_ar_flags_count(int world, int64_t oc);
+SPARK_API int64_t spark_batch_ar_recv_bytes(int world, int64_t M, int64_t oc);
 SPARK_API int spark_linear_batch_ar(const SparkChainOp* ops, int n_ops, int64_t M, const SparkBatchAllReduce* ar,
                                     void* workspace, size_t workspace_bytes, void* stream);
 

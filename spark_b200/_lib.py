@@ -42,7 +42,7 @@ class SparkChainOp(ctypes.Structure):
 class SparkBatchAllReduce(ctypes.Structure):
     """struct SparkBatchAllReduce of include/spark_b200.h."""
     _fields_ = [("op", ctypes.c_int), ("world", ctypes.c_int), ("rank", ctypes.c_int),
-                ("recv", ctypes.c_void_p), ("flags", ctypes.c_void_p)]
+                ("recv", ctypes.c_void_p), ("counter", ctypes.c_void_p)]
 
 
 class SparkError(RuntimeError):
@@ -88,8 +88,7 @@ _SIGNATURES = {
     "spark_linear_batch_workspace_size": (_sz, [_p, _i, _i64]),
     "spark_linear_batch": (_i, [_p, _i, _i64, _p, _sz, _p]),
     "spark_linear_batch_ar_workspace_size": (_sz, [_p, _i, _i64, _p]),
-    "spark_batch_ar_recv_floats": (_i64, [_i, _i64, _i64]),
-    "spark_batch_ar_flags_count": (_i64, [_i, _i64]),
+    "spark_batch_ar_recv_bytes": (_i64, [_i, _i64, _i64]),
     "spark_linear_batch_ar": (_i, [_p, _i, _i64, _p, _p, _sz, _p]),
     "spark_linear_chain_workspace_size": (_sz, [_i]),
     "spark_linear_chain": (_i, [_p, _i, _i64, _p, _sz, _p]),

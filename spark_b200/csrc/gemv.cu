@@ -1653,14 +1653,9 @@ int spark_linear_batch(const SparkChainOp* ops, int n_ops, int64_t M, void* work
     return rc;
 }
 
-int64_t spark_batch_ar_recv_floats(int world, int64_t M, int64_t oc) {
+int64_t spark_batch_ar_recv_bytes(int world, int64_t M, int64_t oc) {
     if (world < 1 || world > SPARK_MAX_PEERS || M < 1 || M > 16 || oc < 1) return 0;
-    return (int64_t)2 * world * ((oc + 15) / 16) * M * 16;
-}
-
-int64_t spark_batch_ar_flags_count(int world, int64_t oc) {
-    if (world < 1 || world > SPARK_MAX_PEERS || oc < 1) return 0;
-    return (int64_t)world * ((oc + 15) / 16) + 1;
+    return (int64_t)2 * world * ((oc + 15) / 16) * M * 16 * 8;
 }
 
 }  // extern "C"

@@ -79,12 +79,13 @@ struct Op {
                                       // chunk0: its first chunk in the batch's converted-activation arrays
     int feed, feed_rgs, feed_cnt, fed;   // feed: 1 + the op whose activation chunks this op's rows complete
                                          // (0: none), feed_rgs row groups per chunk, counters at feed_cnt
-                                         // (kFlagStride apart); fed: this op's chunks come from its producer
+                                         // (kFlagStride apart); fed: 1 + that producer (on the consumer)
 };
 
 // A segment: ops k0..k1-1, units [ub, ub + units) of the sequence, split over
 // T = G * kCW warps: warp v holds q + (v < rem) units from ub + v * q + min(v, rem).
 constexpr int kFlagStride = 32;       // ints between two chunk flags (one 128-byte line each)
+constexpr int kF16Units = 40;         // below this many units per warp, an all-SPFP2 batch keeps the bf16 path
 
 struct Seg {
     int ub, units, q, rem;
@@ -105,10 +106,10 @@ struct Args {
     float* xinv;             // [chunk][16]: 1 / sigma per token
     uint16_t* xh;            // [chunk][M][256]: f16 activations times sigma
     // the fused all-reduce of one op (ar_world = 0: none): every rank's
-    // receive buffer [2][world][ar_nrg][M][16] fp32 and flag array
-    // [world][ar_nrg] (+ this rank's call count), as this process maps them
-    float* ar_recv[SPARK_MAX_PEERS];
-    int* ar_flags[SPARK_MAX_PEERS];
+    // receive buffer [2][world][ar_nrg][M][16] of tagged words, as this
+    // process maps them, and this rank's call counter
+    uint64_t* ar_recv[SPARK_MAX_PEERS];
+    int* ar_counter;
     int ar_world, ar_rank, ar_nrg, ar_op;
     float* ar_local;         // the op's rank-local sums [M][ar_nrg * 16] (the op's y during the launch)
     void* ar_y;              // the op's real output, bias and dtypes
@@ -503,79 +504,83 @@ struct Ctl {
 };
 
 // ---------------------------------------------------------------- fused all-reduce
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-    int v;
-    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Bounded wait (one thread) until a flag another GPU writes reaches `target`.
-__device__ bool wait_peer(const int* p, int target, const Ctl& C) {
-    if (ld_acquire_sys(p) >= target) return true;
-    const uint64_t dl = globaltimer_ns() + kWaitNs;
-    unsigned ns = 32;
-    while (true) {
-        __nanosleep(ns);
-        ns = min(2 * ns, 256u);
-        if (ld_acquire_sys(p) >= target) return true;
-        if (*C.abort) return false;
-        if (globaltimer_ns() > dl) {
-            report_device_error(C.err, 5);
-            *C.abort = 1;
-            return false;
-        }
-    }
-}
-
-// All-reduce of one finished row group over the ranks, in two halves.
+// All-reduce of one finished row group over the ranks, in two halves.  Every
+// value travels as one 8-byte word: the fp32 bits in the low half, the call
+// number in the high half, written and read with single 64-bit accesses (a
+// naturally aligned 64-bit access is single-copy atomic, over NVLink too), so
+// a reader that sees this call's number sees the value: no release fence,
+// no flag round trip.
 // ar_publish: this lane's values val[e] (token mm[e], row rr[e] of the group,
-// valid ok[e]) into every rank's receive slot for (this rank, rg), then a
-// release flag per rank.  ar_collect: once every rank's flag for rg is up,
-// val[e] becomes the sum over ranks 0..W-1 in that order (this rank's own term
-// from registers: the same bits the others read).  Slots alternate by call
-// parity; a rank reuses a slot two calls later only after every rank has
-// published (and so finished reading) the call in between.
-__device__ __forceinline__ int ar_epoch(const Args& a) {
+// valid ok[e]) into every rank's receive slot for (this rank, rg).
+// ar_collect: val[e] becomes the sum over ranks 0..W-1 in that order, each
+// term waited for (bounded) until its word carries this call's number (this
+// rank's own term from registers: the same bits the others read).  Slots
+// alternate by call parity; a rank writes a slot two calls later only after
+// it has read every rank's words of the call in between, so every rank has
+// finished with that slot.
+__device__ __forceinline__ uint32_t ar_epoch(const Args& a) {
     // this call's number: the calls this rank made before it, + 1
-    return *reinterpret_cast<volatile int*>(a.ar_flags[a.ar_rank] + a.ar_world * a.ar_nrg) + 1;
+    return (uint32_t)*reinterpret_cast<volatile int*>(a.ar_counter) + 1u;
+}
+__device__ __forceinline__ void st_word_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
 }
 template <int NE>
 __device__ void ar_publish(const Args& a, int rg, const int (&mm)[NE], const int (&rr)[NE], const float (&val)[NE],
-                           const bool (&ok)[NE], int lane) {
+                           const bool (&ok)[NE], uint32_t epoch) {
     const int W = a.ar_world, R = a.ar_rank, nrg = a.ar_nrg, M = a.M;
-    const int epoch = ar_epoch(a);
     const int64_t stride = (int64_t)nrg * M * 16;                             // one rank's slots
-    const int64_t off = ((int64_t)(epoch & 1) * W * nrg + rg) * M * 16;       // (parity, rank 0, rg)
+    const int64_t off = ((int64_t)(epoch & 1u) * W * nrg + rg) * M * 16;      // (parity, rank 0, rg)
     for (int p = 0; p < W; ++p) {
-        float* dst = a.ar_recv[p] + off + R * stride;
+        uint64_t* dst = a.ar_recv[p] + off + R * stride;
 #pragma unroll
         for (int e = 0; e < NE; ++e)
-            if (ok[e]) __stcg(dst + mm[e] * 16 + rr[e], val[e]);
+            if (ok[e]) st_word_sys(dst + mm[e] * 16 + rr[e], (uint64_t)epoch << 32 | __float_as_uint(val[e]));
     }
-    __syncwarp();                     // every lane's stores before the releases
-    if (lane < W) st_release_sys(a.ar_flags[lane] + R * nrg + rg, epoch);
 }
 template <int NE>
 __device__ bool ar_collect(const Args& a, const Ctl& C, int rg, const int (&mm)[NE], const int (&rr)[NE],
-                           float (&val)[NE], const bool (&ok)[NE], int lane) {
+                           float (&val)[NE], const bool (&ok)[NE], uint32_t epoch) {
     const int W = a.ar_world, R = a.ar_rank, nrg = a.ar_nrg, M = a.M;
-    const int epoch = ar_epoch(a);
     const int64_t stride = (int64_t)nrg * M * 16;
-    const int64_t off = ((int64_t)(epoch & 1) * W * nrg + rg) * M * 16;
+    const int64_t off = ((int64_t)(epoch & 1u) * W * nrg + rg) * M * 16;
+    const uint64_t* base = a.ar_recv[R] + off;
     bool good = true;
-    if (lane < W && lane != R) good = wait_peer(a.ar_flags[R] + lane * nrg + rg, epoch, C);
-    if (!__all_sync(0xffffffffu, good)) return false;
-    const float* base = a.ar_recv[R] + off;
 #pragma unroll
     for (int e = 0; e < NE; ++e) {
         if (!ok[e]) continue;
         float sum = 0.0f;
-        for (int r = 0; r < W; ++r) sum += r == R ? val[e] : __ldcg(base + r * stride + mm[e] * 16 + rr[e]);
+        for (int r = 0; r < W; ++r) {
+            if (r == R) {
+                sum += val[e];
+                continue;
+            }
+            const uint64_t* q = base + r * stride + mm[e] * 16 + rr[e];
+            uint64_t w = ld_word_sys(q);
+            if ((uint32_t)(w >> 32) != epoch && good) {
+                const uint64_t dl = globaltimer_ns() + kWaitNs;
+                unsigned ns = 32;
+                while ((uint32_t)((w = ld_word_sys(q)) >> 32) != epoch) {
+                    if (*C.abort || globaltimer_ns() > dl) {
+                        if (!*C.abort) report_device_error(C.err, 5);
+                        *C.abort = 1;
+                        good = false;
+                        break;
+                    }
+                    __nanosleep(ns);
+                    ns = min(2 * ns, 256u);
+                }
+            }
+            sum += __uint_as_float((uint32_t)w);
+        }
         val[e] = sum;
     }
-    return true;
+    return __all_sync(0xffffffffu, good);
 }
 
 // The exchange of the all-reduced op, after this warp's units of it: the op
@@ -588,6 +593,7 @@ __device__ __noinline__ void ar_pass(const Args& a, const Ctl& C, int r_lo, int 
     __syncwarp();                     // this warp's own row writes before its reads
     const int row = lane & 15;
     constexpr int NE = 8;
+    const uint32_t epoch = ar_epoch(a);
     for (int pass = 0; pass < 2; ++pass)
         for (int rg = r_lo; rg <= r_hi; ++rg) {
             int mm[NE], rr[NE];
@@ -601,10 +607,10 @@ __device__ __noinline__ void ar_pass(const Args& a, const Ctl& C, int r_lo, int 
                 val[i] = ok[i] ? __ldcg(a.ar_local + (int64_t)mm[i] * ld + rg * 16 + row) : 0.0f;
             }
             if (pass == 0) {
-                ar_publish<NE>(a, rg, mm, rr, val, ok, lane);
+                ar_publish<NE>(a, rg, mm, rr, val, ok, epoch);
                 continue;
             }
-            if (!ar_collect<NE>(a, C, rg, mm, rr, val, ok, lane)) return;
+            if (!ar_collect<NE>(a, C, rg, mm, rr, val, ok, epoch)) return;
             const int64_t r = (int64_t)rg * 16 + row;
 #pragma unroll
             for (int i = 0; i < NE; ++i) {
@@ -617,6 +623,44 @@ __device__ __noinline__ void ar_pass(const Args& a, const Ctl& C, int r_lo, int 
 
 template <bool PROD>
 __device__ __noinline__ void prep_chunk(const Args& a, int k, int c, int lane);
+
+// A consumer on the bf16 path (no conversion) that its producer feeds: wait
+// (bounded, growing sleeps) until every row group of the chunks that units
+// [u0, u1) of op k read is written.
+__device__ __noinline__ bool wait_fed(const Args& a, const Ctl& C, int k, int u0, int u1, int lane) {
+    const Op& op = a.op[k];
+    const Op& pr = a.op[op.fed - 1];
+    const int n = op.n_kc, L = min(u1 - u0, n), c0 = u0 % n;
+    bool ok = true;
+    for (int b0 = 0; b0 < L && ok; b0 += 32) {
+        int c = c0 + b0 + lane;
+        c -= c >= n ? n : 0;
+        c -= c >= n ? n : 0;
+        if (b0 + lane < L) {
+            const int* cnt = a.counters + pr.feed_cnt + c * kFlagStride;
+            if (ld_acquire(cnt) < pr.feed_rgs) {
+                const uint64_t dl = globaltimer_ns() + kWaitNs;
+                unsigned ns = 64;
+                while (ld_acquire(cnt) < pr.feed_rgs) {
+                    if (*C.abort) {
+                        ok = false;
+                        break;
+                    }
+                    if (globaltimer_ns() > dl) {
+                        report_device_error(C.err, 1);
+                        *C.abort = 1;
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(ns);
+                    ns = min(2 * ns, 1024u);
+                }
+            }
+        }
+        ok = __all_sync(0xffffffffu, ok);   // every lane's acquire before any lane's reads
+    }
+    return ok;
+}
 // Op k feeds a later op's converted activations.  After its units of op k,
 // a warp counts the row groups it wrote (r_lo..r_hi, those whose first unit
 // lies in its range) toward their chunks; the warp that completes a chunk
@@ -635,7 +679,8 @@ __device__ __noinline__ void feed_pass(const Args& a, int k, int r_lo, int r_hi,
             asm volatile("atom.release.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(cnt), "r"(n) : "memory");
             if (old + n == op.feed_rgs) (void)ld_acquire(cnt);
         }
-        if (__shfl_sync(0xffffffffu, old, 0) + n == op.feed_rgs) prep_chunk<true>(a, op.feed - 1, c, lane);
+        if (__shfl_sync(0xffffffffu, old, 0) + n == op.feed_rgs && a.op[op.feed - 1].f16)
+            prep_chunk<true>(a, op.feed - 1, c, lane);
     }
 }
 
@@ -1119,7 +1164,13 @@ __device__ void warp_main(const Args& a, const Ctl& C, const uint8_t* ring_p, ui
             const Op& op = a.op[k];
             const int end = min(gend, op.ub + op.units);
             const bool prod = op.dseg0 >= 0 || op.dseg1 >= 0;
-            if (prod && !op.fed) {
+            if (prod && op.fed && !(NTB == 1 && op.f16)) {
+                // the chunks this warp reads, as the producer writes them
+                if (!wait_fed(a, C, k, gu - op.ub, end - op.ub, lane)) {
+                    Wk.dead = true;
+                    break;
+                }
+            } else if (prod && !op.fed) {
                 // earlier segments whose output this op reads
                 bool ok = true;
                 if (lane == 0) {
@@ -1243,7 +1294,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream(const __grid_constant__ 
         __syncthreads();
         if (threadIdx.x == 0) {
             // this rank's count of fused all-reduce calls (the next call's number - 1)
-            if (a.ar_world > 0) a.ar_flags[a.ar_rank][a.ar_world * a.ar_nrg] += 1;
+            if (a.ar_world > 0) *a.ar_counter += 1;
             *C.abort = 0;
             __threadfence();
             *reinterpret_cast<volatile int*>(a.ws + kCtlCtaDone) = 0;
@@ -1411,8 +1462,14 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
     // line would serialise those atomics and loads in one L2 slice
     const int64_t fbase = (cnt + kFlagStride - 1) / kFlagStride * kFlagStride;
     // (a one-op batch keeps the bf16 path: the conversion's latency at launch
-    // start costs more than it saves over the few units each warp then has)
-    for (int k = 0; k < n_ops && M <= 8 && n_ops > 1; ++k) {
+    // start costs more than it saves over the few units each warp then has;
+    // so does an all-SPFP2 batch of fewer than kF16Units units per warp, whose
+    // bf16 decode is nearly as cheap; with FP3 / NVFP4 ops in the batch the
+    // conversion runs anyway and SPFP2 keeps the f16 path too)
+    bool all_spfp2 = true;
+    for (int k = 0; k < n_ops; ++k) all_spfp2 &= a.op[k].fmt == SPARK_FMT_SPFP2;
+    const bool f16_ok = M <= 8 && n_ops > 1 && !(all_spfp2 && ub < (int64_t)kF16Units * T);
+    for (int k = 0; k < n_ops && f16_ok; ++k) {
         Op& p = a.op[k];
         if ((size_t)(chunks + p.n_kc) * 512 * M > kXhBudget || fbase + (chunks + p.n_kc) * kFlagStride > max_counters)
             continue;
@@ -1421,13 +1478,14 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
         p.flag_off = (int)(fbase + chunks * kFlagStride);
         chunks += p.n_kc;
     }
-    // a consumer whose one input is an earlier op's whole bf16 output gets its
-    // chunks converted by that producer as their row groups complete
+    // a consumer whose one input is an earlier op's whole bf16 output waits
+    // only for the chunks it reads, as the producer's row groups complete (the
+    // producer's warp that completes a chunk converts it for an f16 consumer)
     int64_t feeds = fbase + chunks * kFlagStride;
     for (int k = 0; k < n_ops; ++k) {
         Op& c = a.op[k];
         const SparkChainOp& o = ops[k];
-        if (!c.f16 || o.dep[0] < 0 || o.dep[1] >= 0) continue;
+        if (o.dep[0] < 0 || o.dep[1] >= 0) continue;
         Op& pr = a.op[o.dep[0]];
         const int width = pr.silu ? pr.oc / 2 : pr.oc;
         if (pr.feed || pr.y != o.x || pr.ldy != c.ldx || pr.y_dtype != SPARK_DTYPE_BF16 || width != c.n_kc * 256 ||
@@ -1436,10 +1494,10 @@ int stream_plan(const SparkChainOp* ops, int n_ops, int64_t M, uint8_t* ws, size
         pr.feed = k + 1;
         pr.feed_rgs = pr.silu ? 32 : 16;
         pr.feed_cnt = (int)feeds;
-        c.fed = 1;
+        c.fed = o.dep[0] + 1;
         feeds += (int64_t)c.n_kc * kFlagStride;
     }
-    a.n_cnt_all = (int)(chunks ? feeds : cnt);
+    a.n_cnt_all = (int)(feeds > fbase ? feeds : cnt);
     a.n_chunks = (int)chunks;
     a.part_stride = T * 2 * M * 16;
     const size_t area = (size_t)a.part_stride * sizeof(float);
@@ -1492,14 +1550,13 @@ int stream_plan_set_ar(StreamPlan* P, const SparkBatchAllReduce* ar) {
     const size_t local_off = (P->scratch_bytes + 255) / 256 * 256;
     P->scratch_bytes = local_off + (size_t)a.M * nrg * 16 * sizeof(float);
     if (!P->scratch) return SPARK_OK;
-    SPARK_REQUIRE(ar->recv && ar->flags, SPARK_ERR_INVALID, "spark_linear_batch_ar: null all-reduce buffers");
+    SPARK_REQUIRE(ar->recv && ar->counter && aligned(ar->counter, 4), SPARK_ERR_INVALID,
+                  "spark_linear_batch_ar: null receive buffers or call counter");
     for (int r = 0; r < ar->world; ++r)
-        SPARK_REQUIRE(ar->recv[r] && ar->flags[r] && aligned(ar->recv[r], 16) && aligned(ar->flags[r], 4),
-                      SPARK_ERR_INVALID, "spark_linear_batch_ar: rank %d's buffers missing or misaligned", r);
-    for (int r = 0; r < ar->world; ++r) {
-        a.ar_recv[r] = ar->recv[r];
-        a.ar_flags[r] = ar->flags[r];
-    }
+        SPARK_REQUIRE(ar->recv[r] && aligned(ar->recv[r], 16), SPARK_ERR_INVALID,
+                      "spark_linear_batch_ar: rank %d's receive buffer missing or misaligned", r);
+    for (int r = 0; r < ar->world; ++r) a.ar_recv[r] = static_cast<uint64_t*>(ar->recv[r]);
+    a.ar_counter = ar->counter;
     a.ar_world = ar->world;
     a.ar_rank = ar->rank;
     a.ar_nrg = nrg;

@@ -423,24 +423,22 @@ def linear_batch(batch: list[BatchOp], stream=None) -> None:
          ctypes.c_void_p(st.cuda_stream))
 
 
-def linear_batch_allreduce(batch: list[BatchOp], op: int, world: int, rank: int, recv_ptrs, flag_ptrs,
+def linear_batch_allreduce(batch: list[BatchOp], op: int, world: int, rank: int, recv_ptrs, counter: torch.Tensor,
                            stream=None) -> None:
     """linear_batch whose op `op` is all-reduced over `world` ranks inside the
     same launch (spark_linear_batch_ar): every rank runs the same batch on its
     own shard (e.g. the K-sharded down projection of a tensor-parallel MLP)
     and gets the rank-order sum of the ranks' fp32 results (+ bias) in that
-    op's y.  recv_ptrs / flag_ptrs: device addresses of every rank's receive
-    buffer and flag array, as this process maps them (tp.BatchAllReduce
-    shares and owns them)."""
+    op's y.  recv_ptrs: device addresses of every rank's receive buffer, as
+    this process maps them; counter: this rank's call counter (one int32).
+    tp.BatchAllReduce shares and owns both."""
     if not batch:
         raise ValueError("linear_batch_allreduce: empty batch")
     x0 = batch[0].x
     M = x0.shape[0]
     arr = _batch_array(batch)
-    P = ctypes.c_void_p * world
-    recv, flags = P(*recv_ptrs), P(*flag_ptrs)
-    ar = _lib.SparkBatchAllReduce(op, world, rank, ctypes.cast(recv, ctypes.c_void_p),
-                                  ctypes.cast(flags, ctypes.c_void_p))
+    recv = (ctypes.c_void_p * world)(*recv_ptrs)
+    ar = _lib.SparkBatchAllReduce(op, world, rank, ctypes.cast(recv, ctypes.c_void_p), counter.data_ptr())
     st = stream if stream is not None else torch.cuda.current_stream(x0.device)
     n = int(_lib.lib().spark_linear_batch_ar_workspace_size(ctypes.cast(arr, ctypes.c_void_p), len(batch), M,
                                                              ctypes.byref(ar)))

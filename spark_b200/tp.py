@@ -221,11 +221,11 @@ class BatchAllReduce:
     a batched decode launch (width `oc`, up to `max_tokens` tokens) done
     inside that launch over peer memory.
 
-    Every rank owns a receive buffer (2 launch parities x ranks x row groups x
-    tokens x 16 fp32) and a flag array (one flag per rank and row group, then
-    the launch counter); their CUDA IPC handles are exchanged once through the
-    process group.  The launch counter lives on the device, so calls can be
-    captured in a CUDA graph and replayed any number of times.  Every rank
+    Every rank owns a receive buffer (2 call parities x ranks x row groups x
+    tokens x 16 words of 8 bytes: an fp32 value tagged with the call number)
+    and a call counter; the buffers' CUDA IPC handles are exchanged once
+    through the process group.  The counter lives on the device, so calls can
+    be captured in a CUDA graph and replayed any number of times.  Every rank
     must make the same sequence of calls, each with the same batch shapes."""
 
     def __init__(self, oc: int, max_tokens: int = 16, group=None):
@@ -238,12 +238,11 @@ class BatchAllReduce:
             raise ValueError("BatchAllReduce: 1 to 16 tokens")
         self.oc, self.max_tokens, self._group = oc, max_tokens, group
         dev = torch.device("cuda", torch.cuda.current_device())
-        L = _lib.lib()
-        self.recv = torch.zeros(L.spark_batch_ar_recv_floats(self.world, max_tokens, oc), dtype=torch.float32,
-                                device=dev)
-        self.flags = torch.zeros(L.spark_batch_ar_flags_count(self.world, oc), dtype=torch.int32, device=dev)
+        n = _lib.lib().spark_batch_ar_recv_bytes(self.world, max_tokens, oc)
+        self.recv = torch.zeros(n // 8, dtype=torch.int64, device=dev)
+        self.counter = torch.zeros(4, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
-        (self._recv, self._flags), self._opened = _share([self.recv, self.flags], self.rank, self.world, group)
+        (self._recv,), self._opened = _share([self.recv], self.rank, self.world, group)
         if self.world > 1:
             dist.barrier(group=group)
 
@@ -255,7 +254,7 @@ class BatchAllReduce:
         if batch[op].silu or y.shape[1] != self.oc or M > self.max_tokens:
             raise ValueError(f"BatchAllReduce: op {op} must be a plain linear of width {self.oc} "
                              f"on at most {self.max_tokens} tokens")
-        ops.linear_batch_allreduce(batch, op, self.world, self.rank, self._recv, self._flags, stream=stream)
+        ops.linear_batch_allreduce(batch, op, self.world, self.rank, self._recv, self.counter, stream=stream)
 
     def check(self) -> None:
         """Raise if a launch gave up waiting for a peer (synchronises)."""

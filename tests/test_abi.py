@@ -80,6 +80,7 @@ def test_batch_allreduce_argument_validation():
     assert run(0, 2, 0) == (_lib.ERR_UNSUPPORTED, 0)         # a later op reads the summed output
     assert "later launch" in _lib.last_error()
     assert L.spark_linear_batch_ar(ctypes.cast(ops, P), 2, 1, None, P(256), 1 << 20, None) == _lib.ERR_INVALID
-    assert L.spark_batch_ar_recv_floats(2, 16, 2560) == 2 * 2 * 160 * 16 * 16
-    assert L.spark_batch_ar_flags_count(2, 2560) == 2 * 160 + 1
-    assert L.spark_batch_ar_recv_floats(0, 16, 2560) == 0 and L.spark_batch_ar_flags_count(9, 16) == 0
+    # 2 call parities x 2 ranks x 160 row groups x 16 tokens x 16 rows, 8-byte words
+    assert L.spark_batch_ar_recv_bytes(2, 16, 2560) == 2 * 2 * 160 * 16 * 16 * 8
+    assert L.spark_batch_ar_recv_bytes(0, 16, 2560) == 0 and L.spark_batch_ar_recv_bytes(9, 1, 16) == 0
+    assert L.spark_batch_ar_recv_bytes(2, 17, 16) == 0

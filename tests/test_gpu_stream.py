@@ -184,6 +184,36 @@ def test_batch_dependent_chain(M):
     ops().check_device_errors()
 
 
+@pytest.mark.parametrize("M", [1, 5, 12])
+def test_batch_fed_consumer(M):
+    """An all-SPFP2 two-op batch (gate|up with the SiLU epilogue, then down
+    reading its output) small enough to keep the bf16 path: the consumer waits
+    only for the chunks of h it reads, as the producer's row groups complete.
+    Checked bit for bit against the two ops as separate launches."""
+    H, I = 1024, 4096
+    g = torch.Generator().manual_seed(60 + M)
+    from spark_b200.inference_v3 import V3GateUpSiLU, V3PackedLinear
+    gate = (torch.randn(I, H, generator=g) * 0.02).cuda()
+    up = (torch.randn(I, H, generator=g) * 0.02).cuda()
+    down = (torch.randn(H, I, generator=g) * 0.02).cuda()
+    gu = V3GateUpSiLU(V3PackedLinear("spfp2", ops().spfp2_pack(gate)[0], I, H),
+                      V3PackedLinear("spfp2", ops().spfp2_pack(up)[0], I, H))
+    dn = V3PackedLinear("spfp2", ops().spfp2_pack(down)[0], H, I)
+    x = torch.randn(M, H, generator=g).bfloat16().cuda()
+    h = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(M, H, dtype=torch.float32, device="cuda")
+    batch = [ops().BatchOp("spfp2", gu.merged.w_tiled, x, h, silu=True),
+             ops().BatchOp("spfp2", dn.w_tiled, h, y, deps=[0])]
+    for _ in range(3):                      # the feed counters reset between launches
+        ops().linear_batch(batch)
+    torch.cuda.synchronize()
+    h_ref = gu(x)
+    y_ref = ops().linear("spfp2", dn.w_tiled, None, h_ref, H, I, out_dtype=torch.float32, tiled=True)
+    assert torch.equal(h, h_ref)
+    assert torch.equal(y, y_ref)
+    ops().check_device_errors()
+
+
 def test_batch_rejects_bad_ops():
     from spark_b200._lib import SparkError
     wq, s, wt, dec = make("spfp2", 256, 512, seed=40)
