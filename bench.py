@@ -464,7 +464,10 @@ def run_gpu(args, rank, world, local):
 
     # ---------------- BASELINE config 4, tensor-parallel over the ranks of this run
     tp = tp_mlp_measure(args, rank, world, local)
-    tp_dec = tp_decode_measure(args, rank, world, local)
+    try:
+        tp_dec = tp_decode_measure(args, rank, world, local)
+    except Exception as e:        # a device-side error reaches every rank alike; keep the line
+        tp_dec = {"error": f"{type(e).__name__}: {e}"[:300]}
     clk.__exit__(None, None, None)
     pre_flops = sum(2.0 * PREFILL_M * oc * ic for _, _, oc, ic in SHAPES)
     pre_tflops = world * pre_flops * pre_steps / (ms_pre * 1e-3) / 1e12

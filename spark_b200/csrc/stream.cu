@@ -366,13 +366,15 @@ __device__ __forceinline__ void load_frag(const uint8_t* slot, int lane, uint32_
 template <int FMT, int NTB, bool PROD>
 __device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* const (&xr)[NTB], int64_t col,
                                          const uint32_t* pair_tab, const uint32_t* scale_tab,
-                                         float (&acc)[2][NTB][4]) {
+                                         float (&acc)[2][NTB][4], uint32_t xl) {
     // one token tile: the unit's activations for all 8 steps are loaded first,
-    // so their latency overlaps the decode
+    // so their latency overlaps the decode.  Only lanes that feed a real
+    // token load (bit j of xl: token tile j); the others feed zeros, to
+    // columns that are never written, and keep the L1 return path free.
     uint4 xs[NTB == 1 ? 8 : 1];
     if constexpr (NTB == 1) {
 #pragma unroll
-        for (int s = 0; s < 8; ++s) xs[s] = ld_x<PROD>(xr[0] + col + 8 * s);
+        for (int s = 0; s < 8; ++s) xs[s] = (xl & 1u) ? ld_x<PROD>(xr[0] + col + 8 * s) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
@@ -397,7 +399,7 @@ __device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* con
         for (int j = 0; j < NTB; ++j) {
             uint4 x;
             if constexpr (NTB == 1) x = xs[s];
-            else x = ld_x<PROD>(xr[j] + col + 8 * s);
+            else x = (xl >> j & 1u) ? ld_x<PROD>(xr[j] + col + 8 * s) : make_uint4(0u, 0u, 0u, 0u);
             mma_bf16(acc[0][j], A0[0], A1[0], A0[1], A1[1], x.x, x.y);
             mma_bf16(acc[1][j], A0[2], A1[2], A0[3], A1[3], x.z, x.w);
         }
@@ -474,6 +476,8 @@ __device__ __forceinline__ void unit_h(const uint32_t* fw, const uint16_t* const
 template <int FMT>
 __device__ __forceinline__ void unit_h1(const uint32_t* fw, uint4 (&xs)[8], const uint16_t* nxt,
                                         float (&acc)[2][1][4]) {
+    // nxt: null after the op's last unit, and for lanes past the last token
+    // when there are several tokens (they keep feeding zeros and load nothing)
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
         uint32_t A0[4], A1[4];
@@ -994,6 +998,10 @@ __device__ __forceinline__ void run_units(const Args& a, const Ctl& C, Feed& F, 
         xi = a.xinv + (int64_t)op.chunk0 * 16 + 2 * t;
         kc_stride = 256 * M;
     }
+    const uint32_t xl = (g < M ? 1u : 0u) | (8 + g < M ? 2u : 0u);   // token tiles this lane feeds a real token
+    // f16 path: with one token every lane loads it (a warp-uniform branch
+    // measured faster); with several, lanes past the last token skip the loads
+    const bool ldx = M == 1 || (xl & 1u) != 0;
     const int lu0 = gu - op.ub;
     int rg = lu0 / n_kc, kc = lu0 - rg * n_kc;
     int seg0 = gu;
@@ -1011,7 +1019,7 @@ __device__ __forceinline__ void run_units(const Args& a, const Ctl& C, Feed& F, 
     if constexpr (H && NTB == 1) {
         const uint16_t* x0 = xr[0] + (int64_t)kc * kc_stride;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xs[q] = ld_v4(x0 + 8 * q);
+        for (int q = 0; q < 8; ++q) xs[q] = ldx ? ld_v4(x0 + 8 * q) : make_uint4(0u, 0u, 0u, 0u);
         rr = *reinterpret_cast<const float2*>(xi + kc * 16);
     }
     for (; gu < end; ++gu) {
@@ -1038,7 +1046,7 @@ __device__ __forceinline__ void run_units(const Args& a, const Ctl& C, Feed& F, 
             const bool more = gu + 1 < end;
             const int kn = kc + 1 == n_kc ? 0 : kc + 1;
             float u[2][1][4];
-            unit_h1<FMT>(fw, xs, more ? xr[0] + (int64_t)kn * kc_stride : nullptr, u);
+            unit_h1<FMT>(fw, xs, more && ldx ? xr[0] + (int64_t)kn * kc_stride : nullptr, u);
             const float2 r = rr;
             if (more) rr = *reinterpret_cast<const float2*>(xi + kn * 16);
             acc[0][0][0] += (u[0][0][0] + u[1][0][0]) * r.x;
@@ -1063,7 +1071,7 @@ __device__ __forceinline__ void run_units(const Args& a, const Ctl& C, Feed& F, 
             const uint16_t* xq[NTB];
 #pragma unroll
             for (int j = 0; j < NTB; ++j) xq[j] = xr[j];
-            unit_mma<FMT, NTB, PROD>(fw, xq, (int64_t)kc * 256, pair_tab, scale_tab, acc);
+            unit_mma<FMT, NTB, PROD>(fw, xq, (int64_t)kc * 256, pair_tab, scale_tab, acc, xl);
         }
 
         if (kc == n_kc - 1 || gu + 1 == gend) {
