@@ -232,18 +232,24 @@ __device__ __forceinline__ uint4 ld_v4(const void* p) {
 
 // Bounded wait on a shared-memory barrier phase.  False (and the abort flags
 // raised) once kWaitNs pass, or when another warp has raised an abort flag.
+// Bounded wait for a ring slot.  The global abort word and the clock are
+// read every 16th round only: thousands of warps reading one global word in
+// a tight loop make its L2 line a hot spot in the middle of the weight stream.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* s_abort, volatile int* g_abort,
                                            int* err) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t dl = globaltimer_ns() + kWaitNs;
-    while (true) {
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try(bar, parity)) return true;
-        if (*s_abort || *g_abort) return false;
-        if (globaltimer_ns() > dl) {
-            report_device_error(err, 1);
-            *s_abort = 1;
-            *g_abort = 1;
-            return false;
+        if (*s_abort) return false;
+        if ((i & 15u) == 0) {
+            if (*g_abort) return false;
+            if (globaltimer_ns() > dl) {
+                report_device_error(err, 1);
+                *s_abort = 1;
+                *g_abort = 1;
+                return false;
+            }
         }
     }
 }
