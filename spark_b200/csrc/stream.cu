@@ -375,8 +375,9 @@ __device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* con
                                          float (&acc)[2][NTB][4], uint32_t xl) {
     // one token tile: the unit's activations for all 8 steps are loaded first,
     // so their latency overlaps the decode.  Only lanes that feed a real
-    // token load (bit j of xl: token tile j); the others feed zeros, to
-    // columns that are never written, and keep the L1 return path free.
+    // token load (bit 0 of xl); the others feed zeros, to columns that are
+    // never written, and keep the L1 return path free.  (Two token tiles load
+    // step by step, every lane: predicating those loads measured slower.)
     uint4 xs[NTB == 1 ? 8 : 1];
     if constexpr (NTB == 1) {
 #pragma unroll
@@ -405,7 +406,7 @@ __device__ __forceinline__ void unit_mma(const uint32_t* fw, const uint16_t* con
         for (int j = 0; j < NTB; ++j) {
             uint4 x;
             if constexpr (NTB == 1) x = xs[s];
-            else x = (xl >> j & 1u) ? ld_x<PROD>(xr[j] + col + 8 * s) : make_uint4(0u, 0u, 0u, 0u);
+            else x = ld_x<PROD>(xr[j] + col + 8 * s);
             mma_bf16(acc[0][j], A0[0], A1[0], A0[1], A1[1], x.x, x.y);
             mma_bf16(acc[1][j], A0[2], A1[2], A0[3], A1[3], x.z, x.w);
         }
