@@ -462,6 +462,40 @@ def run_gpu(args, rank, world, local):
     ops.check_device_errors()
     del graph_pre, graph, graph_spfp2, graph_pl, graph_pp
 
+    # ---------------- native NVFP4 x NVFP4 (a reported mode): the out_proj weight
+    # [2560, 4096] at PREFILL_M tokens on tcgen05.mma kind::mxf4nvf4, activations
+    # quantised to NVFP4 by the weights' quantiser; error against the parity path
+    _, wq_o, s_o, oc_o, ic_o, _ = merged[0]["out_proj"]
+    x_o = xs[ic_o]
+    xq_o = ops.nvfp4_pack(x_o)
+    y_nat = ops.nvfp4_native_linear(wq_o, s_o, x_o, oc_o, ic_o, out_dtype=torch.float32, xq=xq_o)
+    y_par = ops.linear("nvfp4", wq_o, s_o, x_o, oc_o, ic_o, out_dtype=torch.float32)
+    nat_rel = float((y_nat.double() - y_par.double()).norm() / y_par.double().norm())
+    del y_nat, y_par
+    y_n = torch.empty(PREFILL_M, oc_o, device=device, dtype=torch.bfloat16)
+    x_c, x_s = xq_o
+
+    def native_gemm():
+        ops.nvfp4_native_linear(wq_o, s_o, x_o, oc_o, ic_o, xq=(x_c, x_s))
+
+    def native_full():
+        ops.nvfp4_native_linear(wq_o, s_o, x_o, oc_o, ic_o)
+
+    nat = {}
+    for name, fn in (("gemm", native_gemm), ("with_x_quantisation", native_full)):
+        with torch.cuda.stream(stream):
+            fn()
+            fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for _ in range(4):
+                fn()
+        nat[name] = timed(gr, pre_steps) / (4 * pre_steps)
+        del gr
+    ops.check_device_errors()
+    del y_n
+
     # ---------------- BASELINE config 4, tensor-parallel over the ranks of this run
     tp = tp_mlp_measure(args, rank, world, local)
     try:
@@ -471,6 +505,8 @@ def run_gpu(args, rank, world, local):
     clk.__exit__(None, None, None)
     pre_flops = sum(2.0 * PREFILL_M * oc * ic for _, _, oc, ic in SHAPES)
     pre_tflops = world * pre_flops * pre_steps / (ms_pre * 1e-3) / 1e12
+    nat_flops = 2.0 * PREFILL_M * oc_o * ic_o
+    nat_tf = {k: round(nat_flops / (v * 1e-3) / 1e12, 1) for k, v in nat.items()}
     tpeak, tpeak_kind = tensor_peak()
 
     peak, peak_kind = peaks()
@@ -525,6 +561,18 @@ def run_gpu(args, rank, world, local):
             "kernel": "k_tc_linear<FMT, 128 or 256 tokens> (tcgen05.mma kind::f16, A = decoded weights in TMEM)",
             "roofline": {"bound": "tensor", "achieved": round(pre_tflops / world, 1), "peak": tpeak,
                          "unit": "TFLOP/s", "frac": round(pre_tflops / world / tpeak, 4), "peak_source": tpeak_kind},
+            "nvfp4_native": {
+                "workload": f"out_proj [{oc_o}, {ic_o}] NVFP4 at M={PREFILL_M}, activations quantised to NVFP4 "
+                            "(spark_nvfp4_native_linear: tcgen05.mma kind::mxf4nvf4 block16, fp32 accumulate)",
+                "value": nat_tf["gemm"], "unit": "TFLOP/s", "ms": round(nat["gemm"], 4),
+                "with_x_quantisation": {"value": nat_tf["with_x_quantisation"], "unit": "TFLOP/s",
+                                        "ms": round(nat["with_x_quantisation"], 4)},
+                "roofline": {"bound": "tensor", "achieved": nat_tf["gemm"], "peak": 9000.0, "unit": "TFLOP/s",
+                             "frac": round(nat_tf["gemm"] / 9000.0, 4),
+                             "peak_source": "nominal dense FP4 (no measured FP4 peak on this pool)"},
+                "rel_frobenius_vs_parity_path": round(nat_rel, 5),
+                "note": "a reported mode, not the parity path: the error is the activations' FP4 rounding",
+            },
         },
     }
     if rank == 0:

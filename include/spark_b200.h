@@ -119,6 +119,18 @@ SPARK_API int spark_nvfp4_unpack(const uint8_t* codes, const uint8_t* scales, in
 SPARK_API int spark_nvfp4_embedding(const uint8_t* codes, const uint8_t* scales, int64_t num_embeddings, int64_t dim,
                                     const int64_t* ids, int64_t n_ids, void* out, int out_dtype, int* err,
                                     void* stream);
+/* Native block-scaled FP4 linear, a reported mode beside the parity path (no reference
+ * counterpart; the reference quantises only weights to NVFP4, nvfp4_emu.py:37-57): the
+ * activations are NVFP4 too (xq, x_scales = spark_nvfp4_pack of x [M, ic]) and
+ * y[M, oc] = dequant(xq) . dequant(wq)^T runs on tcgen05.mma kind::mxf4nvf4 (block16, ue4m3
+ * scales, fp32 accumulate) with both operands packed.  wq / w_scales: spark_nvfp4_pack of the
+ * weight [oc, ic] (row-major codes [oc, ic/2], scales [oc, ic/16], all scales non-negative).
+ * oc a multiple of 128, ic a multiple of 256, 16-byte aligned inputs; y [M, ldy] of y_dtype.  A
+ * bounded in-kernel wait that expires stores error code 4 in *err (read it with
+ * spark_workspace_check on a workspace whose first int is err). */
+SPARK_API int spark_nvfp4_native_linear(const uint8_t* wq, const uint8_t* w_scales, const uint8_t* xq,
+                                        const uint8_t* x_scales, int64_t M, int64_t oc, int64_t ic, void* y,
+                                        int y_dtype, int64_t ldy, int* err, void* stream);
 /* nvfp4_fake_quant -- 01_core/nvfp4_emu.py:37 (NVFP4STE backward is the identity, :66-68). */
 SPARK_API int spark_nvfp4_fake_quant(const void* w, int w_dtype, int64_t oc, int64_t ic, void* out, int out_dtype,
                            void* stream);

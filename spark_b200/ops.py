@@ -157,6 +157,22 @@ def nvfp4_unpack(codes: torch.Tensor, scales: torch.Tensor, oc: int, ic: int, dt
     return _home(out, codes)
 
 
+def nvfp4_native_linear(codes: torch.Tensor, scales: torch.Tensor, x: torch.Tensor, oc: int, ic: int,
+                        out_dtype=torch.bfloat16, xq=None) -> torch.Tensor:
+    """Native NVFP4 x NVFP4 linear (spark_nvfp4_native_linear, a reported mode:
+    the activations are quantised to NVFP4 by the weights' own quantiser, so
+    the result differs from the parity path `linear("nvfp4", ...)` by the
+    activations' FP4 rounding).  codes / scales: nvfp4_pack of the weight;
+    x: [M, ic]; xq: an already packed (codes, scales) of x, to skip that step."""
+    xc, xs = nvfp4_pack(x) if xq is None else xq
+    M = x.shape[0]
+    y = torch.empty(M, oc, dtype=out_dtype, device=x.device)
+    ws = workspace(x.device, 1 << 20)
+    call("spark_nvfp4_native_linear", _p(_bytes(codes)), _p(_bytes(scales)), _p(_bytes(xc)), _p(_bytes(xs)), M, oc,
+         ic, _p(y), _dt(y), oc, _p(ws), _stream(x))
+    return y
+
+
 def nvfp4_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
     x = _cuda(w.detach())
     oc, ic = x.shape
