@@ -11,16 +11,17 @@
 // rate of bf16.
 //
 // Tile: 128 weight rows x 128 tokens per CTA, K in blocks of 256 (128 bytes
-// per row: one 128-byte-swizzled TMA box), kStages blocks in flight.
+// of codes per row: one 128-byte-swizzled TMA box; 16 bytes of scales per
+// row: one plain box), kStages blocks in flight, two CTAs per SM.
 // Roles (192 threads):
 //   warps 0-3  scale writers, then the epilogue: warp q owns TMEM lanes
-//              32q..32q+31.  Per K block each thread loads the 16 scale
+//              32q..32q+31.  Per K block each thread reads the 16 scale
 //              bytes of weight rows g*32 + l and of tokens g*32 + l (g = 0..3)
-//              and stores them with tcgen05.st into the block's scale
-//              columns: per MMA (K = 64) column g holds the 4 scales of rows
-//              g*32 + lane in one 32-bit word, replicated in all four lane
-//              quadrants (the layout the block-scaled MMA reads).
-//   warp 4     lane 0 issues the TMA loads of the code tiles.
+//              from the stage and stores them with tcgen05.st into the
+//              block's scale columns: per MMA (K = 64) column g holds the 4
+//              scales of rows g*32 + lane in one 32-bit word, replicated in
+//              all four lane quadrants (the layout the block-scaled MMA reads).
+//   warp 4     lane 0 issues the TMA loads of the code and scale tiles.
 //   warp 5     allocates TMEM; lane 0 issues the MMAs (4 per K block) and
 //              commits each block back to its producers.
 // Every mbarrier wait is bounded (2 s); an expired wait records error code 4
@@ -43,11 +44,13 @@ namespace nvn {
 constexpr int kRows = 128;          // weight rows per CTA (MMA M)
 constexpr int kTok = 128;           // tokens per CTA (MMA N)
 constexpr int kKB = 256;            // K elements per block: 128 bytes of codes per row
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kStageA = kRows * 128;
 constexpr int kStageB = kTok * 128;
-constexpr int kStageBytes = kStageA + kStageB;
+constexpr int kStageSA = kRows * 16, kStageSB = kTok * 16;  // scale tiles
+constexpr int kStageBytes = kStageA + kStageB + kStageSA + kStageSB;
 constexpr int kSmem = kStages * kStageBytes + 1024;          // + alignment slack
+static_assert(2 * (kSmem + 256) <= 228 * 1024, "two CTAs per SM");
 constexpr int kThreads = 192;
 constexpr int kTmaWarp = 4, kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 256;                          // D: 128 columns; scales: 32 per stage
@@ -137,16 +140,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 }
 
 struct Params {
-    const uint8_t* wsc;     // weight scales [oc][ic / 16] (e4m3, positive: read as ue4m3)
-    const uint8_t* xsc;     // activation scales [M][ic / 16]
     void* y;
     int64_t ldy;
     int M, oc, n_kb, y_dtype;
     int* err;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     k_nvfp4_native(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap wsmap, const __grid_constant__ CUtensorMap xsmap,
                    const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -187,6 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_expect_tx(full + 8 * s, kStageBytes);
                 tma_load_2d(st, &wmap, kb * 128, row0, full + 8 * s);
                 tma_load_2d(st + kStageA, &xmap, kb * 128, tok0, full + 8 * s);
+                tma_load_2d(st + kStageA + kStageB, &wsmap, kb * 16, row0, full + 8 * s);
+                tma_load_2d(st + kStageA + kStageB + kStageSA, &xsmap, kb * 16, tok0, full + 8 * s);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -209,24 +213,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // scale writers: warp q writes its lane quadrant of every block's scale columns
+        // (the stage's TMA waited for the MMAs of its previous block, so its
+        // scale columns are free once the stage is full)
         const int q = warp;
-        const int64_t ldsc = (int64_t)p.n_kb * 16;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         for (int kb = 0; kb < p.n_kb && ok; ++kb) {
             const int s = kb % kStages;
-            if (kb >= kStages) ok = mbar_wait(empty + 8 * s, (uint32_t)((kb / kStages - 1) & 1));
+            ok = mbar_wait(full + 8 * s, (uint32_t)((kb / kStages) & 1));
             if (!__all_sync(0xffffffffu, ok)) {
                 ok = false;
                 break;
             }
+            const uint4* sa = reinterpret_cast<const uint4*>(smem + s * kStageBytes + kStageA + kStageB);
+            const uint4* sb = sa + kRows;
             uint32_t va[16], vb[16];
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
-                const int r = row0 + g * 32 + lane, t = tok0 + g * 32 + lane;
-                const uint4 a = r < p.oc ? *reinterpret_cast<const uint4*>(p.wsc + r * ldsc + kb * 16)
-                                         : make_uint4(0u, 0u, 0u, 0u);
-                const uint4 b = t < p.M ? *reinterpret_cast<const uint4*>(p.xsc + t * ldsc + kb * 16)
-                                        : make_uint4(0u, 0u, 0u, 0u);
+                const uint4 a = sa[g * 32 + lane], b = sb[g * 32 + lane];   // rows / tokens past the end read 0
                 // word kk of a row's 16 scale bytes: its 4 scales of MMA kk
                 va[0 * 4 + g] = a.x, va[1 * 4 + g] = a.y, va[2 * 4 + g] = a.z, va[3 * 4 + g] = a.w;
                 vb[0 * 4 + g] = b.x, vb[1 * 4 + g] = b.y, vb[2 * 4 + g] = b.z, vb[3 * 4 + g] = b.w;
@@ -285,18 +288,23 @@ int spark_nvfp4_native_linear(const uint8_t* wq, const uint8_t* w_scales, const 
                   SPARK_ERR_ALIGNMENT, "spark_nvfp4_native_linear: 16-byte aligned codes and scales");
     int rc = tc::get_encoder();
     if (rc) return rc;
-    CUtensorMap wmap, xmap;
+    CUtensorMap wmap, xmap, wsmap, xsmap;
     rc = tc::encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)(ic / 2), (uint64_t)oc, (uint64_t)(ic / 2),
                        128, kRows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     rc = tc::encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)(ic / 2), (uint64_t)M, (uint64_t)(ic / 2),
                        128, kTok, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
+    // scales: [rows][ic / 16] bytes, e4m3 (non-negative, read as ue4m3)
+    rc = tc::encode_2d(&wsmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_scales, (uint64_t)(ic / 16), (uint64_t)oc,
+                       (uint64_t)(ic / 16), 16, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = tc::encode_2d(&xsmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, x_scales, (uint64_t)(ic / 16), (uint64_t)M,
+                       (uint64_t)(ic / 16), 16, kTok, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
     cudaError_t e = cudaFuncSetAttribute(k_nvfp4_native, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return set_error((int)e, "spark_nvfp4_native_linear: %s", cudaGetErrorString(e));
     Params p;
-    p.wsc = w_scales;
-    p.xsc = x_scales;
     p.y = y;
     p.ldy = ldy;
     p.M = (int)M;
@@ -305,7 +313,7 @@ int spark_nvfp4_native_linear(const uint8_t* wq, const uint8_t* w_scales, const 
     p.y_dtype = y_dtype;
     p.err = err;
     const dim3 grid((unsigned)(oc / kRows), (unsigned)((M + kTok - 1) / kTok));
-    k_nvfp4_native<<<grid, kThreads, kSmem, reinterpret_cast<cudaStream_t>(stream)>>>(wmap, xmap, p);
+    k_nvfp4_native<<<grid, kThreads, kSmem, reinterpret_cast<cudaStream_t>(stream)>>>(wmap, xmap, wsmap, xsmap, p);
     return check_launch("spark_nvfp4_native_linear");
 }
 
