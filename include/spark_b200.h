@@ -142,6 +142,15 @@ SPARK_API int spark_twofour_pack(const void* w, int w_dtype, int64_t oc, int64_t
 SPARK_API int spark_twofour_unpack(const uint8_t* packed, int64_t n_elements, void* out, int out_dtype, void* stream);
 /* two_four_fake_quant -- 01_core/two_four.py:70 (TwoFourSTE backward is the identity, :65-67). */
 SPARK_API int spark_twofour_fake_quant(const void* w, int w_dtype, int64_t n, void* out, int out_dtype, void* stream);
+/* 2:4-sparse SPFP2 linear on the sparse tensor cores: y[M, oc] = x . decode(W)^T (+ bias), the
+ * forward of spark_v3_twofour_forward (01_core/spark_v3_twofour.cu:124-181), W in the reference's
+ * 2:4 layout (two_four_pack of [oc, ic]).  Each group of four columns holds at most two nonzeros:
+ * they are kept (bf16, exact) with their positions as metadata for tcgen05.mma.sp kind::f16, so the
+ * MMA skips the zero half.  x bf16 [M, ic] contiguous, 16-byte aligned; oc a multiple of 128, ic
+ * of 128; y [M, ldy] of y_dtype.  An expired bounded wait stores error code 6 in *err. */
+SPARK_API int spark_twofour_sparse_linear(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int64_t ic,
+                                          const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy,
+                                          int* err, void* stream);
 
 /* ---------------------------------------------------------------- INT8 (lm_head tier) */
 /* int8_fake_quant -- 01_core/int8_emu.py:12 (INT8STE backward is the identity, :26-27):

@@ -100,6 +100,7 @@ _SIGNATURES = {
     "spark_silu_mul_rows": (_i, [_p, _p, _i64, _p, _i64, _i, _i64, _i64, _p]),
     "spark_nvfp4_embedding": (_i, [_p, _p, _i64, _i64, _p, _i64, _p, _i, _p, _p]),
     "spark_nvfp4_native_linear": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _i64, _p, _p]),
+    "spark_twofour_sparse_linear": (_i, [_p, _p, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _p, _p]),
     "spark_peer_flags_count": (_i, [_i]),
     "spark_peer_allreduce": (_i, [_p, _p, _i, _i, _i64, _i, _p, _i, _p, _p, _p]),
     "spark_ipc_handle": (_i, [_p, _p, ctypes.POINTER(ctypes.c_int64)]),

@@ -31,6 +31,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace spark {
 namespace tc {
@@ -40,6 +41,7 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
 }  // namespace tc
 
 namespace nvn {
+using namespace tcx;
 
 constexpr int kRows = 128;          // weight rows per CTA (MMA M)
 constexpr int kTok = 128;           // tokens per CTA (MMA N)
@@ -55,51 +57,7 @@ constexpr int kThreads = 192;
 constexpr int kTmaWarp = 4, kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 256;                          // D: 128 columns; scales: 32 per stage
 constexpr uint32_t kSfCol = 128;
-constexpr uint64_t kWaitNs = 2000000000ull;
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    if (mbar_try(bar, parity)) return true;
-    const uint64_t deadline = globaltimer_ns() + kWaitNs;
-    while (!mbar_try(bar, parity))
-        if (globaltimer_ns() > deadline) return false;
-    return true;
-}
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            dst),
-        "l"(map), "r"(c0), "r"(c1), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major operand in shared memory, 128-byte swizzle, 8-row groups 1024 bytes
-// apart (the leading byte offset is unused for this layout).
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3fffu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
-           ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
-}
 // Block-scaled instruction descriptor: A and B e2m1 (bits 7-9, 10-12 = 1),
 // K-major, N = kTok (bits 17-22: N >> 3), ue4m3 scales (bit 23 = 0),
 // M = 128 (bits 24-28: M >> 4), scale byte ids 0, K = 64.
@@ -112,33 +70,6 @@ __device__ __forceinline__ void mma_fp4(uint32_t d, uint64_t a, uint64_t b, uint
         "l"(a), "l"(b), "r"(kIdesc), "r"(acc), "r"(sfa), "r"(sfb)
         : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
-}
-// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16};" ::"r"(taddr),
-        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-        : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 struct Params {
     void* y;
     int64_t ldy;

@@ -173,6 +173,23 @@ def nvfp4_native_linear(codes: torch.Tensor, scales: torch.Tensor, x: torch.Tens
     return y
 
 
+def twofour_sparse_linear(packed: torch.Tensor, x: torch.Tensor, oc: int, ic: int, bias=None,
+                          out_dtype=torch.bfloat16) -> torch.Tensor:
+    """2:4 linear on the sparse tensor cores (spark_twofour_sparse_linear):
+    the kept values of every group of four with their positions as the MMA's
+    sparsity metadata.  x: bf16 [M, ic]; packed: twofour_pack of [oc, ic]."""
+    x2 = _cuda(x).contiguous()
+    if x2.dtype != torch.bfloat16:
+        raise TypeError("twofour_sparse_linear: bf16 activations")
+    M = x2.shape[0]
+    y = torch.empty(M, oc, dtype=out_dtype, device=x2.device)
+    ws = workspace(x2.device, 1 << 20)
+    b = _cuda(bias) if bias is not None else None
+    call("spark_twofour_sparse_linear", _p(_bytes(packed)), _p(x2), M, oc, ic, _p(b), _dt(b) if b is not None else 0,
+         _p(y), _dt(y), oc, _p(ws), _stream(x2))
+    return y
+
+
 def nvfp4_fake_quant(w: torch.Tensor, out_dtype=None) -> torch.Tensor:
     x = _cuda(w.detach())
     oc, ic = x.shape
