@@ -12,9 +12,12 @@
 // decode is skipped.
 //
 // Tile: 128 weight rows x 128 tokens per CTA; K in blocks of 128 columns.
-// Roles (192 threads):
-//   warps 0-3  decoders, then the epilogue.  Thread r (of 128) decodes weight
-//              row r of the block: the 64 kept values of its 32 groups go to
+// Roles (32 * (4 * kGroups + 2) threads):
+//   warps 0 .. 4*kGroups-1  decoders, then the epilogue.  kGroups groups of
+//              four warps decode alternate K blocks (group g the blocks
+//              kb = g mod kGroups), warp w for the 32 weight rows of lane
+//              quadrant w % 4; its thread r decodes row r of the block: the
+//              64 kept values of its 32 groups go to
 //              the block's A stage in shared memory (one 128-byte-swizzled,
 //              K-major row, the MMA's compressed operand), the group indices
 //              to the block's metadata columns in TMEM: per MMA (32 columns)
@@ -22,8 +25,8 @@
 //              k%16 + 16*((m/8)%2) of row m (each group's nibble: first index
 //              in bits 0-1, second in bits 2-3, first < second).  Rows reach
 //              their lanes by two warp shuffles per MMA.
-//   warp 4     lane 0 issues the TMA loads of the activation tiles.
-//   warp 5     allocates TMEM; lane 0 issues 4 sparse MMAs per block and
+//   next warp  lane 0 issues the TMA loads of the activation tiles.
+//   last warp  allocates TMEM; lane 0 issues 4 sparse MMAs per block and
 //              commits each block back to its producers.
 // Every wait is bounded (2 s): an expired wait stores error code 6 in the
 // caller's error word, and every role still reaches the final barrier and
@@ -50,8 +53,13 @@ constexpr int kStageA = kRows * 128;                  // 64 kept bf16 values per
 constexpr int kStageB = kTok * kKB * 2;               // two 64-column swizzled boxes
 constexpr int kStageBytes = kStageA + kStageB;
 constexpr int kSmem = kStages * kStageBytes + 1024;
-constexpr int kThreads = 192;
-constexpr int kTmaWarp = 4, kMmaWarp = 5;
+// One decoder warp per lane quadrant handles a block alone, and its chain per
+// block (loads, table lookups, shared and TMEM stores, fences) is what bounds
+// the kernel, so groups of four warps take alternate blocks.
+constexpr int kGroups = 2;
+constexpr int kDecWarps = 4 * kGroups;
+constexpr int kThreads = 32 * (kDecWarps + 2);
+constexpr int kTmaWarp = kDecWarps, kMmaWarp = kDecWarps + 1;
 constexpr uint32_t kTmemCols = 256;                   // D: 128 columns; metadata: 4 per stage
 constexpr uint32_t kECol = 128;
 // bf16 x bf16 -> f32, K-major, N = kTok, M = 128, sparse (bit 2)
@@ -68,10 +76,8 @@ __device__ __forceinline__ void mma_sp(uint32_t d, uint64_t a, uint64_t b, uint3
         "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(e & ~1u)
         : "memory");
 }
-__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t* r) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
-                 "r"(r[2]), "r"(r[3])
-                 : "memory");
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, uint32_t a, uint32_t b) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(a), "r"(b) : "memory");
 }
 
 struct Params {
@@ -113,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < kStages; ++s) {
             mbar_init(bfull + 8 * s, 1);
             mbar_init(empty + 8 * s, 1);
-            mbar_init(afull + 8 * s, 4);
+            mbar_init(afull + 8 * s, 4);   // the four warps of the block's group
         }
         mbar_init(done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -160,12 +166,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(done);
         }
     } else {
-        const int q = warp, r = q * 32 + lane;              // this thread's weight row in the tile
+        const int q = warp & 3, grp = warp >> 2, r = q * 32 + lane;   // weight row in the tile, decoder group
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        const uint8_t* wrow = p.wq + (int64_t)(row0 + r) * p.row_bytes;
+        const uint32_t* wrow = reinterpret_cast<const uint32_t*>(p.wq + (int64_t)(row0 + r) * p.row_bytes);
         // the two rows whose metadata halves this lane's TMEM word holds
         const int lm1 = 16 * (lane >> 4) + (lane & 7), hsel = (lane >> 3) & 1;
-        for (int kb = 0; kb < p.n_kb && ok; ++kb) {
+        // the row's 28 bytes of this group's next block, loaded one block ahead
+        uint32_t wn[7] = {0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        if (grp < p.n_kb) {
+#pragma unroll
+            for (int i = 0; i < 7; ++i) wn[i] = wrow[7 * grp + i];
+        }
+        for (int kb = grp; kb < p.n_kb && ok; kb += kGroups) {
             const int s = kb % kStages;
             if (kb >= kStages) ok = mbar_wait(empty + 8 * s, (uint32_t)((kb / kStages - 1) & 1));
             if (!__all_sync(0xffffffffu, ok)) {
@@ -174,10 +186,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // 128 columns = 8 fields = 28 bytes of the row
             uint32_t w[8];
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(wrow + kb * 28);
 #pragma unroll
-            for (int i = 0; i < 7; ++i) w[i] = src[i];
+            for (int i = 0; i < 7; ++i) w[i] = wn[i];
             w[7] = 0u;
+            if (kb + kGroups < p.n_kb) {
+#pragma unroll
+                for (int i = 0; i < 7; ++i) wn[i] = wrow[7 * (kb + kGroups) + i];
+            }
             uint32_t kept[32], meta[4];
 #pragma unroll
             for (int pp = 0; pp < 4; ++pp) {
@@ -214,20 +229,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t b = __shfl_sync(0xffffffffu, meta[kk], lm1 + 8);
                 ev[kk] = (hsel ? (a >> 16) : (a & 0xffffu)) | ((hsel ? (b >> 16) : (b & 0xffffu)) << 16);
             }
-            tmem_st4(tbase + lane_off + kECol + (uint32_t)(s * 4), ev);
+            tmem_st2(tbase + lane_off + kECol + (uint32_t)(s * 4), ev[0], ev[1]);
+            tmem_st2(tbase + lane_off + kECol + (uint32_t)(s * 4 + 2), ev[2], ev[3]);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the A stage, for the tensor core
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(afull + 8 * s);
         }
-        // epilogue: this quadrant's 32 weight rows, every token of the tile
+        // epilogue: this quadrant's 32 weight rows, the groups taking 16-column chunks in turn
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(done, 0));
         if (ok) {
             tc_fence_after();
             const int64_t row = row0 + r;
             const float b = p.bias ? load_as_float(p.bias, p.bias_dtype, row) : 0.0f;
-            for (int c0 = 0; c0 < kTok; c0 += 16) {
+            for (int c0 = 16 * grp; c0 < kTok; c0 += 16 * kGroups) {
                 float v[16];
                 tmem_ld16(tbase + lane_off + (uint32_t)c0, v);
 #pragma unroll
