@@ -56,7 +56,7 @@ constexpr int kSmem = kStages * kStageBytes + 1024;
 // One decoder warp per lane quadrant handles a block alone, and its chain per
 // block (loads, table lookups, shared and TMEM stores, fences) is what bounds
 // the kernel, so groups of four warps take alternate blocks.
-constexpr int kGroups = 2;
+constexpr int kGroups = 3;
 constexpr int kDecWarps = 4 * kGroups;
 constexpr int kThreads = 32 * (kDecWarps + 2);
 constexpr int kTmaWarp = kDecWarps, kMmaWarp = kDecWarps + 1;
