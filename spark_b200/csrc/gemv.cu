@@ -1455,6 +1455,13 @@ int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, con
                       "spark_linear: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
         SPARK_REQUIRE(aligned(workspace, 256), SPARK_ERR_ALIGNMENT, "spark_linear: workspace must be 256-byte aligned");
         uint8_t* ws = static_cast<uint8_t*>(workspace);
+        // 2:4 at 128 to 1024 tokens: the sparse tensor-core kernel, which keeps
+        // the two nonzeros of every group and skips the zero half of the MMA
+        // (measured 25-28% faster there than decoding to dense; equal at 2048)
+        if (fmt == SPARK_FMT_TWOFOUR && !tcgen05 && M >= 128 && M <= 1024 && oc % 128 == 0 && ic % 128 == 0 &&
+            ldx == ic && aligned(wq, 4))
+            return spark_twofour_sparse_linear(wq, x, M, oc, ic, bias, bias_dtype, y, y_dtype, ldy,
+                                               reinterpret_cast<int*>(ws + L.err), stream);
         return tc_linear(fmt, wq, scales, x, M, oc, ic, ldx, bias, bias_dtype, y, y_dtype, ldy,
                                reinterpret_cast<int*>(ws + L.err), reinterpret_cast<int*>(ws + L.counters),
                                kMaxRowGroups, reinterpret_cast<float*>(ws + L.partials), s);
