@@ -496,6 +496,33 @@ def run_gpu(args, rank, world, local):
     ops.check_device_errors()
     del y_n
 
+    # ---------------- 2:4 down_proj [2560, 9728] (seeded N(0, 0.02) weights) on the
+    # sparse tensor cores (spark_linear's route at 128-1024 tokens, and the kernel
+    # called directly at PREFILL_M) against the dense decode (tcgen05 kind::f16)
+    g24 = torch.Generator(device=device).manual_seed(24)
+    oc24, ic24 = 2560, 9728
+    w24 = ops.twofour_pack(torch.randn(oc24, ic24, device=device, generator=g24) * 0.02)
+    tf24 = {}
+    for name, m24, fn in (
+            ("sparse_m512", 512, lambda x: ops.linear("twofour", w24, None, x, oc24, ic24)),
+            ("dense_m512", 512, lambda x: ops.linear("twofour", w24, None, x, oc24, ic24, tcgen05=True)),
+            ("sparse_m2048", PREFILL_M, lambda x: ops.twofour_sparse_linear(w24, x, oc24, ic24)),
+            ("dense_m2048", PREFILL_M, lambda x: ops.linear("twofour", w24, None, x, oc24, ic24))):
+        x24 = torch.randn(m24, ic24, device=device, generator=g24).bfloat16()
+        with torch.cuda.stream(stream):
+            fn(x24)
+            fn(x24)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for _ in range(4):
+                fn(x24)
+        ms24 = timed(gr, pre_steps) / (4 * pre_steps)
+        tf24[name] = {"ms": round(ms24, 4), "TFLOP/s dense-equivalent": round(2.0 * m24 * oc24 * ic24 / (ms24 * 1e-3) / 1e12, 1)}
+        del gr, x24
+    ops.check_device_errors()
+    del w24
+
     # ---------------- BASELINE config 4, tensor-parallel over the ranks of this run
     tp = tp_mlp_measure(args, rank, world, local)
     try:
@@ -572,6 +599,12 @@ def run_gpu(args, rank, world, local):
                              "peak_source": "nominal dense FP4 (no measured FP4 peak on this pool)"},
                 "rel_frobenius_vs_parity_path": round(nat_rel, 5),
                 "note": "a reported mode, not the parity path: the error is the activations' FP4 rounding",
+            },
+            "twofour": {
+                "workload": "2:4 down_proj [2560, 9728], bf16 x: tcgen05.mma.sp kind::f16 on the kept values "
+                            "(spark_twofour_sparse_linear; spark_linear's route at 128-1024 tokens) vs the dense "
+                            "decode on tcgen05.mma kind::f16",
+                **tf24,
             },
         },
     }
