@@ -34,6 +34,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "tc_common.cuh"
 
@@ -86,6 +88,9 @@ struct Params {
     void* y;
     int64_t ldy, row_bytes;
     int M, oc, n_kb, bias_dtype, y_dtype;
+    int split;              // K ranges (blockIdx.z); above 1: fp32 partials and a last-CTA sum
+    float* part;            // [split][oc][M] partial sums (split > 1)
+    int* cnt;               // per output tile: CTAs done, back to zero after the sum (split > 1)
     int* err;
 };
 
@@ -112,6 +117,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ uint16_t s_tab[64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * kRows, tok0 = blockIdx.y * kTok;
+    // this CTA's K blocks [kb0, kb0 + nk); blocks below are numbered from kb0
+    const int kb0 = (int)((int64_t)blockIdx.z * p.n_kb / p.split);
+    const int nk = (int)((int64_t)(blockIdx.z + 1) * p.n_kb / p.split) - kb0;
+    __shared__ int s_last;
     const uint32_t bfull = smem_u32(&bars[0]), empty = smem_u32(&bars[kStages]), afull = smem_u32(&bars[2 * kStages]);
     const uint32_t done = smem_u32(&bars[3 * kStages]);
     if (threadIdx.x < 64) s_tab[threadIdx.x] = (uint16_t)group_entry(threadIdx.x);
@@ -138,19 +147,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kTmaWarp) {
         if (lane == 0) {
-            for (int kb = 0; kb < p.n_kb && ok; ++kb) {
+            for (int kb = 0; kb < nk && ok; ++kb) {
                 const int s = kb % kStages;
                 if (kb >= kStages) ok = mbar_wait(empty + 8 * s, (uint32_t)((kb / kStages - 1) & 1));
                 if (!ok) break;
                 const uint32_t st = smem_u32(smem + s * kStageBytes + kStageA);
                 mbar_expect_tx(bfull + 8 * s, kStageB);
-                tma_load_2d(st, &xmap, kb * kKB, tok0, bfull + 8 * s);
-                tma_load_2d(st + kStageB / 2, &xmap, kb * kKB + 64, tok0, bfull + 8 * s);
+                tma_load_2d(st, &xmap, (kb0 + kb) * kKB, tok0, bfull + 8 * s);
+                tma_load_2d(st + kStageB / 2, &xmap, (kb0 + kb) * kKB + 64, tok0, bfull + 8 * s);
             }
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
-            for (int kb = 0; kb < p.n_kb && ok; ++kb) {
+            for (int kb = 0; kb < nk && ok; ++kb) {
                 const int s = kb % kStages;
                 const uint32_t par = (uint32_t)((kb / kStages) & 1);
                 ok = mbar_wait(bfull + 8 * s, par) && mbar_wait(afull + 8 * s, par);
@@ -173,11 +182,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int lm1 = 16 * (lane >> 4) + (lane & 7), hsel = (lane >> 3) & 1;
         // the row's 28 bytes of this group's next block, loaded one block ahead
         uint32_t wn[7] = {0u, 0u, 0u, 0u, 0u, 0u, 0u};
-        if (grp < p.n_kb) {
+        if (grp < nk) {
 #pragma unroll
-            for (int i = 0; i < 7; ++i) wn[i] = wrow[7 * grp + i];
+            for (int i = 0; i < 7; ++i) wn[i] = wrow[7 * (kb0 + grp) + i];
         }
-        for (int kb = grp; kb < p.n_kb && ok; kb += kGroups) {
+        for (int kb = grp; kb < nk && ok; kb += kGroups) {
             const int s = kb % kStages;
             if (kb >= kStages) ok = mbar_wait(empty + 8 * s, (uint32_t)((kb / kStages - 1) & 1));
             if (!__all_sync(0xffffffffu, ok)) {
@@ -189,9 +198,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 7; ++i) w[i] = wn[i];
             w[7] = 0u;
-            if (kb + kGroups < p.n_kb) {
+            if (kb + kGroups < nk) {
 #pragma unroll
-                for (int i = 0; i < 7; ++i) wn[i] = wrow[7 * (kb + kGroups) + i];
+                for (int i = 0; i < 7; ++i) wn[i] = wrow[7 * (kb0 + kb + kGroups) + i];
             }
             uint32_t kept[32], meta[4];
 #pragma unroll
@@ -239,18 +248,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // epilogue: this quadrant's 32 weight rows, the groups taking 16-column chunks in turn
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(done, 0));
-        if (ok) {
-            tc_fence_after();
-            const int64_t row = row0 + r;
-            const float b = p.bias ? load_as_float(p.bias, p.bias_dtype, row) : 0.0f;
-            for (int c0 = 16 * grp; c0 < kTok; c0 += 16 * kGroups) {
-                float v[16];
-                tmem_ld16(tbase + lane_off + (uint32_t)c0, v);
+        const int64_t row = row0 + r;
+        const float b = p.bias ? load_as_float(p.bias, p.bias_dtype, row) : 0.0f;
+        if (p.split == 1) {
+            if (ok) {
+                tc_fence_after();
+                for (int c0 = 16 * grp; c0 < kTok; c0 += 16 * kGroups) {
+                    float v[16];
+                    tmem_ld16(tbase + lane_off + (uint32_t)c0, v);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int t = tok0 + c0 + i;
-                    if (t < p.M) store_from_float(p.y, p.y_dtype, (int64_t)t * p.ldy + row, v[i] + b);
+                    for (int i = 0; i < 16; ++i) {
+                        const int t = tok0 + c0 + i;
+                        if (t < p.M) store_from_float(p.y, p.y_dtype, (int64_t)t * p.ldy + row, v[i] + b);
+                    }
                 }
+            }
+        } else {
+            // K split: store this range's fp32 sums; the CTA that completes the
+            // tile's count adds the ranges in order 0..split-1 (the result does
+            // not depend on which CTA finishes last) and writes y.  Every decoder
+            // thread passes both barriers, also after an error.
+            float* mine = p.part + (int64_t)blockIdx.z * p.oc * p.M;
+            if (ok) {
+                tc_fence_after();
+                for (int c0 = 16 * grp; c0 < kTok && tok0 + c0 < p.M; c0 += 16 * kGroups) {
+                    float v[16];
+                    tmem_ld16(tbase + lane_off + (uint32_t)c0, v);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int t = tok0 + c0 + i;
+                        if (t < p.M) __stcg(mine + row * p.M + t, v[i]);
+                    }
+                }
+            }
+            __threadfence();
+            asm volatile("bar.sync 1, %0;" ::"r"(kDecWarps * 32) : "memory");
+            int* cnt = p.cnt + blockIdx.y * gridDim.x + blockIdx.x;
+            if (threadIdx.x == 0) s_last = atomicAdd(cnt, 1) == p.split - 1;
+            asm volatile("bar.sync 1, %0;" ::"r"(kDecWarps * 32) : "memory");
+            if (s_last) {
+                __threadfence();
+                for (int c = grp; c < kTok && tok0 + c < p.M; c += kGroups) {
+                    const int t = tok0 + c;
+                    float sum = 0.0f;
+                    for (int z = 0; z < p.split; ++z) sum += __ldcg(p.part + ((int64_t)z * p.oc + row) * p.M + t);
+                    store_from_float(p.y, p.y_dtype, (int64_t)t * p.ldy + row, sum + b);
+                }
+                if (threadIdx.x == 0) *cnt = 0;
             }
         }
     }
@@ -264,13 +308,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 }  // namespace tfs
-}  // namespace spark
 
-extern "C" {
-
-int spark_twofour_sparse_linear(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int64_t ic, const void* bias,
-                                int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err, void* stream) {
-    using namespace spark;
+// counters (int[], zero, left zero) and part (part_bytes) : scratch for the
+// K split of small token counts; null counters: no split.
+int twofour_sparse_run(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int64_t ic, const void* bias,
+                       int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err, int* counters, float* part,
+                       size_t part_bytes, cudaStream_t stream) {
     using namespace spark::tfs;
     SPARK_REQUIRE(wq && x && y && err, SPARK_ERR_INVALID, "spark_twofour_sparse_linear: null pointer");
     SPARK_REQUIRE(M >= 1 && M < (1ll << 31) && oc >= kRows && oc % kRows == 0 && oc < (1ll << 31) && ic >= kKB &&
@@ -302,9 +345,37 @@ int spark_twofour_sparse_linear(const uint8_t* wq, const void* x, int64_t M, int
     p.bias_dtype = bias_dtype;
     p.y_dtype = y_dtype;
     p.err = err;
-    const dim3 grid((unsigned)(oc / kRows), (unsigned)((M + kTok - 1) / kTok));
-    k_twofour_sparse<<<grid, kThreads, kSmem, reinterpret_cast<cudaStream_t>(stream)>>>(xmap, p);
+    p.split = 1;
+    p.part = nullptr;
+    p.cnt = nullptr;
+    // few output tiles (decode sizes): split K so that about one CTA per SM
+    // runs; the ranges' fp32 sums go to the caller's scratch
+    const int64_t tiles = (oc / kRows) * ((M + kTok - 1) / kTok);
+    if (counters && part && tiles < 74) {
+        int sm = 0, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
+        int64_t split = std::min<int64_t>({(int64_t)sm / tiles, (int64_t)p.n_kb, (int64_t)16});
+        while (split > 1 && (size_t)split * oc * M * sizeof(float) > part_bytes) --split;
+        if (split > 1) {
+            p.split = (int)split;
+            p.cnt = counters;
+            p.part = part;
+        }
+    }
+    const dim3 grid((unsigned)(oc / kRows), (unsigned)((M + kTok - 1) / kTok), (unsigned)p.split);
+    k_twofour_sparse<<<grid, kThreads, kSmem, stream>>>(xmap, p);
     return check_launch("spark_twofour_sparse_linear");
+}
+
+}  // namespace spark
+
+extern "C" {
+
+int spark_twofour_sparse_linear(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int64_t ic, const void* bias,
+                                int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err, void* stream) {
+    return spark::twofour_sparse_run(wq, x, M, oc, ic, bias, bias_dtype, y, y_dtype, ldy, err, nullptr, nullptr, 0,
+                                     reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
