@@ -504,6 +504,8 @@ def run_gpu(args, rank, world, local):
     w24 = ops.twofour_pack(torch.randn(oc24, ic24, device=device, generator=g24) * 0.02)
     tf24 = {}
     for name, m24, fn in (
+            ("sparse_m1", 1, lambda x: ops.linear("twofour", w24, None, x, oc24, ic24)),
+            ("dense_m1", 1, lambda x: ops.linear("twofour", w24, None, x, oc24, ic24, tcgen05=True)),
             ("sparse_m512", 512, lambda x: ops.linear("twofour", w24, None, x, oc24, ic24)),
             ("dense_m512", 512, lambda x: ops.linear("twofour", w24, None, x, oc24, ic24, tcgen05=True)),
             ("sparse_m2048", PREFILL_M, lambda x: ops.twofour_sparse_linear(w24, x, oc24, ic24)),
@@ -602,8 +604,8 @@ def run_gpu(args, rank, world, local):
             },
             "twofour": {
                 "workload": "2:4 down_proj [2560, 9728], bf16 x: tcgen05.mma.sp kind::f16 on the kept values "
-                            "(spark_twofour_sparse_linear; spark_linear's route at 128-1024 tokens) vs the dense "
-                            "decode on tcgen05.mma kind::f16",
+                            "(spark_twofour_sparse_linear; spark_linear's route at up to 8 tokens, K split, and at "
+                            "128-1024 tokens) vs the dense decode on tcgen05.mma kind::f16",
                 **tf24,
             },
         },
