@@ -84,3 +84,23 @@ def test_batch_allreduce_argument_validation():
     assert L.spark_batch_ar_recv_bytes(2, 16, 2560) == 2 * 2 * 160 * 16 * 16 * 8
     assert L.spark_batch_ar_recv_bytes(0, 16, 2560) == 0 and L.spark_batch_ar_recv_bytes(9, 1, 16) == 0
     assert L.spark_batch_ar_recv_bytes(2, 17, 16) == 0
+
+
+def test_tensor_core_modes_validate_arguments_on_the_host():
+    """The sparse 2:4 and the native NVFP4 entry points reject bad shapes and
+    null pointers before they touch the device."""
+    L = _lib.lib()
+    P = ctypes.c_void_p
+    p = P(256)
+    err = P(256)
+    # 2:4 sparse: oc must be a multiple of 128, ic of 128
+    assert L.spark_twofour_sparse_linear(p, p, 4, 100, 256, None, 0, p, 1, 100, err, None) == _lib.ERR_INVALID
+    assert L.spark_twofour_sparse_linear(p, p, 4, 128, 96, None, 0, p, 1, 128, err, None) == _lib.ERR_INVALID
+    assert L.spark_twofour_sparse_linear(None, p, 4, 128, 128, None, 0, p, 1, 128, err, None) == _lib.ERR_INVALID
+    assert "multiple of 128" in _lib.last_error() or "null" in _lib.last_error()
+    assert L.spark_twofour_sparse_linear(p, P(258), 4, 128, 128, None, 0, p, 1, 128, err, None) == _lib.ERR_ALIGNMENT
+    # native NVFP4: oc a multiple of 128, ic of 256
+    assert L.spark_nvfp4_native_linear(p, p, p, p, 4, 100, 256, p, 1, 100, err, None) == _lib.ERR_INVALID
+    assert L.spark_nvfp4_native_linear(p, p, p, p, 4, 128, 128, p, 1, 128, err, None) == _lib.ERR_INVALID
+    assert L.spark_nvfp4_native_linear(p, p, None, p, 4, 128, 256, p, 1, 128, err, None) == _lib.ERR_INVALID
+    assert L.spark_nvfp4_native_linear(P(264), p, p, p, 4, 128, 256, p, 1, 128, err, None) == _lib.ERR_ALIGNMENT
