@@ -1385,6 +1385,7 @@ int stream_plan_set_ar(StreamPlan* P, const SparkBatchAllReduce* ar);
 int twofour_sparse_run(const uint8_t* wq, const void* x, int64_t M, int64_t oc, int64_t ic, const void* bias,
                        int bias_dtype, void* y, int y_dtype, int64_t ldy, int* err, int* counters, float* part,
                        size_t part_bytes, cudaStream_t stream);
+constexpr int64_t kSplitMaxTok = 16;    // 2:4 token counts whose sparse launch splits K
 size_t stream_scratch_single(int64_t M, int64_t ic);
 size_t tc_partials_bytes(int dev, int64_t M);
 bool tc_linear_ok(int fmt, const void* wq, const void* scales, const void* x, int x_dtype, int64_t ic,
@@ -1458,13 +1459,13 @@ int spark_linear_prefetch(int fmt, const uint8_t* wq, const uint8_t* scales, con
                       "spark_linear: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
         SPARK_REQUIRE(aligned(workspace, 256), SPARK_ERR_ALIGNMENT, "spark_linear: workspace must be 256-byte aligned");
         uint8_t* ws = static_cast<uint8_t*>(workspace);
-        // 2:4 at up to 8 tokens and at 128 to 1024: the sparse tensor-core
+        // 2:4 at up to 16 tokens and at 128 to 1024: the sparse tensor-core
         // kernel, which keeps the two nonzeros of every group and skips the
-        // zero half of the MMA.  Up to 8 tokens it splits K over the SMs (the
+        // zero half of the MMA.  Up to 16 tokens it splits K over the SMs (the
         // partial sums in the workspace's partial area): down_proj 2560x9728
         // 21 -> 15 us at one token; at 128-1024 tokens 71-73 -> 53-55 us.  In
-        // between (16-64 tokens) the dense decode measured equal or faster.
-        const bool sparse_small = M <= 8, sparse_mid = M >= 128 && M <= 1024;
+        // between (32-64 tokens) the dense decode measured faster.
+        const bool sparse_small = M <= kSplitMaxTok, sparse_mid = M >= 128 && M <= 1024;
         if (fmt == SPARK_FMT_TWOFOUR && !tcgen05 && (sparse_small || sparse_mid) && oc % 128 == 0 &&
             ic % 128 == 0 && ldx == ic && aligned(wq, 4))
             return twofour_sparse_run(wq, x, M, oc, ic, bias, bias_dtype, y, y_dtype, ldy,

@@ -89,7 +89,7 @@ struct Params {
     int64_t ldy, row_bytes;
     int M, oc, n_kb, bias_dtype, y_dtype;
     int split;              // K ranges (blockIdx.z); above 1: fp32 partials and a last-CTA sum
-    float* part;            // [split][oc][M] partial sums (split > 1)
+    float* part;            // [split][M][oc] partial sums (split > 1): a warp's 32 rows are contiguous
     int* cnt;               // per output tile: CTAs done, back to zero after the sum (split > 1)
     int* err;
 };
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int t = tok0 + c0 + i;
-                        if (t < p.M) __stcg(mine + row * p.M + t, v[i]);
+                        if (t < p.M) __stcg(mine + (int64_t)t * p.oc + row, v[i]);
                     }
                 }
             }
@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = grp; c < kTok && tok0 + c < p.M; c += kGroups) {
                     const int t = tok0 + c;
                     float sum = 0.0f;
-                    for (int z = 0; z < p.split; ++z) sum += __ldcg(p.part + ((int64_t)z * p.oc + row) * p.M + t);
+                    for (int z = 0; z < p.split; ++z) sum += __ldcg(p.part + ((int64_t)z * p.M + t) * p.oc + row);
                     store_from_float(p.y, p.y_dtype, (int64_t)t * p.ldy + row, sum + b);
                 }
                 if (threadIdx.x == 0) *cnt = 0;
