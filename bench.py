@@ -604,7 +604,7 @@ def run_gpu(args, rank, world, local):
             },
             "twofour": {
                 "workload": "2:4 down_proj [2560, 9728], bf16 x: tcgen05.mma.sp kind::f16 on the kept values "
-                            "(spark_twofour_sparse_linear; spark_linear's route at up to 8 tokens, K split, and at "
+                            "(spark_twofour_sparse_linear; spark_linear's route at up to 16 tokens, K split, and at "
                             "128-1024 tokens) vs the dense decode on tcgen05.mma kind::f16",
                 **tf24,
             },
